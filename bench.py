@@ -1,0 +1,280 @@
+"""Benchmark of the B200 FFT engine on BASELINE config 2 (C2C f32, N=4096 x batch 65536,
+forward then normalised inverse).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one forward + one inverse C2C pass over the whole batch.  `value` is the
+aggregate GFLOP/s (5 N log2 N per complex transform, two transforms per element per
+step) with the data resident in HBM; `e2e` is the same metric through the host API
+(execute_transform with pinned host arrays: each step uploads its input and downloads
+its result).  Under torchrun every rank processes its own 65536-transform shard (weak
+scaling, no collective on the data path); times are CUDA-event durations on the
+launching stream, max over ranks.  `--impl reference` times the CPU oracle (the
+reference's CPU path restated in C, oracle/) on this host's cores instead.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "vkfft-rs_b200"))
+
+N = 4096
+BATCH = 65536
+FLOP_PER_TRANSFORM = 5.0 * N * math.log2(N)
+METRIC = "batched C2C FFT GFLOP/s (5N*log2N), N=4096 f32, forward+inverse"
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        return d.get("c2c_4096_f32_bytes_per_launch")
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (the pool's clocks line)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def cpu_baseline(steps_hint=1, budget_s=12.0):
+    """The CPU oracle on a bounded sample of the same workload (all host cores)."""
+    import oracle
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1)
+    sample = max(threads * 2, 16)
+    x = (rng.uniform(-1, 1, (sample, N)) + 1j * rng.uniform(-1, 1, (sample, N))).astype(np.complex64)
+    xd = x.astype(np.complex128)
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        y = np.empty_like(xd)
+        oracle.lib().oracle_fft_batch(oracle._dp(xd), oracle._dp(y), N, sample, 0, 0, threads)
+        oracle.lib().oracle_fft_batch(oracle._dp(y), oracle._dp(xd), N, sample, 1, 1, threads)
+        done += sample
+        if time.perf_counter() - t0 >= budget_s / max(steps_hint, 1):
+            break
+    dt = time.perf_counter() - t0
+    gflops = 2 * FLOP_PER_TRANSFORM * done / dt / 1e9
+    return {"value": gflops, "unit": "GFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{done} forward+inverse pairs of N=4096 (f64 oracle) in {dt:.1f}s"}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    steps = []
+    for _ in range(args.warmup):
+        cpu_baseline(1, budget_s=1.0)
+    for _ in range(args.steps):
+        steps.append(cpu_baseline(1, budget_s=max(4.0, 30.0 / max(args.steps, 1))))
+    value = statistics.mean(s["value"] for s in steps)
+    cb = dict(steps[-1])
+    cb["value"] = value
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 2 * FLOP_PER_TRANSFORM * BATCH / value / 1e6,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "C2C N=4096 x batch 65536 (per rank), forward + normalised inverse",
+                   "global_batch": BATCH, "parallelism": "host cores"},
+        "cpu_baseline": cb,
+        "e2e": {"value": value, "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import vkfft_rs as V
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    ctx = V.CudaExecutionContext(local)
+    dev = ctx.device_profile()
+    cfg = V.FftConfig([N]).with_batch_count(BATCH).with_inverse_normalization(True)
+    fwd = V.TransformIr.build(cfg, V.Direction.FORWARD, dev)
+    inv = V.TransformIr.build(cfg, V.Direction.INVERSE, dev)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1 + rank)
+    a = (torch.rand((BATCH, N, 2), device="cuda", generator=gen) * 2 - 1).contiguous()
+    b = torch.empty_like(a)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        ctx.execute_resident(fwd, a.data_ptr(), b.data_ptr(), stream=sp)
+        ctx.execute_resident(inv, b.data_ptr(), a.data_ptr(), stream=sp)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # per-launch timing of the dominant kernel (forward pass) on the same stream
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for k in range(args.steps):
+            evs[k][0].record(stream)
+            ctx.execute_resident(fwd, a.data_ptr(), b.data_ptr(), stream=sp)
+            evs[k][1].record(stream)
+            ctx.execute_resident(inv, b.data_ptr(), a.data_ptr(), stream=sp)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    if dist:
+        t = torch.tensor([elapsed_ms, fwd_ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, fwd_ms = float(t[0]), float(t[1])
+    ms_per_step = elapsed_ms / args.steps
+    total_transforms = 2 * BATCH * ws
+    value = total_transforms * FLOP_PER_TRANSFORM / (ms_per_step * 1e-3) / 1e9
+
+    # e2e through the host API with pinned host arrays
+    host_in = torch.empty((BATCH, N, 2), dtype=torch.float32, pin_memory=True)
+    host_in.copy_(a.cpu())
+    x_host = host_in.numpy().view(np.complex64).reshape(BATCH * N)
+    e2e_steps = max(1, min(args.steps, 3))
+    ctx.execute_transform(fwd, x_host)  # warm the staging buffers
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        spec = ctx.execute_transform(fwd, x_host)
+        back = ctx.execute_transform(inv, spec)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t[0])
+    e2e_value = total_transforms * FLOP_PER_TRANSFORM / e2e_s / 1e9
+    bytes_one = BATCH * N * 8
+
+    peak, peak_kind = load_peaks()
+    alg_bytes = 2 * N * BATCH * 8  # one read + one write of the tensor per launch
+    achieved = alg_bytes / (fwd_ms * 1e-3) / 1e9
+    traffic = load_traffic()
+    line = {
+        "metric": METRIC, "value": value, "unit": "GFLOP/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (uniform [-1,1], torch generator seed 1+rank)",
+        "config": {"workload": "BASELINE config 2: C2C N=4096 x batch 65536 per rank, forward + normalised inverse",
+                   "global_batch": BATCH * ws, "seq_len": N, "parallelism": f"batch-sharded x{ws}",
+                   "l2": "inputs (2 GiB per rank) larger than L2; no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_source": peak_kind,
+                     "kernel": "fft_pass_kernel<float> (forward, one launch per transform direction)"},
+        "e2e": {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": 2 * bytes_one,
+                "d2h_bytes_per_step": 2 * bytes_one, "path": "execute_transform (host arrays, pinned)"},
+        "gpu_launches": args.steps * (fwd.launch_count + inv.launch_count),
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        line["cpu_baseline"] = cpu_baseline(1, budget_s=12.0) if ws == 1 else None
+        print(json.dumps(line))
+    del back
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

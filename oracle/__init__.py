@@ -1,0 +1,140 @@
+"""numpy front end of the CPU oracle -- TEST INFRASTRUCTURE ONLY.
+
+Wraps ``liboracle.so`` (a C restatement of vkfft-rs ``src/reference.rs``; see
+``reference_oracle.c`` for the line-by-line citations).  Imported by the test
+suite, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference
+arm, always as the checker or the timed CPU reference, never by the product.
+
+ND transforms apply the 1D oracle along every axis, fastest axis first, as the
+reference's separable ND path does (nd_ir.rs:671-673, :1303-1338).  R2C keeps
+the first n/2+1 bins of the complex FFT of (x, 0); C2R expands the Hermitian
+half spectrum and keeps the real part (real_ir.rs:1037-1053).
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+
+def build():
+    """Compile liboracle.so with the committed Makefile."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        l = ctypes.CDLL(_LIB_PATH)
+        dp = ctypes.POINTER(ctypes.c_double)
+        sz = ctypes.c_size_t
+        ci = ctypes.c_int
+        l.oracle_fft.argtypes = [dp, dp, sz, ci, ci]
+        l.oracle_dft.argtypes = [dp, dp, sz, ci, ci]
+        l.oracle_fft_axis.argtypes = [dp, dp, sz, sz, sz, ci, ci, ci]
+        l.oracle_fft_batch.argtypes = [dp, dp, sz, sz, ci, ci, ci]
+        l.oracle_r2c_batch.argtypes = [dp, dp, sz, sz, ci]
+        l.oracle_c2r_batch.argtypes = [dp, dp, sz, sz, ci, ci]
+        l.oracle_next_smooth_at_least.argtypes = [sz]
+        l.oracle_next_smooth_at_least.restype = sz
+        for f in (l.oracle_fft, l.oracle_dft, l.oracle_fft_axis, l.oracle_fft_batch,
+                  l.oracle_r2c_batch, l.oracle_c2r_batch):
+            f.restype = ci
+        _lib = l
+    return _lib
+
+
+def _dp(a):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
+
+
+def default_threads():
+    return max(1, os.cpu_count() or 1)
+
+
+def fft(x, inverse=False, normalize=False):
+    """1D C2C of one sequence, complex128 in/out (reference::fft)."""
+    x = np.ascontiguousarray(x, dtype=np.complex128)
+    out = np.empty_like(x)
+    if lib().oracle_fft(_dp(x), _dp(out), x.size, int(inverse), int(normalize)) != 0:
+        raise RuntimeError("oracle fft failed")
+    return out
+
+
+def dft(x, inverse=False, normalize=False):
+    """O(n^2) direct DFT (reference::dft)."""
+    x = np.ascontiguousarray(x, dtype=np.complex128)
+    out = np.empty_like(x)
+    lib().oracle_dft(_dp(x), _dp(out), x.size, int(inverse), int(normalize))
+    return out
+
+
+def fft_axis(x, axis, inverse=False, normalize=False, threads=None):
+    """C2C along one axis of a dense complex128 array (returns a new array)."""
+    x = np.ascontiguousarray(x, dtype=np.complex128)
+    out = np.empty_like(x)
+    shape = x.shape
+    outer = int(np.prod(shape[:axis], dtype=np.int64))
+    inner = int(np.prod(shape[axis + 1:], dtype=np.int64))
+    rc = lib().oracle_fft_axis(_dp(x), _dp(out), outer, shape[axis], inner, int(inverse),
+                               int(normalize), threads or default_threads())
+    if rc != 0:
+        raise RuntimeError("oracle fft_axis failed")
+    return out
+
+
+def fft_nd(x, ndim, inverse=False, normalize=False, threads=None):
+    """Separable C2C over the last ``ndim`` axes (leading axes are batch)."""
+    y = np.ascontiguousarray(x, dtype=np.complex128)
+    for axis in range(y.ndim - 1, y.ndim - 1 - ndim, -1):
+        y = fft_axis(y, axis, inverse, normalize, threads)
+    return y
+
+
+def r2c(x, threads=None):
+    """Batched R2C along the last axis: (..., n) float64 -> (..., n//2+1) complex128."""
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    n = x.shape[-1]
+    batch = x.size // n
+    out = np.empty(x.shape[:-1] + (n // 2 + 1,), dtype=np.complex128)
+    if lib().oracle_r2c_batch(_dp(x), _dp(out), n, batch, threads or default_threads()) != 0:
+        raise RuntimeError("oracle r2c failed")
+    return out
+
+
+def c2r(x, n, normalize=False, threads=None):
+    """Batched C2R along the last axis: (..., n//2+1) complex128 -> (..., n) float64."""
+    x = np.ascontiguousarray(x, dtype=np.complex128)
+    batch = x.size // (n // 2 + 1)
+    out = np.empty(x.shape[:-1] + (n,), dtype=np.float64)
+    if lib().oracle_c2r_batch(_dp(x), _dp(out), n, batch, int(normalize),
+                              threads or default_threads()) != 0:
+        raise RuntimeError("oracle c2r failed")
+    return out
+
+
+def r2c_nd(x, ndim, threads=None):
+    """ND R2C: real axis on the fastest dim, then complex axes on the compact shape
+    (nd_real_ir.rs:21-41)."""
+    y = r2c(x, threads)
+    for axis in range(y.ndim - 2, y.ndim - 1 - ndim, -1):
+        y = fft_axis(y, axis, False, False, threads)
+    return y
+
+
+def c2r_nd(x, shape_last, ndim, normalize=False, threads=None):
+    """ND C2R: complex inverse axes on the compact shape, then C2R on the fastest."""
+    y = np.ascontiguousarray(x, dtype=np.complex128)
+    for axis in range(y.ndim - 1 - ndim + 1, y.ndim - 1):
+        y = fft_axis(y, axis, True, normalize, threads)
+    return c2r(y, shape_last, normalize, threads)
+
+
+def next_smooth_at_least(target):
+    return int(lib().oracle_next_smooth_at_least(target))

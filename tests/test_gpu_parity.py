@@ -1,0 +1,180 @@
+"""GPU parity: the B200 kernels, called through the C ABI, against the CPU oracle
+(a restatement of vkfft-rs src/reference.rs) on identical seeded inputs.
+
+Tolerances: relative L2 <= 2e-6 for f32 compute, <= 1e-13 for f64.
+FFTW golden vectors are also checked at the reference's own GPU tolerances
+(tests/fftw_medium_golden.rs:161-171: f64 1e-8*n, f32 1e-4*n max abs)."""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_l2, uniform_complex
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"F32": 2e-6, "F64": 1e-13}
+NP = {"F32": (np.complex64, np.float32), "F64": (np.complex128, np.float64)}
+
+
+def run_c2c(V, ctx, dims, batch, prec, direction, normalize=False, tuning=None, seed=0):
+    cfg = V.FftConfig(dims).with_batch_count(batch).with_precision(V.Precision[prec])
+    cfg = cfg.with_inverse_normalization(normalize)
+    if tuning is not None:
+        cfg = cfg.with_tuning(tuning)
+    ir = V.TransformIr.build(cfg, direction, ctx.device_profile())
+    rng = np.random.default_rng(seed)
+    x = uniform_complex(rng, (batch,) + tuple(dims), NP[prec][0])
+    y = ctx.execute_transform(ir, x).reshape(x.shape)
+    ref = oracle.fft_nd(x.astype(np.complex128), len(dims), inverse=direction == V.Direction.INVERSE,
+                        normalize=normalize)
+    return ir, rel_l2(y, ref)
+
+
+C2C_1D = [
+    # (N, batch): BASELINE config 1 (1024 x 8) plus radix / Rader / Bluestein coverage
+    (1024, 8), (4096, 64), (8, 16), (16, 8), (64, 33), (100, 7), (360, 5), (1000, 3), (1536, 4), (2048, 4),
+    (3 ** 7, 2), (5 ** 5, 2), (7 ** 4, 2), (11 * 13 * 16, 2), (17, 64), (47, 32), (257, 8), (89, 16),
+    (4099, 6), (83 * 4, 4), (17 * 17, 3), (1, 5), (2, 9),
+]
+
+
+@pytest.mark.parametrize("prec", ["F32", "F64"])
+@pytest.mark.parametrize("n,batch", C2C_1D)
+def test_c2c_1d_forward(V, ctx, n, batch, prec):
+    ir, err = run_c2c(V, ctx, [n], batch, prec, V.Direction.FORWARD, seed=n)
+    assert err <= TOL[prec], (ir.axis_child(0), err)
+
+
+@pytest.mark.parametrize("prec", ["F32", "F64"])
+@pytest.mark.parametrize("n,batch", [(1024, 8), (17, 16), (4099, 3), (360, 4), (47, 8), (131072, 2)])
+def test_c2c_1d_inverse_normalized(V, ctx, n, batch, prec):
+    ir, err = run_c2c(V, ctx, [n], batch, prec, V.Direction.INVERSE, normalize=True, seed=n + 1)
+    assert err <= TOL[prec], (ir.axis_child(0), err)
+
+
+@pytest.mark.parametrize("prec", ["F32", "F64"])
+def test_c2c_large_four_step_and_bluestein_multipass(V, ctx, prec):
+    # 2^17 (four-step) and the BASELINE Bluestein N=65537 (device M=131220, three passes)
+    for n, batch in ((131072, 3), (65537, 2)):
+        ir, err = run_c2c(V, ctx, [n], batch, prec, V.Direction.FORWARD, seed=7)
+        assert err <= TOL[prec], (n, ir.axis_child(0), err)
+
+
+@pytest.mark.parametrize("prec", ["F32", "F64"])
+def test_recursive_rader_tuning_plans_rader_for_4099(V, ctx, prec):
+    rec = V.PlannerTuning.portable().with_recursive_fft_rader(True)
+    cfg = V.FftConfig([4099]).with_batch_count(2).with_precision(V.Precision[prec]).with_tuning(rec)
+    ir = V.TransformIr.build(cfg, V.Direction.FORWARD, ctx.device_profile())
+    assert ir.axis_child(0).kind == V.AlgorithmKind.RADER
+
+
+@pytest.mark.parametrize("prec", ["F32", "F64"])
+@pytest.mark.parametrize("dims,batch", [([8, 16], 3), ([64, 64, 64], 1), ([32, 17, 100], 2), ([5, 47, 12], 2),
+                                        ([2, 17, 4099], 1), ([16, 1, 64], 2)])
+def test_c2c_nd(V, ctx, dims, batch, prec):
+    for direction, norm in ((V.Direction.FORWARD, False), (V.Direction.INVERSE, True)):
+        ir, err = run_c2c(V, ctx, dims, batch, prec, direction, normalize=norm, seed=len(dims))
+        assert err <= TOL[prec], (dims, direction, err)
+
+
+@pytest.mark.parametrize("prec", ["F32", "F64"])
+def test_c2c_3d_stockham_rader_bluestein_small_batch(V, ctx, prec):
+    # BASELINE config 4 shape family [.., 17, 65537] with the outer axis shortened
+    ir, err = run_c2c(V, ctx, [2, 17, 65537], 1, prec, V.Direction.FORWARD, seed=3)
+    assert [ir.axis_child(k).kind.name for k in range(3)] == ["STOCKHAM", "RADER", "BLUESTEIN"]
+    assert err <= TOL[prec]
+
+
+def run_real(V, ctx, dims, batch, prec, seed=0):
+    cdt, rdt = NP[prec]
+    p = V.Precision[prec]
+    dev = ctx.device_profile()
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(-1, 1, size=(batch,) + tuple(dims)).astype(rdt)
+    fwd = V.TransformIr.build(V.FftConfig(dims).with_batch_count(batch).with_precision(p)
+                              .with_transform(V.TransformKind.R2C), V.Direction.FORWARD, dev)
+    spec = ctx.execute_transform(fwd, x)
+    ref = oracle.r2c_nd(x.astype(np.float64), len(dims))
+    e1 = rel_l2(spec, ref)
+    inv = V.TransformIr.build(V.FftConfig(dims).with_batch_count(batch).with_precision(p)
+                              .with_transform(V.TransformKind.C2R).with_inverse_normalization(True),
+                              V.Direction.INVERSE, dev)
+    back = ctx.execute_transform(inv, ref.astype(cdt))
+    ref_back = oracle.c2r_nd(ref.astype(cdt).astype(np.complex128), dims[-1], len(dims), normalize=True)
+    e2 = rel_l2(back, ref_back)
+    return fwd, e1, e2
+
+
+@pytest.mark.parametrize("prec", ["F32", "F64"])
+@pytest.mark.parametrize("dims,batch", [([4096], 16), ([30], 7), ([94], 5), ([206], 3), ([45], 4), ([2048], 3),
+                                        ([8704], 2), ([4106], 2), ([17, 34], 2), ([64, 64], 2), ([16, 32, 30], 1),
+                                        ([1, 64], 3)])
+def test_r2c_c2r(V, ctx, dims, batch, prec):
+    ir, e1, e2 = run_real(V, ctx, dims, batch, prec, seed=dims[-1])
+    assert e1 <= TOL[prec], (dims, ir.real_algorithm, e1)
+    assert e2 <= TOL[prec], (dims, ir.real_algorithm, e2)
+
+
+def _golden_inputs(kind, n, f32):
+    x = np.arange(n, dtype=np.float32 if f32 else np.float64)
+    if f32:
+        if kind == 0:
+            return (np.sin(np.float32(0.137) * x) + np.float32(0.0013) * x
+                    + 1j * (np.cos(np.float32(0.071) * x) - np.float32(0.0009) * x)).astype(np.complex64)
+        return (np.sin(np.float32(0.173) * x) + np.float32(0.003) * x
+                - np.float32(0.27) * np.cos(np.float32(0.071) * x)).astype(np.float32)
+    if kind == 0:
+        return np.sin(0.137 * x) + 0.0013 * x + 1j * (np.cos(0.071 * x) - 0.0009 * x)
+    return np.sin(0.173 * x) + 0.003 * x - 0.27 * np.cos(0.071 * x)
+
+
+@pytest.mark.parametrize("set_name,prec", [("medium", "F64"), ("medium_f32", "F32")])
+def test_fftw_golden_vectors_on_gpu(V, ctx, set_name, prec):
+    import os
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "fftw_golden.npz"))
+    names = sorted({k.rsplit("/", 1)[0].split("/", 1)[1] for k in z.files if k.startswith(set_name + "/")})
+    dev = ctx.device_profile()
+    for name in names:
+        shape = [int(v) for v in z[f"{set_name}/{name}/shape"]]
+        kind = int(z[f"{set_name}/{name}/kind"])
+        n = int(np.prod(shape))
+        cfg = V.FftConfig(shape).with_precision(V.Precision[prec])
+        if kind == 1:
+            cfg = cfg.with_transform(V.TransformKind.R2C)
+        if name == "c2c-bluestein-n103":
+            t = V.PlannerTuning.portable()
+            t.max_rader_fft_prime = 100
+            cfg = cfg.with_tuning(t)
+        ir = V.TransformIr.build(cfg, V.Direction.FORWARD, dev)
+        got = ctx.execute_transform(ir, _golden_inputs(kind, n, prec == "F32"))
+        tol = (1e-4 if prec == "F32" else 1e-8) * n
+        assert np.abs(got - z[f"{set_name}/{name}/output"]).max() <= tol, name
+
+
+def test_resident_execution_matches_host_execution(V, ctx):
+    torch = pytest.importorskip("torch")
+    dev = ctx.device_profile()
+    ir = V.TransformIr.build(V.FftConfig([4096]).with_batch_count(32), V.Direction.FORWARD, dev)
+    rng = np.random.default_rng(11)
+    x = uniform_complex(rng, (32, 4096), np.complex64)
+    host = ctx.execute_transform(ir, x)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty_like(xd)
+    stream = torch.cuda.current_stream().cuda_stream
+    ctx.execute_resident(ir, xd.data_ptr(), yd.data_ptr(), stream=stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(yd.cpu().numpy().ravel(), host)
+    # in place
+    ctx.execute_resident(ir, xd.data_ptr(), xd.data_ptr(), stream=stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(xd.cpu().numpy().ravel(), host)
+
+
+def test_input_length_mismatch_is_reported(V, ctx):
+    ir = V.TransformIr.build(V.FftConfig([64]).with_batch_count(2), V.Direction.FORWARD, ctx.device_profile())
+    import ctypes
+    x = np.zeros(100, dtype=np.complex64)
+    out = np.zeros(128, dtype=np.complex64)
+    lib = V.library()
+    st = lib.b200fft_execute_host(ctx._h, ir._h, x.ctypes.data, x.nbytes, out.ctypes.data, out.nbytes)
+    assert st == V.Status.InputLengthMismatch

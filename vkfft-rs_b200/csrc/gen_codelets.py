@@ -1,0 +1,174 @@
+"""Generate dft_codelets.cuh: fully unrolled forward DFT butterflies for the
+radices the B200 Stockham kernels use.
+
+Each codelet ``dft<R>(v)`` computes, in place on ``v[0..R)``,
+    y[k] = sum_n v[n] * exp(-2*pi*i*n*k/R).
+Odd primes use the symmetric pair form y[k] = A_k - i B_k, y[R-k] = A_k + i B_k
+with A_k = x0 + sum_n (x_n + x_{R-n}) cos(2 pi n k / R) and
+B_k = sum_n (x_n - x_{R-n}) sin(2 pi n k / R).  Composite radices use one
+Cooley-Tukey split R = R1 * R2 with literal twiddles; trivial twiddles
+(+-1, +-i, (+-1 +-i)/sqrt2) are emitted without multiplications.
+Inverse transforms are obtained by the caller through conjugation.
+
+Constants are computed with numpy longdouble and printed with 21 significant
+digits, so the double literals are correctly rounded.
+
+Usage: python gen_codelets.py  (writes dft_codelets.cuh beside this file)
+"""
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PI = np.longdouble("3.14159265358979323846264338327950288")
+
+PRIMES = [2, 3, 5, 7, 11, 13]
+SPLITS = {4: (2, 2), 8: (2, 4), 9: (3, 3), 16: (4, 4), 6: (2, 3), 10: (2, 5), 12: (3, 4), 14: (2, 7),
+          15: (3, 5), 32: (4, 8)}
+RADICES = [2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 32]
+
+
+def lit(x):
+    s = np.format_float_scientific(np.longdouble(x), precision=20, unique=False)
+    return f"T({s})"
+
+
+def cs(m, r):
+    a = 2 * PI * np.longdouble(m % r) / np.longdouble(r)
+    return np.cos(a), np.sin(a)
+
+
+def emit_prime(r):
+    lines = [f"template <typename T> B200FFT_HD void dft{r}(cplx<T>* v) {{"]
+    if r == 2:
+        lines += [
+            "    const cplx<T> a = v[0], b = v[1];",
+            "    v[0].x = a.x + b.x; v[0].y = a.y + b.y;",
+            "    v[1].x = a.x - b.x; v[1].y = a.y - b.y;",
+            "}",
+        ]
+        return lines
+    h = (r - 1) // 2
+    lines.append("    const cplx<T> x0 = v[0];")
+    for n in range(1, h + 1):
+        lines.append(f"    const T s{n}x = v[{n}].x + v[{r - n}].x, s{n}y = v[{n}].y + v[{r - n}].y;")
+        lines.append(f"    const T d{n}x = v[{n}].x - v[{r - n}].x, d{n}y = v[{n}].y - v[{r - n}].y;")
+    sx = " + ".join(f"s{n}x" for n in range(1, h + 1))
+    sy = " + ".join(f"s{n}y" for n in range(1, h + 1))
+    lines.append(f"    v[0].x = x0.x + {sx}; v[0].y = x0.y + {sy};")
+    for k in range(1, h + 1):
+        ax, ay, bx, by = ["x0.x"], ["x0.y"], [], []
+        for n in range(1, h + 1):
+            c, s = cs(n * k, r)
+            ax.append(f"{lit(c)} * s{n}x")
+            ay.append(f"{lit(c)} * s{n}y")
+            bx.append(f"{lit(s)} * d{n}x")
+            by.append(f"{lit(s)} * d{n}y")
+        lines.append(f"    {{ const T ax = {' + '.join(ax)}; const T ay = {' + '.join(ay)};")
+        lines.append(f"      const T bx = {' + '.join(bx)}; const T by = {' + '.join(by)};")
+        lines.append(f"      v[{k}].x = ax + by; v[{k}].y = ay - bx;")
+        lines.append(f"      v[{r - k}].x = ax - by; v[{r - k}].y = ay + bx; }}")
+    lines.append("}")
+    return lines
+
+
+def twiddle_stmt(dst, m, r):
+    """dst *= exp(-2 pi i m / r), with the trivial cases special-cased."""
+    m %= r
+    if m == 0:
+        return []
+    # reduce to eighths when exact
+    if (8 * m) % r == 0:
+        e = (8 * m) // r  # angle = -e*pi/4
+        sq = lit(np.sqrt(np.longdouble(0.5)))
+        if e == 2:  # -i
+            return [f"{{ const T q = {dst}.x; {dst}.x = {dst}.y; {dst}.y = -q; }}"]
+        if e == 4:  # -1
+            return [f"{dst}.x = -{dst}.x; {dst}.y = -{dst}.y;"]
+        if e == 6:  # +i
+            return [f"{{ const T q = {dst}.x; {dst}.x = -{dst}.y; {dst}.y = q; }}"]
+        if e == 1:  # (1 - i)/sqrt2
+            return [f"{{ const T a = {dst}.x, b = {dst}.y; {dst}.x = {sq} * (a + b); {dst}.y = {sq} * (b - a); }}"]
+        if e == 3:  # (-1 - i)/sqrt2
+            return [f"{{ const T a = {dst}.x, b = {dst}.y; {dst}.x = {sq} * (b - a); {dst}.y = -{sq} * (a + b); }}"]
+        if e == 5:  # (-1 + i)/sqrt2
+            return [f"{{ const T a = {dst}.x, b = {dst}.y; {dst}.x = -{sq} * (a + b); {dst}.y = {sq} * (a - b); }}"]
+        if e == 7:  # (1 + i)/sqrt2
+            return [f"{{ const T a = {dst}.x, b = {dst}.y; {dst}.x = {sq} * (a - b); {dst}.y = {sq} * (a + b); }}"]
+    c, s = cs(m, r)
+    return [f"{{ const T a = {dst}.x, b = {dst}.y; {dst}.x = a * {lit(c)} + b * {lit(s)}; "
+            f"{dst}.y = b * {lit(c)} - a * {lit(s)}; }}"]
+
+
+def emit_split(r):
+    r1, r2 = SPLITS[r]
+    lines = [f"template <typename T> B200FFT_HD void dft{r}(cplx<T>* v) {{"]
+    lines.append(f"    cplx<T> t[{r}];")
+    for n1 in range(r1):
+        lines.append(f"    {{ cplx<T> u[{r2}];")
+        for n2 in range(r2):
+            lines.append(f"      u[{n2}] = v[{n1 + r1 * n2}];")
+        lines.append(f"      dft{r2}<T>(u);")
+        for k2 in range(r2):
+            lines += ["      " + s for s in twiddle_stmt(f"u[{k2}]", n1 * k2, r)]
+            lines.append(f"      t[{n1 * r2 + k2}] = u[{k2}];")
+        lines.append("    }")
+    for k2 in range(r2):
+        lines.append(f"    {{ cplx<T> w[{r1}];")
+        for n1 in range(r1):
+            lines.append(f"      w[{n1}] = t[{n1 * r2 + k2}];")
+        lines.append(f"      dft{r1}<T>(w);")
+        for k1 in range(r1):
+            lines.append(f"      v[{k2 + r2 * k1}] = w[{k1}];")
+        lines.append("    }")
+    lines.append("}")
+    return lines
+
+
+def main():
+    out = [
+        "// Generated by gen_codelets.py -- do not edit by hand.",
+        "// Forward DFT butterflies y[k] = sum_n v[n] exp(-2 pi i n k / R), in place.",
+        "#pragma once",
+        "",
+        "#ifndef B200FFT_HD",
+        "#ifdef __CUDACC__",
+        "#define B200FFT_HD __host__ __device__ __forceinline__",
+        "#else",
+        "#define B200FFT_HD inline",
+        "#endif",
+        "#endif",
+        "",
+        "template <typename T> struct alignas(2 * sizeof(T)) cplx { T x, y; };",
+        "",
+    ]
+    done = set()
+
+    def gen(r):
+        if r in done:
+            return
+        if r in PRIMES:
+            out.extend(emit_prime(r))
+        else:
+            r1, r2 = SPLITS[r]
+            gen(r1)
+            gen(r2)
+            out.extend(emit_split(r))
+        out.append("")
+        done.add(r)
+
+    for r in RADICES:
+        gen(r)
+    out.append("template <int R, typename T> B200FFT_HD void dft(cplx<T>* v) {")
+    for i, r in enumerate(RADICES):
+        kw = "if" if i == 0 else "else if"
+        out.append(f"    {kw} constexpr (R == {r}) dft{r}<T>(v);")
+    out.append("}")
+    path = os.path.join(HERE, "dft_codelets.cuh")
+    with open(path, "w") as fh:
+        fh.write("\n".join(out) + "\n")
+    print("wrote", path)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,866 @@
+// Lowering: per-axis plans -> B200 launch programs.
+//
+// Every axis transform becomes one pass when its working set fits in one CTA's
+// shared memory (Stockham / Rader / Bluestein all fused into a single
+// load -> on-chip program -> store), otherwise a four-step split (Stockham) or a
+// three-pass convolution (Bluestein) through device scratch.  Tables are built
+// on the host in f64 (roots from long double, the Bluestein chirp with the
+// reference's own f64 expression) and rounded to f32 for f32 passes.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "lower.hpp"
+
+namespace b200fft {
+
+FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f{};
+    f.d = d;
+    uint32_t s = 0;
+    while (s < 31 && (1u << s) < d) s++;
+    f.s = s;
+    f.m = (uint32_t)((((uint64_t)1 << 32) * (((uint64_t)1 << s) - d)) / d + 1);
+    return f;
+}
+
+// ---- host tables ------------------------------------------------------------
+
+static std::complex<double> root(size_t m, size_t n) {
+    // exp(-2 pi i m / n) rounded from long double
+    const long double PIL = 3.141592653589793238462643383279502884L;
+    long double a = -2.0L * PIL * (long double)(m % n) / (long double)n;
+    return {(double)cosl(a), (double)sinl(a)};
+}
+
+static int add_table(Program &prog, const std::string &key, HostTable t) {
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    prog.tables.push_back(std::move(t));
+    int id = (int)prog.tables.size() - 1;
+    prog.table_cache[key] = id;
+    return id;
+}
+
+int table_twiddle(Program &prog, size_t n) {
+    std::string key = "W" + std::to_string(n);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    HostTable t;
+    t.c.resize(n);
+    for (size_t m = 0; m < n; m++) t.c[m] = root(m, n);
+    return add_table(prog, key, std::move(t));
+}
+
+// Bluestein chirp exactly as the reference evaluates it (reference.rs:121-125,
+// lut.rs:295-299): angle = sign * PI * (i as f64) * (i as f64) / (n as f64), not
+// reduced modulo 2n, then libm cos / sin.  Forward sign (-1); inverse transforms
+// use the conjugate, which is bit-identical to the +1 evaluation.
+static std::vector<std::complex<double>> reference_chirp(size_t n) {
+    const double PI = 3.14159265358979323846264338327950288;
+    std::vector<std::complex<double>> c(n);
+    for (size_t i = 0; i < n; i++) {
+        double x = (double)i;
+        double angle = -1.0 * PI * x * x / (double)n;
+        c[i] = {std::cos(angle), std::sin(angle)};
+    }
+    return c;
+}
+
+int table_bluestein_chirp(Program &prog, size_t n) {
+    std::string key = "chirp" + std::to_string(n);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    HostTable t;
+    t.c = reference_chirp(n);
+    return add_table(prog, key, std::move(t));
+}
+
+// FFT_M(b) / M with b[i] = b[M-i] = conj(chirp[i]) (bluestein_ir.rs:629, reference.rs:125-130).
+int table_bluestein_spectrum(Program &prog, size_t n, size_t m) {
+    std::string key = "bspec" + std::to_string(n) + "_" + std::to_string(m);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    auto chirp = reference_chirp(n);
+    std::vector<std::complex<double>> b(m, {0.0, 0.0});
+    for (size_t i = 0; i < n; i++) {
+        std::complex<double> ic = std::conj(chirp[i]);
+        b[i] = ic;
+        if (i != 0) b[m - i] = ic;
+    }
+    host_fft_inplace(b, false);
+    double s = 1.0 / (double)m;
+    for (auto &v : b) v *= s;
+    HostTable t;
+    t.c = std::move(b);
+    return add_table(prog, key, std::move(t));
+}
+
+// Accurate host mixed-radix FFT (Stockham, twiddles from long double), used only to
+// build kernel spectra.  O(n * sum of prime factors).
+void host_fft_inplace(std::vector<std::complex<double>> &x, bool inverse) {
+    const size_t n = x.size();
+    if (n <= 1) return;
+    auto f = prime_factorization(n);
+    std::vector<std::complex<double>> w(n);
+    for (size_t m = 0; m < n; m++) {
+        auto r = root(m, n);
+        w[m] = inverse ? std::conj(r) : r;
+    }
+    std::vector<std::complex<double>> y(n);
+    size_t P = 1;
+    for (size_t r : f) {
+        const size_t nbl = n / r;
+        const size_t tstep = n / (P * r);
+        std::vector<std::complex<double>> v(r), o(r);
+        for (size_t bb = 0; bb < nbl; bb++) {
+            const size_t j = bb % P;
+            for (size_t q = 0; q < r; q++) v[q] = x[bb + q * nbl] * w[(j * q * tstep) % n];
+            for (size_t k = 0; k < r; k++) {
+                std::complex<double> s = 0;
+                for (size_t q = 0; q < r; q++) s += v[q] * w[((q * k) % r) * (n / r)];
+                o[k] = s;
+            }
+            const size_t e0 = (bb - j) * r + j;
+            for (size_t q = 0; q < r; q++) y[e0 + q * P] = o[q];
+        }
+        std::swap(x, y);
+        P *= r;
+    }
+}
+
+// Rader tables for prime p with generator g (rader_ir.rs:35-380, lut.rs:375-435):
+// perm[m] = g^m mod p, ginv[m] = g^-m mod p, b[m] = W_p^{ginv[m]};
+// FFT mode uses FFT_{p-1}(b) / (p-1).
+struct RaderTables {
+    int perm, ginv, kernel;
+};
+
+static RaderTables table_rader(Program &prog, size_t p, size_t g, bool fft_mode) {
+    std::string kp = "rperm" + std::to_string(p), ki = "rginv" + std::to_string(p);
+    std::string kk = (fft_mode ? "rspec" : "rker") + std::to_string(p);
+    RaderTables rt{};
+    std::vector<int32_t> perm(p - 1), ginv(p - 1);
+    size_t v = 1;
+    for (size_t m = 0; m < p - 1; m++) {
+        perm[m] = (int32_t)v;
+        v = (v * g) % p;
+    }
+    // g^-1 = g^(p-2)
+    size_t gi = 1;
+    for (size_t m = 0; m < p - 2; m++) gi = (gi * g) % p;
+    v = 1;
+    for (size_t m = 0; m < p - 1; m++) {
+        ginv[m] = (int32_t)v;
+        v = (v * gi) % p;
+    }
+    HostTable tp;
+    tp.is_int = true;
+    tp.i = perm;
+    rt.perm = add_table(prog, kp, std::move(tp));
+    HostTable ti;
+    ti.is_int = true;
+    ti.i = ginv;
+    rt.ginv = add_table(prog, ki, std::move(ti));
+    std::vector<std::complex<double>> b(p - 1);
+    for (size_t m = 0; m < p - 1; m++) b[m] = root((size_t)ginv[m], p);
+    if (fft_mode) {
+        host_fft_inplace(b, false);
+        double s = 1.0 / (double)(p - 1);
+        for (auto &x : b) x *= s;
+    }
+    HostTable tk;
+    tk.c = std::move(b);
+    rt.kernel = add_table(prog, kk, std::move(tk));
+    return rt;
+}
+
+// ---- radix schedules ----------------------------------------------------------
+
+// Radix stages for a {2,3,5,7,11,13}-smooth length (the B200 kernel's own choice;
+// only the algorithm family is contractual).
+std::vector<int> radix_schedule(size_t L) {
+    std::vector<int> st;
+    if (L <= 1) return st;
+    size_t e2 = 0, e3 = 0, rem = L;
+    while (rem % 2 == 0) rem /= 2, e2++;
+    while (rem % 3 == 0) rem /= 3, e3++;
+    while (e2 >= 4) st.push_back(16), e2 -= 4;
+    while (e3 >= 2) st.push_back(9), e3 -= 2;
+    if (e2 == 3) {
+        st.push_back(8);
+    } else if (e2 == 2) {
+        if (e3) {
+            st.push_back(12);
+            e3--;
+        } else {
+            st.push_back(4);
+        }
+    } else if (e2 == 1) {
+        if (e3) {
+            st.push_back(6);
+            e3--;
+        } else if (rem % 5 == 0) {
+            st.push_back(10);
+            rem /= 5;
+        } else {
+            st.push_back(2);
+        }
+    }
+    if (e3) st.push_back(3);
+    for (int p : {5, 7, 11, 13})
+        while (rem % p == 0) st.push_back(p), rem /= p;
+    if (rem != 1) fail_invalid_ir("radix schedule requested for a non-smooth length");
+    return st;
+}
+
+static bool is_kernel_smooth(size_t L) {
+    for (size_t p : {2, 3, 5, 7, 11, 13})
+        while (L % p == 0) L /= p;
+    return L == 1;
+}
+
+// ---- one pass --------------------------------------------------------------------
+
+static int odd_stride(int len_with_pad) { return len_with_pad | 1; }
+static int spad_h(int e) { return e + (e >> 4); }
+static int line_stride_for(int L) { return odd_stride(spad_h(L) + 1); }
+
+struct StageSpec {
+    int radix;
+    bool rader = false;
+    bool direct = false;
+    size_t generator = 0;
+};
+
+// Stages of a line of length L for an axis algorithm (Stockham radices, Rader primes).
+std::vector<StageSpec> line_stages(size_t L, const AxisAlgorithm *alg) {
+    std::vector<StageSpec> out;
+    size_t smooth = L;
+    std::vector<StageSpec> rader;
+    if (alg && alg->kind == AlgorithmKind::Rader) {
+        for (auto &rp : alg->primes) {
+            for (size_t k = 0; k < rp.multiplicity; k++) {
+                StageSpec s;
+                s.radix = (int)rp.prime;
+                s.rader = true;
+                s.direct = !rp.fft_convolution;
+                s.generator = rp.generator;
+                rader.push_back(s);
+                smooth /= rp.prime;
+            }
+        }
+    }
+    for (int r : radix_schedule(smooth)) out.push_back(StageSpec{r});
+    for (auto &s : rader) out.push_back(s);
+    return out;
+}
+
+struct PassShape {
+    int G = 1, threads = 64, ls = 1, ws = 1, nbw = 0;
+    size_t smem = 0, meta_off = 0;
+};
+
+static size_t budget_bytes() { return 200 * 1024; }
+
+// Choose lines per CTA, threads and shared-memory layout.  Returns false when one
+// line does not fit on chip.
+static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bool strided, int64_t nlines,
+                       int nops, PassShape &sh) {
+    const size_t esz = dbl ? 16 : 8;
+    sh.ls = line_stride_for(L);
+    int pmin = 0, pmax = 0;
+    for (auto &s : stages)
+        if (s.rader) {
+            pmin = pmin ? std::min(pmin, s.radix) : s.radix;
+            pmax = std::max(pmax, s.radix);
+        }
+    sh.ws = pmax ? line_stride_for(pmax - 1) : 0;
+    auto bytes_for = [&](int G) {
+        size_t nbw = pmin ? (size_t)G * L / pmin : 0;
+        size_t data = (2 * (size_t)G * sh.ls + 2 * nbw * sh.ws + 2 * nbw) * esz;
+        data = (data + 15) & ~size_t(15);
+        size_t meta = (size_t)G * 16 + (size_t)((G + 3) & ~3) * 4;
+        meta = (meta + 15) & ~size_t(15);
+        return data + meta + (size_t)nops * sizeof(Op);
+    };
+    const int gmin = strided ? (dbl ? 4 : 8) : 1;
+    int G = std::max(gmin, (int)((2048 + L - 1) / L));
+    if (!strided) G = std::min<int64_t>(G, std::max<int64_t>(nlines, 1));
+    const size_t soft = 96 * 1024;
+    while (G > gmin && bytes_for(G) > soft) G--;
+    while (G > 1 && bytes_for(G) > budget_bytes()) G--;
+    if (bytes_for(G) > budget_bytes()) return false;
+    sh.G = G;
+    sh.nbw = pmin ? G * L / pmin : 0;
+    size_t nbw = sh.nbw;
+    size_t data = (2 * (size_t)G * sh.ls + 2 * nbw * sh.ws + 2 * nbw) * esz;
+    data = (data + 15) & ~size_t(15);
+    sh.meta_off = data;
+    sh.smem = bytes_for(G);
+    const int maxt = dbl ? 512 : 1024;
+    int64_t work = (int64_t)G * L / 8;
+    int t = (int)std::min<int64_t>(std::max<int64_t>(work, 64), maxt);
+    sh.threads = (t + 31) / 32 * 32;
+    return true;
+}
+
+// Shared-memory capacity only (for passes without an FFT network, e.g. real pre/post).
+static bool line_capacity_ok(bool dbl, size_t L) {
+    if (L > (1u << 20)) return false;
+    PassShape sh;
+    return shape_pass(dbl, (int)L, {}, false, 1 << 20, 8, sh);
+}
+
+bool line_fits_on_chip(bool dbl, size_t L, const AxisAlgorithm *alg, bool strided) {
+    if (L > (1u << 20)) return false;
+    if (alg && alg->kind == AlgorithmKind::Rader) {
+        for (auto &rp : alg->primes)
+            if (rp.fft_convolution && !is_kernel_smooth(rp.prime - 1)) return false;
+    }
+    size_t smooth = L;
+    if (alg && alg->kind == AlgorithmKind::Rader)
+        for (auto &rp : alg->primes)
+            for (size_t k = 0; k < rp.multiplicity; k++) smooth /= rp.prime;
+    if (!is_kernel_smooth(smooth)) return false;
+    PassShape sh;
+    return shape_pass(dbl, (int)L, line_stages(L, alg), strided, 1 << 20, 16, sh);
+}
+
+// Builds the op program of one pass.
+class PassBuilder {
+   public:
+    PassBuilder(Program &prog, int L, std::vector<StageSpec> stages, bool strided, int64_t nlines, int nops_hint)
+        : prog_(prog), L_(L), stages_(std::move(stages)) {
+        if (!shape_pass(prog.is_double, L, stages_, strided, nlines, nops_hint, sh_))
+            fail_resource("B200 FFT pass shared memory", (size_t)L * (prog.is_double ? 32 : 16), budget_bytes());
+        A_ = 0;
+        B_ = sh_.G * sh_.ls;
+        W_ = 2 * sh_.G * sh_.ls;
+        W2_ = W_ + sh_.nbw * sh_.ws;
+        X0_ = W2_ + sh_.nbw * sh_.ws;
+        cur_ = A_;
+        other_ = B_;
+        for (auto &row : plan_.op_tables) row[0] = row[1] = row[2] = -1;
+    }
+    int G() const { return sh_.G; }
+
+    Op &push(int type) {
+        if (nops_ >= kMaxOps) fail_invalid_ir("pass op program exceeds the kernel's op capacity");
+        Op &o = plan_.p.ops[nops_++];
+        std::memset(&o, 0, sizeof(Op));
+        o.type = type;
+        return o;
+    }
+    void set_tables(int a, int b = -1, int c = -1) {
+        plan_.op_tables[nops_ - 1][0] = a;
+        plan_.op_tables[nops_ - 1][1] = b;
+        plan_.op_tables[nops_ - 1][2] = c;
+    }
+
+    // global -> line region A
+    void load(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0) {
+        Op &o = push(OP_LOAD);
+        o.len = len;
+        o.flags = flags;
+        o.mul = mul;
+        o.dst_base = A_;
+        o.sub_stride = sh_.ls;
+        o.scale = scale;
+        o.div_a = make_fastdiv((uint32_t)len);
+        set_tables(table);
+        cur_ = A_;
+        other_ = B_;
+    }
+
+    // the full FFT network of the line (length L_) on the current region
+    void fft() {
+        const int tw = table_twiddle(prog_, (size_t)L_);
+        int P = 1;
+        for (auto &st : stages_) {
+            if (!st.rader) {
+                Op &o = push(OP_STAGE);
+                o.radix = st.radix;
+                o.P = P;
+                o.len = L_;
+                o.nsub = sh_.G;
+                o.src_base = cur_;
+                o.dst_base = other_;
+                o.sub_stride = sh_.ls;
+                o.div_a = make_fastdiv((uint32_t)(L_ / st.radix));
+                o.div_b = make_fastdiv((uint32_t)P);
+                set_tables(tw);
+            } else {
+                emit_rader(st, P, tw);
+            }
+            std::swap(cur_, other_);
+            P *= st.radix;
+        }
+    }
+
+    void herm_expand(int n) {
+        Op &o = push(OP_HERM_EXPAND);
+        o.src_base = cur_;
+        o.sub_stride = sh_.ls;
+        o.nfull = n;
+    }
+
+    void mul_region(int table, int flags, int cm, int em, int count = 0) {
+        Op &o = push(OP_MUL);
+        o.nfull = count;
+        o.len = L_;
+        o.nsub = sh_.G;
+        o.src_base = cur_;
+        o.sub_stride = sh_.ls;
+        o.mul = MUL_LUT_N;
+        o.cm = cm;
+        o.em = em;
+        o.flags = flags;
+        o.div_a = make_fastdiv((uint32_t)L_);
+        set_tables(table);
+    }
+
+    void r2c_post(int h, int wn_table) {
+        Op &o = push(OP_R2C_POST);
+        o.len = h;
+        o.src_base = cur_;
+        o.sub_stride = sh_.ls;
+        o.nfull = 2 * h;
+        set_tables(-1, wn_table);
+    }
+
+    void c2r_pre(int h, int wn_table, int flags, double scale) {
+        Op &o = push(OP_C2R_PRE);
+        o.len = h;
+        o.src_base = cur_;
+        o.sub_stride = sh_.ls;
+        o.nfull = 2 * h;
+        o.flags = flags;
+        o.scale = scale;
+        set_tables(-1, wn_table);
+    }
+
+    void store(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0) {
+        Op &o = push(OP_STORE);
+        o.len = len;
+        o.flags = flags;
+        o.mul = mul;
+        o.src_base = cur_;
+        o.sub_stride = sh_.ls;
+        o.scale = scale;
+        o.div_a = make_fastdiv((uint32_t)len);
+        set_tables(table);
+    }
+
+    PassPlan finish(int64_t no, int64_t ni, int64_t nc, const Side &in, const Side &out, int src_buf, int64_t src_off,
+                    int dst_buf, int64_t dst_off, const std::string &label) {
+        PassParams &p = plan_.p;
+        p.nlines = no * ni * nc;
+        p.ni = ni;
+        p.nc = nc;
+        p.G = sh_.G;
+        p.div_g = make_fastdiv((uint32_t)sh_.G);
+        p.nops = nops_;
+        p.line_len = L_;
+        p.line_stride = sh_.ls;
+        p.meta_off = (int32_t)sh_.meta_off;
+        p.in = in;
+        p.out = out;
+        plan_.src_buf = src_buf;
+        plan_.src_off = src_off;
+        plan_.dst_buf = dst_buf;
+        plan_.dst_off = dst_off;
+        plan_.grid = (p.nlines + sh_.G - 1) / sh_.G;
+        plan_.threads = sh_.threads;
+        plan_.smem = sh_.smem;
+        plan_.label = label;
+        return plan_;
+    }
+
+   private:
+    void emit_rader(const StageSpec &st, int P, int tw) {
+        const int p = st.radix;
+        const int nb = sh_.G * (L_ / p);
+        RaderTables rt = table_rader(prog_, (size_t)p, st.generator, !st.direct);
+        {
+            Op &o = push(OP_RADER_GATHER);
+            o.radix = p;
+            o.P = P;
+            o.len = L_;
+            o.nsub = sh_.G;
+            o.src_base = cur_;
+            o.sub_stride = sh_.ls;
+            o.w_base = W_;
+            o.w_stride = sh_.ws;
+            o.x0_base = X0_;
+            o.div_a = make_fastdiv((uint32_t)(L_ / p));
+            o.div_b = make_fastdiv((uint32_t)P);
+            o.div_c = make_fastdiv((uint32_t)p);
+            set_tables(tw, rt.perm);
+        }
+        int wcur = W_;
+        if (!st.direct) {
+            const int n1 = p - 1;
+            const int tw1 = table_twiddle(prog_, (size_t)n1);
+            auto sub = [&](int wsrc) {
+                int s = wsrc, d = (wsrc == W_) ? W2_ : W_;
+                int PP = 1;
+                for (int r : radix_schedule((size_t)n1)) {
+                    Op &o = push(OP_STAGE);
+                    o.radix = r;
+                    o.P = PP;
+                    o.len = n1;
+                    o.nsub = nb;
+                    o.src_base = s;
+                    o.dst_base = d;
+                    o.sub_stride = sh_.ws;
+                    o.div_a = make_fastdiv((uint32_t)(n1 / r));
+                    o.div_b = make_fastdiv((uint32_t)PP);
+                    set_tables(tw1);
+                    std::swap(s, d);
+                    PP *= r;
+                }
+                return s;
+            };
+            wcur = sub(W_);
+            {
+                Op &o = push(OP_MUL);
+                o.len = n1;
+                o.nsub = nb;
+                o.src_base = wcur;
+                o.sub_stride = sh_.ws;
+                o.mul = MUL_LUT_N;
+                o.cm = 0;
+                o.em = 1;
+                o.x0_base = X0_;
+                o.flags = F_SAVE_DC | F_CONJ_OUT;
+                o.div_a = make_fastdiv((uint32_t)n1);
+                set_tables(rt.kernel);
+            }
+            wcur = sub(wcur);
+        }
+        {
+            Op &o = push(OP_RADER_SCATTER);
+            o.radix = p;
+            o.P = P;
+            o.len = L_;
+            o.nsub = sh_.G;
+            o.dst_base = other_;
+            o.sub_stride = sh_.ls;
+            o.w_base = wcur;
+            o.w_stride = sh_.ws;
+            o.x0_base = X0_;
+            o.flags = st.direct ? F_DIRECT : F_CONJ_IN;
+            o.div_a = make_fastdiv((uint32_t)(L_ / p));
+            o.div_b = make_fastdiv((uint32_t)P);
+            o.div_c = make_fastdiv((uint32_t)p);
+            set_tables(rt.kernel, -1, rt.ginv);
+        }
+    }
+
+    Program &prog_;
+    int L_;
+    std::vector<StageSpec> stages_;
+    PassShape sh_;
+    PassPlan plan_{};
+    int nops_ = 0;
+    int A_, B_, W_, W2_, X0_, cur_, other_;
+};
+
+static Side make_side(int64_t os, int64_t is, int64_t cs, int64_t es, bool real, int64_t count, int cm, int em) {
+    Side s{};
+    s.os = os;
+    s.is = is;
+    s.cs = cs;
+    s.es = es;
+    s.real = real ? 1 : 0;
+    s.count = (int32_t)std::min<int64_t>(count, INT32_MAX);
+    s.cm = cm;
+    s.em = em;
+    return s;
+}
+
+// ---- axis lowering ----------------------------------------------------------------
+
+// Split a smooth length into N1 (columns pass, strided) x N2 (rows pass).
+static bool four_step_split(size_t N, size_t &N1, size_t &N2) {
+    size_t best = 0;
+    for (size_t d = 2; d * d <= N; d++)
+        if (N % d == 0 && is_kernel_smooth(d) && is_kernel_smooth(N / d)) best = d;
+    if (!best) return false;
+    N1 = best;
+    N2 = N / best;
+    return true;
+}
+
+void lower_c2c_axis(Program &prog, const AxisJob &job) {
+    const bool inv = job.inverse;
+    const size_t N = job.N;
+    const AxisAlgorithm *alg = job.alg;
+    const int64_t no = job.no, S = job.S;
+    const bool strided = S > 1;
+    // inverse = conj(forward(conj(x))): conjugate the raw input before any multiply of
+    // the first load and the final value after every multiply of the last store
+    const int cin = inv ? F_CONJ_IN : 0;
+    const int cout = inv ? F_CONJ_OUT : 0;
+    const double scale = job.scale;
+    const int fscale = scale != 1.0 ? F_SCALE : 0;
+    const size_t out_count = job.out_count ? job.out_count : N;
+    const size_t in_count = job.in_herm ? N / 2 + 1 : N;
+    const int in_len = (int)in_count;
+
+    if (N == 1) {
+        PassBuilder b(prog, 1, {}, strided, no * S, 4);
+        b.load(1, 0);
+        b.store(1, fscale, MUL_NONE, -1, scale);
+        prog.passes.push_back(b.finish(no, S, 1, make_side(job.in_os, 1, 0, S, job.in_real, 1, 0, 1),
+                                       make_side(job.out_os, 1, 0, S, job.out_real, 1, 0, 1), job.in_buf, job.in_off,
+                                       job.out_buf, job.out_off, "copy"));
+        return;
+    }
+
+    if (alg->kind != AlgorithmKind::Bluestein) {
+        if (line_fits_on_chip(prog.is_double, N, alg, strided)) {
+            PassBuilder b(prog, (int)N, line_stages(N, alg), strided, no * S, 24);
+            b.load(in_len, cin);
+            if (job.in_herm) b.herm_expand((int)N);
+            b.fft();
+            b.store((int)out_count, cout | fscale, MUL_NONE, -1, scale);
+            prog.passes.push_back(b.finish(no, S, 1, make_side(job.in_os, 1, 0, S, job.in_real, in_count, 0, 1),
+                                           make_side(job.out_os, 1, 0, S, job.out_real, out_count, 0, 1), job.in_buf,
+                                           job.in_off, job.out_buf, job.out_off, "stockham"));
+            return;
+        }
+        // four-step through scratch 0: columns (N1, stride N2), then rows (N2)
+        size_t N1, N2;
+        if (job.in_herm) fail_unsupported("B200 engine: multi-pass Hermitian (C2R full-complex) axis");
+        if (alg->kind == AlgorithmKind::Rader || !four_step_split(N, N1, N2))
+            fail_unsupported("B200 engine: axis too large for one CTA and not four-step decomposable");
+        if (!line_fits_on_chip(prog.is_double, N1, nullptr, true) ||
+            !line_fits_on_chip(prog.is_double, N2, nullptr, true))
+            fail_unsupported("B200 engine: four-step factors exceed on-chip capacity");
+        const int tw = table_twiddle(prog, N);
+        const int64_t scr_os = (int64_t)N * S;
+        prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * N * S));
+        {
+            PassBuilder b(prog, (int)N1, line_stages(N1, nullptr), true, no * S * N2, 8);
+            b.load((int)N1, cin);
+            b.fft();
+            b.store((int)N1, 0, MUL_TWIDDLE_CE, tw);
+            prog.passes.push_back(b.finish(no, S, (int64_t)N2,
+                                           make_side(job.in_os, 1, S, (int64_t)N2 * S, job.in_real, N, 1, (int)N2),
+                                           make_side(scr_os, 1, S, (int64_t)N2 * S, false, N, 1, (int)N2), job.in_buf,
+                                           job.in_off, BUF_SCRATCH0, 0, "four-step columns"));
+        }
+        {
+            PassBuilder b(prog, (int)N2, line_stages(N2, nullptr), true, no * S * N1, 8);
+            b.load((int)N2, 0);
+            b.fft();
+            b.store((int)N2, cout | fscale, MUL_NONE, -1, scale);
+            prog.passes.push_back(
+                b.finish(no, S, (int64_t)N1, make_side(scr_os, 1, (int64_t)N2 * S, S, false, N, (int)N2, 1),
+                         make_side(job.out_os, 1, S, (int64_t)N1 * S, job.out_real, out_count, 1, (int)N1),
+                         BUF_SCRATCH0, 0, job.out_buf, job.out_off, "four-step rows"));
+        }
+        return;
+    }
+
+    // Bluestein (bluestein_ir.rs:436-933): chirp, zero-pad to M, FFT_M, x spectrum, IFFT_M,
+    // chirp and take N.  With the conjugation trick the inverse uses the forward chirp.
+    const size_t M = alg->convolution_len;
+    const int chirp = table_bluestein_chirp(prog, N);
+    const int spec = table_bluestein_spectrum(prog, N, M);
+    if (line_fits_on_chip(prog.is_double, M, nullptr, strided)) {
+        PassBuilder b(prog, (int)M, line_stages(M, nullptr), strided, no * S, 24);
+        if (job.in_herm) {
+            b.load(in_len, cin);
+            b.herm_expand((int)N);
+            b.mul_region(chirp, 0, 0, 1, (int)N);
+        } else {
+            b.load((int)M, cin, MUL_LUT_N, chirp);
+        }
+        b.fft();
+        b.mul_region(spec, F_CONJ_OUT, 0, 1);
+        b.fft();
+        // store: conj (undo the inner inverse trick), multiply chirp, conj again if inverse
+        b.store((int)out_count, F_CONJ_IN | cout | fscale, MUL_LUT_N, chirp, scale);
+        prog.passes.push_back(b.finish(no, S, 1, make_side(job.in_os, 1, 0, S, job.in_real, in_count, 0, 1),
+                                       make_side(job.out_os, 1, 0, S, job.out_real, out_count, 0, 1), job.in_buf,
+                                       job.in_off, job.out_buf, job.out_off, "bluestein fused"));
+        return;
+    }
+    if (job.in_herm) fail_unsupported("B200 engine: multi-pass Hermitian (C2R full-complex) Bluestein axis");
+    size_t M1, M2;
+    if (!four_step_split(M, M1, M2)) fail_unsupported("B200 engine: Bluestein length not decomposable");
+    if (!line_fits_on_chip(prog.is_double, M1, nullptr, true) || !line_fits_on_chip(prog.is_double, M2, nullptr, true))
+        fail_unsupported("B200 engine: Bluestein four-step factors exceed on-chip capacity");
+    const int twM = table_twiddle(prog, M);
+    const int64_t scr_os = (int64_t)M * S;
+    prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * M * S));
+    // pass A: columns n2: x[n2 + M2 n1] * chirp (n < N, else 0), FFT over n1, * W_M^{n2 k1}
+    {
+        PassBuilder b(prog, (int)M1, line_stages(M1, nullptr), true, no * S * M2, 8);
+        b.load((int)M1, cin, MUL_LUT_N, chirp);
+        b.fft();
+        b.store((int)M1, 0, MUL_TWIDDLE_CE, twM);
+        prog.passes.push_back(b.finish(no, S, (int64_t)M2,
+                                       make_side(job.in_os, 1, S, (int64_t)M2 * S, job.in_real, N, 1, (int)M2),
+                                       make_side(scr_os, 1, S, (int64_t)M2 * S, false, M, 1, (int)M2), job.in_buf,
+                                       job.in_off, BUF_SCRATCH0, 0, "bluestein columns"));
+    }
+    // pass B: rows k1: FFT over n2 -> k2, * spectrum[k1 + M1 k2], inverse FFT over k2 -> n2,
+    // * conj(W_M^{n2 k1}), in place in scratch
+    {
+        PassBuilder b(prog, (int)M2, line_stages(M2, nullptr), true, no * S * M1, 8);
+        b.load((int)M2, 0);
+        b.fft();
+        b.mul_region(spec, F_CONJ_OUT, 1, (int)M1);
+        b.fft();
+        b.store((int)M2, F_CONJ_IN | F_CONJ_LUT, MUL_TWIDDLE_CE, twM);
+        prog.passes.push_back(b.finish(no, S, (int64_t)M1,
+                                       make_side(scr_os, 1, (int64_t)M2 * S, S, false, M, (int)M2, 1),
+                                       make_side(scr_os, 1, (int64_t)M2 * S, S, false, M, (int)M2, 1), BUF_SCRATCH0,
+                                       0, BUF_SCRATCH0, 0, "bluestein rows"));
+    }
+    // pass C: columns n2: inverse FFT over k1 -> n1, * chirp[n2 + M2 n1], keep n < out_count
+    {
+        PassBuilder b(prog, (int)M1, line_stages(M1, nullptr), true, no * S * M2, 8);
+        b.load((int)M1, F_CONJ_OUT);
+        b.fft();
+        b.store((int)M1, F_CONJ_IN | cout | fscale, MUL_LUT_N, chirp, scale);
+        prog.passes.push_back(
+            b.finish(no, S, (int64_t)M2, make_side(scr_os, 1, S, (int64_t)M2 * S, false, M, 1, (int)M2),
+                     make_side(job.out_os, 1, S, (int64_t)M2 * S, job.out_real, out_count, 1, (int)M2), BUF_SCRATCH0,
+                     0, job.out_buf, job.out_off, "bluestein columns inverse"));
+    }
+}
+
+// R2C of the contiguous axis.  EvenHalfSize (real_ir.rs:1002-1013): the real line is
+// read as N/2 complex pairs, transformed and post-processed into N/2+1 bins; fused into
+// one pass when the half-length child runs on chip, otherwise the child transform writes
+// scratch 2 and a post-processing pass produces the bins.  FullComplex: the real line is
+// promoted on load and the complex child keeps the first N/2+1 bins.
+void lower_r2c_axis(Program &prog, const RealAxisJob &job) {
+    const size_t N = job.N;
+    if (!job.full_complex && N % 2 == 0 && N >= 2) {
+        const size_t h = N / 2;
+        const int wn = table_twiddle(prog, N);
+        const bool fused = job.alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.is_double, h, job.alg, false) &&
+                           line_capacity_ok(prog.is_double, h + 1);
+        if (fused) {
+            PassBuilder b(prog, (int)h, line_stages(h, job.alg), false, job.lines, 24);
+            b.load((int)h, 0);
+            b.fft();
+            b.r2c_post((int)h, wn);
+            b.store((int)(h + 1), 0);
+            prog.passes.push_back(b.finish(job.lines, 1, 1, make_side((int64_t)h, 0, 0, 1, false, h, 0, 1),
+                                           make_side((int64_t)(h + 1), 0, 0, 1, false, h + 1, 0, 1), job.in_buf,
+                                           job.in_off, job.out_buf, job.out_off, "r2c even-half"));
+            return;
+        }
+        if (!line_capacity_ok(prog.is_double, h + 1))
+            fail_unsupported("B200 engine: real axis post-processing exceeds on-chip capacity");
+        prog.scratch_elems[2] = std::max(prog.scratch_elems[2], (size_t)job.lines * h);
+        AxisJob a;
+        a.N = h;
+        a.alg = job.alg;
+        a.no = job.lines;
+        a.in_buf = job.in_buf;
+        a.in_off = job.in_off;
+        a.in_os = (int64_t)h;
+        a.out_buf = BUF_SCRATCH2;
+        a.out_os = (int64_t)h;
+        lower_c2c_axis(prog, a);
+        PassBuilder b(prog, (int)h, {}, false, job.lines, 4);
+        b.load((int)h, 0);
+        b.r2c_post((int)h, wn);
+        b.store((int)(h + 1), 0);
+        prog.passes.push_back(b.finish(job.lines, 1, 1, make_side((int64_t)h, 0, 0, 1, false, h, 0, 1),
+                                       make_side((int64_t)(h + 1), 0, 0, 1, false, h + 1, 0, 1), BUF_SCRATCH2, 0,
+                                       job.out_buf, job.out_off, "r2c post-process"));
+        return;
+    }
+    AxisJob a;
+    a.N = N;
+    a.alg = job.alg;
+    a.no = job.lines;
+    a.S = 1;
+    a.in_buf = job.in_buf;
+    a.in_off = job.in_off;
+    a.in_os = (int64_t)N;
+    a.in_real = true;
+    a.out_buf = job.out_buf;
+    a.out_off = job.out_off;
+    a.out_os = (int64_t)(N / 2 + 1);
+    a.out_count = N / 2 + 1;
+    lower_c2c_axis(prog, a);
+}
+
+// C2R of the contiguous axis.  EvenHalfSize (real_ir.rs:1087-1100): N/2+1 bins ->
+// packed half spectrum -> inverse FFT_{N/2} -> N reals stored as N/2 complex pairs
+// (fused, or a pre-processing pass into scratch 2 followed by the child transform).
+// FullComplex: Hermitian expansion on chip, inverse complex transform, real part.
+void lower_c2r_axis(Program &prog, const RealAxisJob &job) {
+    const size_t N = job.N;
+    if (!job.full_complex && N % 2 == 0 && N >= 2) {
+        const size_t h = N / 2;
+        const int wn = table_twiddle(prog, N);
+        const bool fused = job.alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.is_double, h, job.alg, false) &&
+                           line_capacity_ok(prog.is_double, h + 1);
+        const int fsc = job.normalize ? F_SCALE : 0;
+        if (fused) {
+            PassBuilder b(prog, (int)h, line_stages(h, job.alg), false, job.lines, 24);
+            b.load((int)(h + 1), 0);
+            b.c2r_pre((int)h, wn, F_CONJ_OUT | fsc, job.normalize ? 0.5 : 1.0);
+            b.fft();
+            b.store((int)h, F_CONJ_OUT | fsc, MUL_NONE, -1, job.normalize ? 1.0 / (double)h : 1.0);
+            prog.passes.push_back(b.finish(job.lines, 1, 1, make_side((int64_t)(h + 1), 0, 0, 1, false, h + 1, 0, 1),
+                                           make_side((int64_t)h, 0, 0, 1, false, h, 0, 1), job.in_buf, job.in_off,
+                                           job.out_buf, job.out_off, "c2r even-half"));
+            return;
+        }
+        if (!line_capacity_ok(prog.is_double, h + 1))
+            fail_unsupported("B200 engine: real axis pre-processing exceeds on-chip capacity");
+        prog.scratch_elems[2] = std::max(prog.scratch_elems[2], (size_t)job.lines * h);
+        {
+            PassBuilder b(prog, (int)h, {}, false, job.lines, 4);
+            b.load((int)(h + 1), 0);
+            b.c2r_pre((int)h, wn, fsc, job.normalize ? 0.5 : 1.0);
+            b.store((int)h, 0);
+            prog.passes.push_back(b.finish(job.lines, 1, 1, make_side((int64_t)(h + 1), 0, 0, 1, false, h + 1, 0, 1),
+                                           make_side((int64_t)h, 0, 0, 1, false, h, 0, 1), job.in_buf, job.in_off,
+                                           BUF_SCRATCH2, 0, "c2r pre-process"));
+        }
+        AxisJob a;
+        a.N = h;
+        a.alg = job.alg;
+        a.no = job.lines;
+        a.inverse = true;
+        a.scale = job.normalize ? 1.0 / (double)h : 1.0;
+        a.in_buf = BUF_SCRATCH2;
+        a.in_os = (int64_t)h;
+        a.out_buf = job.out_buf;
+        a.out_off = job.out_off;
+        a.out_os = (int64_t)h;
+        lower_c2c_axis(prog, a);
+        return;
+    }
+    AxisJob a;
+    a.N = N;
+    a.alg = job.alg;
+    a.no = job.lines;
+    a.S = 1;
+    a.inverse = true;
+    a.scale = job.normalize ? 1.0 / (double)N : 1.0;
+    a.in_buf = job.in_buf;
+    a.in_off = job.in_off;
+    a.in_os = (int64_t)(N / 2 + 1);
+    a.in_herm = true;
+    a.out_buf = job.out_buf;
+    a.out_off = job.out_off;
+    a.out_os = (int64_t)N;
+    a.out_real = true;
+    lower_c2c_axis(prog, a);
+}
+
+}  // namespace b200fft

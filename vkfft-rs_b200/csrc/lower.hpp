@@ -1,0 +1,42 @@
+// Lowering interface: axis jobs -> passes of a Program.
+#pragma once
+
+#include "program.hpp"
+
+namespace b200fft {
+
+// One complex axis transform over a dense tensor viewed as [no][N][S]: line (o, i)
+// has element e at off + o*os + i + e*S.  (S = 1 for the contiguous axis.)
+struct AxisJob {
+    size_t N = 1;
+    const AxisAlgorithm *alg = nullptr;
+    int64_t no = 1, S = 1;
+    bool inverse = false;
+    double scale = 1.0;
+    int in_buf = BUF_IN, out_buf = BUF_OUT;
+    int64_t in_off = 0, out_off = 0;
+    int64_t in_os = 0, out_os = 0;
+    bool in_real = false;   // promote real input (FullComplex R2C)
+    bool in_herm = false;   // input holds N/2+1 Hermitian bins (FullComplex C2R)
+    bool out_real = false;  // keep the real part (FullComplex C2R)
+    size_t out_count = 0;   // bins stored per line (0: N)
+};
+
+// Real transform of the contiguous axis: lines of N reals <-> N/2+1 complex bins.
+struct RealAxisJob {
+    size_t N = 2;
+    int64_t lines = 1;
+    bool normalize = false;
+    bool full_complex = false;  // RealFftAlgorithm::FullComplex
+    const AxisAlgorithm *alg = nullptr;  // algorithm of the executed complex child
+    int in_buf = BUF_IN, out_buf = BUF_OUT;
+    int64_t in_off = 0, out_off = 0;
+};
+
+std::vector<int> radix_schedule(size_t L);
+bool line_fits_on_chip(bool dbl, size_t L, const AxisAlgorithm *alg, bool strided);
+void lower_c2c_axis(Program &prog, const AxisJob &job);
+void lower_r2c_axis(Program &prog, const RealAxisJob &job);
+void lower_c2r_axis(Program &prog, const RealAxisJob &job);
+
+}  // namespace b200fft

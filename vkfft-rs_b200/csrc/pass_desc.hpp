@@ -1,0 +1,102 @@
+// Launch descriptor of one B200 FFT pass, shared by the host lowering and the
+// device kernel.  A pass processes a batch of "lines" (independent 1D
+// sub-transforms) with one CTA per G lines: the lines are loaded into shared
+// memory, transformed by a short program of in-CTA operations (Stockham radix
+// stages, pointwise multiplies, Rader gather/scatter, real-FFT pre/post
+// processing) and stored back.  Plain POD so it can be a __grid_constant__
+// kernel parameter.
+#pragma once
+#include <cstdint>
+
+namespace b200fft {
+
+constexpr int kMaxOps = 24;
+
+enum OpType : int32_t {
+    OP_LOAD = 1,           // global -> line region (with optional multiply / conjugation)
+    OP_STORE = 2,          // line region -> global
+    OP_STAGE = 3,          // one in-place Stockham radix stage over a region's sub-lines
+    OP_MUL = 4,            // pointwise multiply of a region by a table
+    OP_R2C_POST = 5,       // even-N R2C post-processing of a half-length spectrum
+    OP_C2R_PRE = 6,        // even-N C2R pre-processing into a half-length spectrum
+    OP_RADER_GATHER = 7,   // radix-p Rader step: twiddle, generator permutation into the W region
+    OP_RADER_SCATTER = 8,  // radix-p Rader step: x0 + convolution -> Stockham output positions
+    OP_HERM_EXPAND = 9,    // fill slots N/2+1..N-1 of a Hermitian half spectrum with conj(X[N-k])
+};
+
+enum MulKind : int32_t {
+    MUL_NONE = 0,
+    MUL_LUT_N = 1,       // value *= lut[n], n = c*cm + e*em (logical index of the element)
+    MUL_TWIDDLE_CE = 2,  // value *= lut[c*e]  (four-step twiddle, c*e < table size)
+};
+
+enum OpFlags : int32_t {
+    F_CONJ_IN = 1,    // conjugate the data before the multiply
+    F_CONJ_LUT = 2,   // multiply by the conjugate of the table value
+    F_CONJ_OUT = 4,   // conjugate the data after the multiply
+    F_SAVE_DC = 8,    // OP_MUL: copy element 0 of every sub-line into the X0 region (slot 1) first
+    F_DIRECT = 16,    // OP_RADER_SCATTER: direct O(p^2) convolution instead of the FFT result
+    F_SCALE = 32,     // apply Op::scale
+};
+
+// Fast unsigned division by a run-time constant (round-up multiply-shift, valid for n < 2^31).
+struct FastDiv {
+    uint32_t d, m, s, _pad;
+};
+
+// Global addressing of one side (input or output) of a pass.  A line index l is
+// decomposed as l = (o * nc + c) * ni + i; element e of the line lives at
+//   base + o*os + i*is + c*cs + e*es
+// (units: complex elements, or scalars when real != 0).  The element's logical
+// index within the full axis is n = c*cm + e*em; only n < count is read (others
+// load as zero) or written.
+struct Side {
+    int64_t os, is, cs, es;
+    int32_t real;
+    int32_t count;
+    int32_t cm, em;
+};
+
+struct alignas(16) Op {
+    int32_t type;
+    int32_t flags;
+    int32_t radix;      // STAGE radix; RADER prime p
+    int32_t P;          // STAGE/RADER: product of the radices already applied (sub-transform span)
+    int32_t len;        // length of the transform (sub-line length) this op works on
+    int32_t nsub;       // number of sub-lines in the region
+    int32_t src_base;   // shared-memory offset of the source region (complex elements)
+    int32_t dst_base;   // shared-memory offset of the destination region
+    int32_t sub_stride; // shared-memory distance between sub-lines (complex elements)
+    int32_t mul;        // MulKind for LOAD/STORE/MUL
+    int32_t cm, em;     // MUL: table index = c*cm + e*em (MUL_LUT_N)
+    int32_t w_base;     // RADER: W region base (gather destination / scatter source)
+    int32_t w_stride;   // RADER: W sub-line stride
+    int32_t x0_base;    // RADER / MUL(F_SAVE_DC): X0 region base, two slots per butterfly
+    int32_t nfull;      // R2C/C2R/HERM_EXPAND: full real length N; MUL: only n < nfull (0: all)
+    FastDiv div_a;      // STAGE: len/radix; RADER: len/p; LOAD/STORE/MUL: len
+    FastDiv div_b;      // STAGE/RADER: P
+    FastDiv div_c;      // RADER: p
+    const void *lut;    // twiddle / multiply table (complex of the pass precision)
+    const void *lut2;   // RADER: generator powers (int32) ; R2C/C2R: W_N table
+    const void *lut3;   // RADER: inverse generator powers (int32)
+    double scale;
+};
+
+struct PassParams {
+    int64_t nlines;   // total number of lines in this launch
+    int64_t ni, nc;   // line decomposition
+    int32_t G;        // lines per CTA
+    int32_t nops;
+    int32_t line_len;     // elements kept per line in shared memory
+    int32_t line_stride;  // shared-memory distance between lines (odd, padded)
+    int32_t meta_off;     // byte offset of the per-line address table in shared memory
+    int32_t _pad;
+    FastDiv div_g;        // G
+    Side in, out;
+    const void *src;
+    void *dst;
+    int *err;         // device error word (0 = ok), set instead of trapping
+    Op ops[kMaxOps];
+};
+
+}  // namespace b200fft

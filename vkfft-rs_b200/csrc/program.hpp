@@ -1,0 +1,67 @@
+// Executable form of a transform: the launch list the B200 runtime replays.
+// Built on the host from an FftPlan (lower.cpp); tables are generated in f64 on
+// the host and uploaded once per context (runtime.cpp).
+#pragma once
+
+#include <complex>
+#include <cstdint>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "core.hpp"
+#include "pass_desc.hpp"
+
+namespace b200fft {
+
+enum BufId : int { BUF_IN = 0, BUF_OUT = 1, BUF_SCRATCH0 = 2, BUF_SCRATCH1 = 3, BUF_SCRATCH2 = 4 };
+constexpr int kScratchBuffers = 3;
+
+struct HostTable {
+    bool is_int = false;
+    std::vector<std::complex<double>> c;
+    std::vector<int32_t> i;
+    size_t bytes(bool dbl) const { return is_int ? i.size() * 4 : c.size() * (dbl ? 16 : 8); }
+};
+
+struct PassPlan {
+    PassParams p{};               // device pointers are patched at upload / launch
+    int op_tables[kMaxOps][3];    // table ids per op (lut, lut2, lut3) or -1
+    int src_buf = BUF_IN, dst_buf = BUF_OUT;
+    int64_t src_off = 0, dst_off = 0;  // element offsets (units of the side's element type)
+    int64_t grid = 0;
+    int threads = 0;
+    size_t smem = 0;
+    std::string label;
+};
+
+struct Program {
+    bool is_double = false;
+    std::vector<PassPlan> passes;
+    std::vector<HostTable> tables;
+    std::map<std::string, int> table_cache;
+    size_t scratch_elems[kScratchBuffers] = {0, 0, 0};  // complex elements of the compute precision
+    size_t input_elems = 0, output_elems = 0;
+    bool input_real = false, output_real = false;
+    double algorithmic_flops = 0;  // 5 N log2 N per complex transform (for reports)
+
+    size_t scratch_offset(int k) const {  // byte offset of scratch buffer k (256-byte aligned)
+        size_t off = 0;
+        for (int i = 0; i < k; i++) off += (scratch_elems[i] * (is_double ? 16 : 8) + 255) & ~size_t(255);
+        return off;
+    }
+    size_t scratch_bytes() const { return scratch_offset(kScratchBuffers); }
+};
+
+FastDiv make_fastdiv(uint32_t d);
+
+// Tables (host f64).  All roots are forward: W_N^m = exp(-2 pi i m / N).
+int table_twiddle(Program &prog, size_t n);
+int table_bluestein_chirp(Program &prog, size_t n);
+int table_bluestein_spectrum(Program &prog, size_t n, size_t m);
+void host_fft_inplace(std::vector<std::complex<double>> &x, bool inverse);
+
+// Lowering of a whole transform (TransformIr families) into a Program.
+struct LoweredTransform;
+
+}  // namespace b200fft

@@ -1,0 +1,238 @@
+// CUDA runtime side of the B200 FFT engine.
+#include "runtime.hpp"
+
+#include <algorithm>
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
+#include <set>
+
+namespace b200fft {
+
+int kernel_variant_for(bool is_double);
+cudaError_t launch_pass(int variant, const PassParams &p, int64_t grid, int threads, size_t smem, cudaStream_t stream);
+void set_kernel_smem_limits();
+
+// ---- host-side fault injection (no GPU fault is ever provoked) ------------------
+// B200FFT_FAULT=alloc:<n> or launch:<n> makes the n-th device allocation or kernel
+// launch of the process fail on the host with a NativeRuntime error.
+static std::atomic<long> g_alloc_count{0}, g_launch_count{0};
+static bool injected(const char *what, std::atomic<long> &counter) {
+    const char *env = std::getenv("B200FFT_FAULT");
+    long n = ++counter;
+    if (!env) return false;
+    size_t wl = std::strlen(what);
+    if (std::strncmp(env, what, wl) != 0 || env[wl] != ':') return false;
+    return std::atol(env + wl + 1) == n;
+}
+
+static void check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) fail_runtime(std::string(what) + " failed: " + cudaGetErrorString(e));
+}
+
+static void *device_alloc(size_t bytes, const char *what) {
+    if (injected("alloc", g_alloc_count)) fail_runtime(std::string(what) + " failed: injected allocation fault");
+    void *p = nullptr;
+    check(cudaMalloc(&p, std::max<size_t>(bytes, 256)), what);
+    return p;
+}
+
+static std::mutex g_ctx_mu;
+static std::set<Context *> g_contexts;
+
+int probe_devices() {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail_unavailable(cudaGetErrorString(e));
+    }
+    if (n <= 0) fail_unavailable("no CUDA device is present");
+    return n;
+}
+
+static size_t floor_pow2(size_t v) {
+    size_t p = 1;
+    while (p * 2 <= v) p *= 2;
+    return v ? p : 0;
+}
+
+Context *context_create(int device) {
+    int n = probe_devices();
+    if (device < 0 || device >= n) fail_unavailable("CUDA device ordinal " + std::to_string(device) + " is out of range");
+    check(cudaSetDevice(device), "cudaSetDevice");
+    auto *ctx = new Context();
+    ctx->device = device;
+    try {
+        check(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        ctx->d_err = static_cast<int *>(device_alloc(sizeof(int), "error word allocation"));
+        check(cudaMemset(ctx->d_err, 0, sizeof(int)), "cudaMemset");
+        cudaDeviceProp prop;
+        check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        ctx->name = prop.name;
+        ctx->sm_count = prop.multiProcessorCount;
+        // The profile the reference derives from the same attributes
+        // (backend/cuda/runtime.rs:1204-1225).
+        DeviceProfile d = DeviceProfile::generic(Backend::Cuda, Vendor::Nvidia);
+        d.shared_memory_bytes = prop.sharedMemPerBlock;
+        d.shared_memory_pow2_bytes = floor_pow2(prop.sharedMemPerBlock);
+        d.max_threads_per_block = prop.maxThreadsPerBlock;
+        d.max_workgroup_size[0] = prop.maxThreadsDim[0];
+        d.max_workgroup_size[1] = prop.maxThreadsDim[1];
+        d.max_workgroup_size[2] = prop.maxThreadsDim[2];
+        d.coalesced_memory_bytes = 32;
+        d.shared_banks = 32;
+        d.supports_f64 = prop.major > 1 || (prop.major == 1 && prop.minor >= 3);
+        d.subgroup.size = d.subgroup.min_size = d.subgroup.max_size = 32;
+        d.subgroup.compute_supported = d.subgroup.basic_supported = d.subgroup.shuffle_supported = true;
+        d.subgroup.shuffle_relative_supported = d.subgroup.compute_full_subgroups = true;
+        ctx->profile = d;
+        set_kernel_smem_limits();
+    } catch (...) {
+        if (ctx->stream) cudaStreamDestroy(ctx->stream);
+        if (ctx->d_err) cudaFree(ctx->d_err);
+        delete ctx;
+        throw;
+    }
+    std::lock_guard<std::mutex> g(g_ctx_mu);
+    g_contexts.insert(ctx);
+    return ctx;
+}
+
+void context_destroy(Context *ctx) {
+    if (!ctx) return;
+    {
+        std::lock_guard<std::mutex> g(g_ctx_mu);
+        g_contexts.erase(ctx);
+    }
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    for (auto &kv : ctx->tables) cudaFree(kv.second.base);
+    cudaFree(ctx->scratch);
+    cudaFree(ctx->stage_in);
+    cudaFree(ctx->stage_out);
+    cudaFree(ctx->d_err);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+void forget_program(uint64_t id) {
+    std::lock_guard<std::mutex> g(g_ctx_mu);
+    for (Context *ctx : g_contexts) {
+        std::lock_guard<std::mutex> l(ctx->mu);
+        auto it = ctx->tables.find(id);
+        if (it != ctx->tables.end()) {
+            cudaSetDevice(ctx->device);
+            cudaStreamSynchronize(ctx->stream);
+            cudaFree(it->second.base);
+            ctx->tables.erase(it);
+        }
+    }
+}
+
+// Upload (once per context) every table of the program, rounded to the pass precision.
+static DeviceTables &ensure_tables(Context *ctx, uint64_t id, const Program &prog) {
+    auto it = ctx->tables.find(id);
+    if (it != ctx->tables.end()) return it->second;
+    std::vector<size_t> offs;
+    size_t total = 0;
+    for (auto &t : prog.tables) {
+        offs.push_back(total);
+        total += (t.bytes(prog.is_double) + 255) & ~size_t(255);
+    }
+    DeviceTables dt;
+    std::vector<unsigned char> host(std::max<size_t>(total, 256));
+    for (size_t k = 0; k < prog.tables.size(); k++) {
+        const HostTable &t = prog.tables[k];
+        unsigned char *dst = host.data() + offs[k];
+        if (t.is_int) {
+            std::memcpy(dst, t.i.data(), t.i.size() * 4);
+        } else if (prog.is_double) {
+            std::memcpy(dst, t.c.data(), t.c.size() * 16);
+        } else {
+            float *f = reinterpret_cast<float *>(dst);
+            for (size_t m = 0; m < t.c.size(); m++) {
+                f[2 * m] = (float)t.c[m].real();
+                f[2 * m + 1] = (float)t.c[m].imag();
+            }
+        }
+    }
+    dt.base = device_alloc(host.size(), "table upload allocation");
+    cudaError_t e = cudaMemcpy(dt.base, host.data(), host.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(dt.base);
+        check(e, "table upload");
+    }
+    for (size_t k = 0; k < prog.tables.size(); k++)
+        dt.ptrs.push_back(static_cast<unsigned char *>(dt.base) + offs[k]);
+    return ctx->tables.emplace(id, std::move(dt)).first->second;
+}
+
+static void *ensure_buffer(void *&buf, size_t &have, size_t need, const char *what) {
+    if (need > have) {
+        cudaFree(buf);
+        buf = nullptr;
+        have = 0;
+        buf = device_alloc(need, what);
+        have = need;
+    }
+    return buf;
+}
+
+void execute_program(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out, void *workspace,
+                     cudaStream_t stream) {
+    check(cudaSetDevice(ctx->device), "cudaSetDevice");
+    std::lock_guard<std::mutex> l(ctx->mu);
+    if (!stream) stream = ctx->stream;
+    DeviceTables &dt = ensure_tables(ctx, id, prog);
+    const size_t esz = prog.is_double ? 16 : 8;
+    unsigned char *scr = static_cast<unsigned char *>(workspace);
+    if (!scr && prog.scratch_bytes() > 0)
+        scr = static_cast<unsigned char *>(
+            ensure_buffer(ctx->scratch, ctx->scratch_bytes, prog.scratch_bytes(), "scratch allocation"));
+    void *bufs[2 + kScratchBuffers] = {const_cast<void *>(in), out};
+    for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scr ? scr + prog.scratch_offset(k) : nullptr;
+    const int variant = kernel_variant_for(prog.is_double);
+    for (const PassPlan &pp : prog.passes) {
+        PassParams p = pp.p;
+        for (int k = 0; k < p.nops; k++) {
+            const void **slots[3] = {&p.ops[k].lut, &p.ops[k].lut2, &p.ops[k].lut3};
+            for (int s = 0; s < 3; s++) *slots[s] = pp.op_tables[k][s] >= 0 ? dt.ptrs[pp.op_tables[k][s]] : nullptr;
+        }
+        const size_t in_sz = p.in.real ? esz / 2 : esz, out_sz = p.out.real ? esz / 2 : esz;
+        p.src = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * in_sz;
+        p.dst = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * out_sz;
+        p.err = ctx->d_err;
+        if (injected("launch", g_launch_count)) fail_runtime("kernel launch failed: injected launch fault");
+        check(launch_pass(variant, p, pp.grid, pp.threads, pp.smem, stream), "kernel launch");
+    }
+}
+
+void execute_program_host(Context *ctx, uint64_t id, const Program &prog, const void *in, size_t in_bytes, void *out,
+                          size_t out_bytes) {
+    const size_t esz = prog.is_double ? 16 : 8;
+    const size_t in_need = prog.input_elems * (prog.input_real ? esz / 2 : esz);
+    const size_t out_need = prog.output_elems * (prog.output_real ? esz / 2 : esz);
+    if (in_bytes != in_need) fail_input_length(prog.input_elems, in_bytes / (prog.input_real ? esz / 2 : esz));
+    if (out_bytes != out_need) fail_input_length(prog.output_elems, out_bytes / (prog.output_real ? esz / 2 : esz));
+    check(cudaSetDevice(ctx->device), "cudaSetDevice");
+    void *din, *dout;
+    {
+        std::lock_guard<std::mutex> l(ctx->mu);
+        din = ensure_buffer(ctx->stage_in, ctx->stage_in_bytes, in_need, "input staging allocation");
+        dout = ensure_buffer(ctx->stage_out, ctx->stage_out_bytes, out_need, "output staging allocation");
+        check(cudaMemcpyAsync(din, in, in_need, cudaMemcpyHostToDevice, ctx->stream), "input upload");
+    }
+    execute_program(ctx, id, prog, din, dout, nullptr, ctx->stream);
+    check(cudaMemcpyAsync(out, dout, out_need, cudaMemcpyDeviceToHost, ctx->stream), "output download");
+    int err = 0;
+    check(cudaMemcpyAsync(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream), "error word read");
+    check(cudaStreamSynchronize(ctx->stream), "stream synchronize");
+    if (err) {
+        cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream);
+        cudaStreamSynchronize(ctx->stream);
+        fail_runtime("B200 FFT kernel reported error word " + std::to_string(err));
+    }
+}
+
+}  // namespace b200fft

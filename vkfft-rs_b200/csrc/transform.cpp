@@ -1,0 +1,203 @@
+// TransformIr::build analogue (application.rs:47-167): resolve device tuning, run the
+// device-scored planner, build the per-axis child plans exactly as the reference's IR
+// builders do (nd_ir.rs:676-708, real_ir.rs:282-345, nd_real_ir.rs:88-225) and lower the
+// executed plans to the B200 launch program.
+#include <atomic>
+#include <cstring>
+
+#include "transform.hpp"
+
+namespace b200fft {
+
+static std::atomic<uint64_t> g_next_id{1};
+
+const char *precision_name(Precision p) {
+    switch (p) {
+        case Precision::F16StorageF32Compute: return "f16-storage/f32-compute";
+        case Precision::F32: return "f32";
+        case Precision::F64: return "f64";
+        case Precision::F64ComputeF32Storage: return "f64-compute/f32-storage";
+        case Precision::DoubleDouble: return "double-double";
+        case Precision::DoubleDoubleF64Storage: return "double-double/f64-storage";
+    }
+    return "unknown";
+}
+
+static size_t product(const std::vector<size_t> &v, size_t from, size_t to) {
+    size_t acc = 1;
+    for (size_t i = from; i < to; i++) acc = checked_mul(acc, v[i], "tensor element count");
+    return acc;
+}
+
+static void check_executable(const FftConfig &c) {
+    if (!(c.precision == Precision::F32 || c.precision == Precision::F64))
+        fail_precision("B200 engine", precision_name(c.precision));
+    if (!(c.transform == TransformKind::C2C || c.transform == TransformKind::R2C || c.transform == TransformKind::C2R))
+        fail_unsupported("B200 engine executes C2C, R2C and C2R transforms (R2R is outside the FFT hot path)");
+    for (auto &z : c.zero_padding)
+        if (z) fail_unsupported("B200 engine: zero padding is not implemented yet");
+    if (c.has_formatted_strides()) fail_unsupported("B200 engine: formatted buffer strides are not implemented yet");
+    if (c.kernel_convolution) fail_unsupported("B200 engine: kernelConvolution preparation is not implemented yet");
+}
+
+std::unique_ptr<Transform> build_transform(const FftConfig &config_in, int direction, const DeviceProfile &device) {
+    if (config_in.transform == TransformKind::R2C && direction != B200FFT_FORWARD)
+        fail_unsupported("RealToComplex is a forward transform; use Direction::Forward");
+    if (config_in.transform == TransformKind::C2R && direction != B200FFT_INVERSE)
+        fail_unsupported("ComplexToReal is an inverse transform; use Direction::Inverse");
+    auto t = std::make_unique<Transform>();
+    t->id = g_next_id++;
+    t->direction = direction;
+    t->device = device;
+    t->config = config_in.resolve_tuning_for_device(device);
+    t->plan = FftPlan::build_for_device(t->config, device);
+    const FftConfig &c = t->plan.config;
+    check_executable(c);
+    const bool inverse = direction == B200FFT_INVERSE;
+    const size_t rank = c.dimensions.size();
+    const size_t batch = c.kernel_preparation_system_count();
+    t->children.assign(rank, std::nullopt);
+    Program &prog = t->prog;
+    prog.is_double = c.precision == Precision::F64;
+
+    if (c.transform == TransformKind::C2C) {
+        const size_t tensor = product(c.dimensions, 0, rank);
+        prog.input_elems = prog.output_elems = checked_mul(tensor, batch, "transform element count");
+        if (rank == 1) {
+            t->family = B200FFT_FAMILY_COMPLEX_1D;
+            t->children[0] = t->plan;
+            const size_t n = c.dimensions[0];
+            AxisJob job;
+            job.N = n;
+            job.alg = &t->children[0]->axes[0].algorithm;
+            job.no = (int64_t)batch;
+            job.S = 1;
+            job.inverse = inverse;
+            job.scale = (inverse && c.normalize_inverse) ? 1.0 / (double)n : 1.0;
+            job.in_os = job.out_os = (int64_t)n;
+            lower_c2c_axis(prog, job);
+            return t;
+        }
+        t->family = B200FFT_FAMILY_COMPLEX_ND;
+        bool first = true;
+        for (size_t a = rank; a-- > 0;) {
+            if (c.axis_is_omitted(a)) continue;
+            const size_t len = c.dimensions[a];
+            const size_t inner = product(c.dimensions, a + 1, rank);
+            const size_t lines = tensor / len;
+            FftConfig ac = FftConfig::make({len});
+            ac.batch_count = checked_mul(batch, lines, "multidimensional recursive transform batch count");
+            ac.precision = c.precision;
+            ac.normalize_inverse = c.normalize_inverse;
+            ac.bandwidth_boost = c.bandwidth_boost;
+            ac.with_tuning(c.tuning);
+            if (auto gb = c.grouped_batch_for_axis(a)) ac.grouped_batch[0] = gb;
+            t->children[a] = FftPlan::build_c2c_child_for_device(ac, device,
+                                                                 inner == 1 ? AxisClass::Contiguous : AxisClass::Strided);
+            AxisJob job;
+            job.N = len;
+            job.alg = &t->children[a]->axes[0].algorithm;
+            job.no = (int64_t)(batch * product(c.dimensions, 0, a));
+            job.S = (int64_t)inner;
+            job.inverse = inverse;
+            job.scale = (inverse && c.normalize_inverse) ? 1.0 / (double)len : 1.0;
+            job.in_buf = first ? BUF_IN : BUF_OUT;
+            job.out_buf = BUF_OUT;
+            job.in_os = job.out_os = (int64_t)(len * inner);
+            lower_c2c_axis(prog, job);
+            first = false;
+        }
+        return t;
+    }
+
+    // Real transforms
+    const bool r2c = c.transform == TransformKind::R2C;
+    const size_t n = c.dimensions[rank - 1];
+    const size_t half = n / 2 + 1;
+    const size_t outer = product(c.dimensions, 0, rank - 1);
+    const size_t lines = checked_mul(batch, outer, "multidimensional real FFT last-axis batch count");
+    // The real axis child: RealFftIr::build_for_device_plan / build_with_shape_policy
+    // (real_ir.rs:282-345); the ND builder plans it portably first (nd_real_ir.rs:118-131).
+    t->real_algorithm = real_fft_algorithm_for_device(n, lines, c.precision, c.tuning, device);
+    t->real_transform_len = t->real_algorithm == RealAlgorithm::FullComplex ? n : n / 2;
+    {
+        FftConfig rc = FftConfig::make({t->real_transform_len});
+        rc.batch_count = lines;
+        rc.precision = c.precision;
+        rc.normalize_inverse = !r2c && c.normalize_inverse;
+        rc.bandwidth_boost = c.bandwidth_boost;
+        rc.with_tuning(c.tuning);
+        t->children[rank - 1] = FftPlan::build_c2c_child_for_device(rc, device, AxisClass::Contiguous);
+    }
+    const size_t full_tensor = checked_mul(outer * n, batch, "real tensor element count");
+    const size_t compact_tensor = checked_mul(outer * half, batch, "compact tensor element count");
+    prog.input_real = r2c;
+    prog.output_real = !r2c;
+    prog.input_elems = r2c ? full_tensor : compact_tensor;
+    prog.output_elems = r2c ? compact_tensor : full_tensor;
+    std::vector<size_t> compact = c.dimensions;
+    compact[rank - 1] = half;
+    RealAxisJob rj;
+    rj.N = n;
+    rj.lines = (int64_t)lines;
+    rj.normalize = !r2c && c.normalize_inverse;
+    rj.full_complex = t->real_algorithm == RealAlgorithm::FullComplex;
+    rj.alg = &t->children[rank - 1]->axes[0].algorithm;
+
+    t->family = rank == 1 ? B200FFT_FAMILY_REAL : B200FFT_FAMILY_REAL_ND;
+    // complex axes on the compact tensor (always strided: the real axis is the last one)
+    std::vector<size_t> caxes;
+    for (size_t a = rank - 1; a-- > 0;)
+        if (!c.axis_is_omitted(a)) caxes.push_back(a);
+    for (size_t a : caxes) {
+        const size_t len = compact[a];
+        const size_t inner = product(compact, a + 1, rank);
+        const size_t clines = product(compact, 0, rank) / len;
+        FftConfig ac = FftConfig::make({len});
+        ac.batch_count = checked_mul(batch, clines, "multidimensional real FFT complex-axis batch count");
+        ac.precision = c.precision;
+        ac.normalize_inverse = !r2c && c.normalize_inverse;
+        ac.bandwidth_boost = c.bandwidth_boost;
+        ac.with_tuning(c.tuning);
+        t->children[a] = FftPlan::build_c2c_child_for_device(ac, device, AxisClass::Strided);
+    }
+    auto complex_axis = [&](size_t a, int in_buf, int out_buf) {
+        const size_t len = compact[a];
+        const size_t inner = product(compact, a + 1, rank);
+        AxisJob job;
+        job.N = len;
+        job.alg = &t->children[a]->axes[0].algorithm;
+        job.no = (int64_t)(batch * product(compact, 0, a));
+        job.S = (int64_t)inner;
+        job.inverse = !r2c;
+        job.scale = (!r2c && c.normalize_inverse) ? 1.0 / (double)len : 1.0;
+        job.in_buf = in_buf;
+        job.out_buf = out_buf;
+        job.in_os = job.out_os = (int64_t)(len * inner);
+        lower_c2c_axis(prog, job);
+    };
+    if (r2c) {
+        rj.in_buf = BUF_IN;
+        rj.out_buf = BUF_OUT;
+        lower_r2c_axis(prog, rj);
+        for (size_t a : caxes) complex_axis(a, BUF_OUT, BUF_OUT);
+    } else {
+        if (caxes.empty()) {
+            rj.in_buf = BUF_IN;
+        } else {
+            // inverse complex axes on a scratch copy of the compact input (copy semantics)
+            prog.scratch_elems[1] = compact_tensor;
+            bool first = true;
+            for (size_t k = caxes.size(); k-- > 0;) {
+                complex_axis(caxes[k], first ? BUF_IN : BUF_SCRATCH1, BUF_SCRATCH1);
+                first = false;
+            }
+            rj.in_buf = BUF_SCRATCH1;
+        }
+        rj.out_buf = BUF_OUT;
+        lower_c2r_axis(prog, rj);
+    }
+    return t;
+}
+
+}  // namespace b200fft
