@@ -472,7 +472,11 @@ class PassBuilder {
         plan_.dst_off = dst_off;
         plan_.grid = (p.nlines + sh_.G - 1) / sh_.G;
         plan_.threads = sh_.threads;
-        plan_.smem = sh_.smem;
+        // shared memory = data regions + per-line metadata + the op program actually emitted
+        size_t meta = (size_t)sh_.G * 16 + (size_t)((sh_.G + 3) & ~3) * 4;
+        meta = (meta + 15) & ~size_t(15);
+        plan_.smem = sh_.meta_off + meta + (size_t)nops_ * sizeof(Op);
+        if (plan_.smem > 232448) fail_resource("B200 FFT pass shared memory", plan_.smem, 232448);
         plan_.label = label;
         return plan_;
     }
