@@ -1,0 +1,123 @@
+// CPU emulation of the B200 pass kernel -- TEST INFRASTRUCTURE ONLY.
+//
+// Builds the product's planner and lowering (the same sources as libb200fft.so) and
+// runs every pass of a transform's launch program on host memory: for each CTA the
+// prologue and then each op are executed for every thread in turn.  This is valid
+// because the kernel's threads only communicate through shared memory across the
+// __syncthreads() that separates ops.  Compiled with AddressSanitizer by the tests so
+// any out-of-bounds global or shared-memory index in the lowering or the kernel is a
+// CPU test failure.  Shared memory is filled with NaN bytes before every CTA so reads
+// of unwritten slots poison the result.  Never linked into the product library.
+#define B200FFT_EMULATE 1
+#include "emu_shim.hpp"
+
+EmuDim threadIdx, blockIdx, blockDim;
+
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../vkfft-rs_b200/csrc/kernels.cu"
+#include "../../vkfft-rs_b200/csrc/transform.hpp"
+
+using namespace b200fft;
+
+template <typename T>
+static void emu_launch(const PassParams &p, int64_t grid, int threads, size_t smem) {
+    std::vector<unsigned char> buf(smem + 16);
+    unsigned char *sm_raw = buf.data() + ((16 - ((uintptr_t)buf.data() & 15)) & 15);
+    blockDim.x = threads;
+    for (int64_t b = 0; b < grid; b++) {
+        std::memset(buf.data(), 0xff, buf.size());
+        blockIdx.x = (unsigned)b;
+        Op *s_ops = nullptr;
+        LineMeta lm{};
+        for (int t = 0; t < threads; t++) {
+            threadIdx.x = t;
+            lm = pass_prologue<T>(p, sm_raw, &s_ops);
+        }
+        for (int k = 0; k < p.nops; k++) {
+            Op op = s_ops[k];
+            for (int t = 0; t < threads; t++) {
+                threadIdx.x = t;
+                run_op<T>(p, op, reinterpret_cast<cplx<T> *>(sm_raw), lm);
+            }
+        }
+    }
+}
+
+static void run_program(const Program &prog, const void *in, void *out) {
+    const size_t esz = prog.is_double ? 16 : 8;
+    std::vector<std::vector<unsigned char>> tables;
+    for (const HostTable &t : prog.tables) {
+        std::vector<unsigned char> v(t.bytes(prog.is_double));
+        if (t.is_int) {
+            std::memcpy(v.data(), t.i.data(), v.size());
+        } else if (prog.is_double) {
+            std::memcpy(v.data(), t.c.data(), v.size());
+        } else {
+            float *f = reinterpret_cast<float *>(v.data());
+            for (size_t m = 0; m < t.c.size(); m++) {
+                f[2 * m] = (float)t.c[m].real();
+                f[2 * m + 1] = (float)t.c[m].imag();
+            }
+        }
+        tables.push_back(std::move(v));
+    }
+    std::vector<std::vector<unsigned char>> scratch(kScratchBuffers);
+    for (int k = 0; k < kScratchBuffers; k++) scratch[k].assign(prog.scratch_elems[k] * esz, 0xff);
+    void *bufs[2 + kScratchBuffers] = {const_cast<void *>(in), out};
+    for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scratch[k].empty() ? nullptr : scratch[k].data();
+    int err = 0;
+    for (const PassPlan &pp : prog.passes) {
+        PassParams p = pp.p;
+        for (int k = 0; k < p.nops; k++) {
+            const void **slots[3] = {&p.ops[k].lut, &p.ops[k].lut2, &p.ops[k].lut3};
+            for (int s = 0; s < 3; s++)
+                *slots[s] = pp.op_tables[k][s] >= 0 ? tables[pp.op_tables[k][s]].data() : nullptr;
+        }
+        const size_t in_sz = p.in.real ? esz / 2 : esz, out_sz = p.out.real ? esz / 2 : esz;
+        p.src = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * in_sz;
+        p.dst = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * out_sz;
+        p.err = &err;
+        if (pp.threads > 1024 || pp.smem > 232448) fail_invalid_ir("pass launch exceeds sm_100 limits");
+        if (prog.is_double)
+            emu_launch<double>(p, pp.grid, pp.threads, pp.smem);
+        else
+            emu_launch<float>(p, pp.grid, pp.threads, pp.smem);
+        if (err) fail_runtime("emulated kernel reported error word " + std::to_string(err));
+    }
+}
+
+extern "C" int b200fft_emu_run(const b200fft_config *cfg, int direction, const b200fft_device_profile *dev,
+                               const void *in, size_t in_bytes, void *out, size_t out_bytes, char *errbuf,
+                               size_t errlen, int *launches) {
+    try {
+        DeviceProfile d;
+        d.backend = static_cast<Backend>(dev->backend);
+        d.vendor = static_cast<Vendor>(dev->vendor);
+        d.shared_memory_bytes = dev->shared_memory_bytes;
+        d.shared_memory_pow2_bytes = dev->shared_memory_pow2_bytes;
+        d.max_threads_per_block = dev->max_threads_per_block;
+        for (int i = 0; i < 3; i++) d.max_workgroup_size[i] = dev->max_workgroup_size[i];
+        d.coalesced_memory_bytes = dev->coalesced_memory_bytes;
+        d.supports_f64 = dev->supports_f64;
+        auto t = build_transform(FftConfig::from_c(*cfg), direction, d);
+        const Program &prog = t->prog;
+        const size_t esz = prog.is_double ? 16 : 8;
+        size_t in_need = prog.input_elems * (prog.input_real ? esz / 2 : esz);
+        size_t out_need = prog.output_elems * (prog.output_real ? esz / 2 : esz);
+        if (in_bytes != in_need || out_bytes != out_need) fail_input_length(in_need, in_bytes);
+        // private copies so AddressSanitizer sees exact-size heap buffers
+        std::vector<unsigned char> din((const unsigned char *)in, (const unsigned char *)in + in_need);
+        std::vector<unsigned char> dout(out_need, 0xff);
+        run_program(prog, din.data(), dout.data());
+        std::memcpy(out, dout.data(), out_need);
+        if (launches) *launches = (int)prog.passes.size();
+        return 0;
+    } catch (const FftError &e) {
+        std::strncpy(errbuf, e.message.c_str(), errlen - 1);
+        errbuf[errlen - 1] = 0;
+        return e.code;
+    }
+}

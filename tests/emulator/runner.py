@@ -1,0 +1,80 @@
+"""Child-process runner of emulated cases (loaded with the ASan runtime preloaded).
+
+stdin: JSON list of cases {"kind": "c2c"|"r2c"|"c2r", "dims": [...], "batch": b,
+"prec": "F32"|"F64", "inverse": bool, "normalize": bool, "tuning": {...}|null,
+"seed": s}.  stdout (last line): JSON list of {"err": relL2 vs oracle, "launches": n}
+or {"error": "<variant>: message"}."""
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, HERE)
+
+import oracle  # noqa: E402
+from __init__ import _load, emulate  # noqa: E402
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, dtype=np.complex128).ravel()
+    b = np.asarray(b, dtype=np.complex128).ravel()
+    d = np.linalg.norm(b)
+    return float(np.linalg.norm(a - b) / (d if d > 0 else 1.0))
+
+
+def b200_profile(V):
+    return V.DeviceProfile.generic(V.Backend.CUDA, V.GpuVendor.NVIDIA).replace(
+        shared_memory_bytes=49152, shared_memory_pow2_bytes=32768, max_threads_per_block=1024,
+        max_workgroup_size=[1024, 1024, 64])
+
+
+def run(case, V, lib):
+    dims, batch, prec = case["dims"], case["batch"], case["prec"]
+    cdt, rdt = (np.complex64, np.float32) if prec == "F32" else (np.complex128, np.float64)
+    dev = b200_profile(V)
+    cfg = V.FftConfig(dims).with_batch_count(batch).with_precision(V.Precision[prec])
+    cfg = cfg.with_inverse_normalization(case.get("normalize", False))
+    if case.get("tuning"):
+        cfg = cfg.with_tuning(V.PlannerTuning(**case["tuning"]))
+    rng = np.random.default_rng(case.get("seed", 0))
+    shape = (batch,) + tuple(dims)
+    kind = case["kind"]
+    if kind == "c2c":
+        x = (rng.uniform(-1, 1, shape) + 1j * rng.uniform(-1, 1, shape)).astype(cdt)
+        d = V.Direction.INVERSE if case.get("inverse") else V.Direction.FORWARD
+        y, n = emulate(V, lib, cfg, d, dev, x, x.size, cdt)
+        ref = oracle.fft_nd(x.astype(np.complex128), len(dims), inverse=case.get("inverse", False),
+                            normalize=case.get("normalize", False), threads=4)
+    elif kind == "r2c":
+        x = rng.uniform(-1, 1, shape).astype(rdt)
+        cfg = cfg.with_transform(V.TransformKind.R2C)
+        ref = oracle.r2c_nd(x.astype(np.float64), len(dims), threads=4)
+        y, n = emulate(V, lib, cfg, V.Direction.FORWARD, dev, x, ref.size, cdt)
+    else:
+        x = rng.uniform(-1, 1, shape)
+        spec = oracle.r2c_nd(x, len(dims), threads=4).astype(cdt)
+        cfg = cfg.with_transform(V.TransformKind.C2R)
+        ref = oracle.c2r_nd(spec.astype(np.complex128), dims[-1], len(dims), normalize=case.get("normalize", False),
+                            threads=4)
+        y, n = emulate(V, lib, cfg, V.Direction.INVERSE, dev, spec, ref.size, rdt)
+    return {"err": rel_l2(y, ref), "launches": n}
+
+
+def main():
+    cases = json.loads(sys.stdin.read())
+    V, lib = _load()
+    out = []
+    for c in cases:
+        try:
+            out.append(run(c, V, lib))
+        except V.VkFftError as e:
+            out.append({"error": f"{e.variant}: {e}"})
+    print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

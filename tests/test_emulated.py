@@ -1,0 +1,52 @@
+"""CPU emulation of the B200 launch programs (tests/emulator): the product's lowering and
+the kernel's op functions executed thread by thread on the host, under AddressSanitizer,
+against the oracle.  Catches lowering and index errors without a GPU; the GPU parity
+suite (test_gpu_parity.py) is the parity claim itself."""
+import pytest
+
+import emulator
+
+pytestmark = pytest.mark.skipif(not emulator.available(), reason="AddressSanitizer runtime not installed")
+
+TOL = {"F32": 2e-6, "F64": 1e-13}
+
+CASES = [
+    dict(kind="c2c", dims=[1024], batch=3, prec="F32"),
+    dict(kind="c2c", dims=[4096], batch=1, prec="F64", inverse=True, normalize=True),
+    dict(kind="c2c", dims=[360], batch=3, prec="F64"),
+    dict(kind="c2c", dims=[11 * 13 * 2], batch=2, prec="F32"),
+    dict(kind="c2c", dims=[17], batch=40, prec="F64"),
+    dict(kind="c2c", dims=[47], batch=9, prec="F64"),
+    dict(kind="c2c", dims=[89], batch=9, prec="F32"),
+    dict(kind="c2c", dims=[17 * 17], batch=2, prec="F64"),
+    dict(kind="c2c", dims=[83 * 4], batch=2, prec="F64", inverse=True, normalize=True),
+    dict(kind="c2c", dims=[4099], batch=1, prec="F32"),
+    dict(kind="c2c", dims=[4099], batch=1, prec="F64"),
+    dict(kind="c2c", dims=[65536 * 2], batch=1, prec="F32"),
+    dict(kind="c2c", dims=[8, 16], batch=2, prec="F64"),
+    dict(kind="c2c", dims=[6, 17, 10], batch=1, prec="F64", inverse=True, normalize=True),
+    dict(kind="c2c", dims=[3, 1, 47], batch=2, prec="F64"),
+    dict(kind="r2c", dims=[4096], batch=2, prec="F32"),
+    dict(kind="r2c", dims=[30], batch=3, prec="F64"),
+    dict(kind="r2c", dims=[45], batch=3, prec="F64"),
+    dict(kind="r2c", dims=[94], batch=3, prec="F64"),
+    dict(kind="r2c", dims=[206], batch=2, prec="F64"),
+    dict(kind="r2c", dims=[17, 34], batch=1, prec="F64"),
+    dict(kind="c2r", dims=[4096], batch=2, prec="F32", normalize=True),
+    dict(kind="c2r", dims=[206], batch=2, prec="F64", normalize=True),
+    dict(kind="c2r", dims=[45], batch=2, prec="F64", normalize=True),
+    dict(kind="c2r", dims=[12, 30], batch=1, prec="F64", normalize=True),
+]
+
+
+@pytest.fixture(scope="module")
+def results():
+    emulator.build()
+    return emulator.run_cases(CASES)
+
+
+@pytest.mark.parametrize("i", range(len(CASES)), ids=[f"{c['kind']}-{c['dims']}-{c['prec']}" for c in CASES])
+def test_emulated_program_matches_oracle(results, i):
+    r = results[i]
+    assert "error" not in r, r
+    assert r["err"] <= TOL[CASES[i]["prec"]], (CASES[i], r)

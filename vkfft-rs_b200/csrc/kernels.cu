@@ -16,7 +16,9 @@
 // program sets the conjugation flags), so every table holds forward roots only.
 // Faults are never raised on the device: an unknown op or radix sets the pass's
 // error word and is skipped uniformly by the whole CTA.
+#ifndef B200FFT_EMULATE
 #include <cuda_runtime.h>
+#endif
 
 #include <cstdint>
 
@@ -397,15 +399,14 @@ __device__ __forceinline__ void op_herm_expand(const PassParams &p, const Op &op
     }
 }
 
-template <typename T, int MAXT>
-__global__ void __launch_bounds__(MAXT) fft_pass_kernel(const __grid_constant__ PassParams p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    cplx<T> *sm = reinterpret_cast<cplx<T> *>(smem_raw);
+// Per-thread prologue: copy the op program into shared memory (after the line
+// metadata, so the dynamic op index below reads shared memory rather than the
+// parameter block) and resolve every line's global base addresses.
+template <typename T>
+__device__ __forceinline__ LineMeta pass_prologue(const PassParams &p, unsigned char *smem_raw, Op **ops_out) {
     int64_t *ib = reinterpret_cast<int64_t *>(smem_raw + p.meta_off);
     int64_t *ob = ib + p.G;
     int *col = reinterpret_cast<int *>(ob + p.G);
-    // The op program is copied once into shared memory (after the line metadata) so the
-    // dynamic op index below reads shared memory rather than the parameter block.
     Op *s_ops = reinterpret_cast<Op *>(col + ((p.G + 3) & ~3));
     {
         const int words = p.nops * (int)(sizeof(Op) / sizeof(int4));
@@ -427,21 +428,37 @@ __global__ void __launch_bounds__(MAXT) fft_pass_kernel(const __grid_constant__ 
         ob[g] = o * p.out.os + i * p.out.is + c * p.out.cs;
         col[g] = (int)c;
     }
+    *ops_out = s_ops;
+    return lm;
+}
+
+// One op of the program, this thread's share (threads synchronise between ops).
+template <typename T>
+__device__ __forceinline__ void run_op(const PassParams &p, const Op &op, cplx<T> *sm, const LineMeta &lm) {
+    switch (op.type) {
+        case OP_LOAD: op_load<T>(p, op, sm, lm); break;
+        case OP_STORE: op_store<T>(p, op, sm, lm); break;
+        case OP_STAGE: op_stage_dispatch<T>(op, sm, p.err); break;
+        case OP_MUL: op_mul<T>(op, sm, lm); break;
+        case OP_R2C_POST: op_r2c_post<T>(p, op, sm); break;
+        case OP_C2R_PRE: op_c2r_pre<T>(p, op, sm); break;
+        case OP_RADER_GATHER: op_rader_gather<T>(op, sm); break;
+        case OP_RADER_SCATTER: op_rader_scatter<T>(op, sm); break;
+        case OP_HERM_EXPAND: op_herm_expand<T>(p, op, sm); break;
+        default: raise_error(p.err, 4); break;
+    }
+}
+
+#ifndef B200FFT_EMULATE
+template <typename T, int MAXT>
+__global__ void __launch_bounds__(MAXT) fft_pass_kernel(const __grid_constant__ PassParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    cplx<T> *sm = reinterpret_cast<cplx<T> *>(smem_raw);
+    Op *s_ops;
+    const LineMeta lm = pass_prologue<T>(p, smem_raw, &s_ops);
     __syncthreads();
     for (int k = 0; k < p.nops; k++) {
-        const Op &op = s_ops[k];
-        switch (op.type) {
-            case OP_LOAD: op_load<T>(p, op, sm, lm); break;
-            case OP_STORE: op_store<T>(p, op, sm, lm); break;
-            case OP_STAGE: op_stage_dispatch<T>(op, sm, p.err); break;
-            case OP_MUL: op_mul<T>(op, sm, lm); break;
-            case OP_R2C_POST: op_r2c_post<T>(p, op, sm); break;
-            case OP_C2R_PRE: op_c2r_pre<T>(p, op, sm); break;
-            case OP_RADER_GATHER: op_rader_gather<T>(op, sm); break;
-            case OP_RADER_SCATTER: op_rader_scatter<T>(op, sm); break;
-            case OP_HERM_EXPAND: op_herm_expand<T>(p, op, sm); break;
-            default: raise_error(p.err, 4); break;
-        }
+        run_op<T>(p, s_ops[k], sm, lm);
         __syncthreads();
     }
 }
@@ -482,5 +499,7 @@ cudaError_t launch_pass(int variant, const PassParams &p, int64_t grid, int thre
     void *args[] = {const_cast<PassParams *>(&p)};
     return cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(threads), args, smem, stream);
 }
+
+#endif  // B200FFT_EMULATE
 
 }  // namespace b200fft

@@ -677,7 +677,8 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     if (line_fits_on_chip(prog.is_double, M, nullptr, strided)) {
         PassBuilder b(prog, (int)M, line_stages(M, nullptr), strided, no * S, 24);
         if (job.in_herm) {
-            b.load(in_len, cin);
+            // load the N/2+1 bins and zero-fill the rest of the M-length line, then expand
+            b.load((int)M, cin);
             b.herm_expand((int)N);
             b.mul_region(chirp, 0, 0, 1, (int)N);
         } else {

@@ -700,10 +700,15 @@ class CudaExecutionContext:
         _check(library().b200fft_context_device_name(self._h, buf, 256))
         return buf.value.decode()
 
-    def execute_transform(self, ir, data):
-        """execute_transform_f32/f64 (native_runtime.rs:339-359): host array in, new array out."""
+    def execute_transform(self, ir, data, out=None):
+        """execute_transform_f32/f64 (native_runtime.rs:339-359): host array in, new array out.
+        `out` optionally supplies the (e.g. pinned) destination array."""
         x = np.ascontiguousarray(data, dtype=ir.input_dtype())
-        out = np.empty(ir.output_elements, dtype=ir.output_dtype())
+        if out is None:
+            out = np.empty(ir.output_elements, dtype=ir.output_dtype())
+        elif out.dtype != ir.output_dtype() or out.size != ir.output_elements or not out.flags.c_contiguous:
+            raise VkFftError(Status.InputLengthMismatch,
+                             f"input contains {out.size} complex elements but kernel expects {ir.output_elements}")
         _check(library().b200fft_execute_host(self._h, ir._h, x.ctypes.data, x.nbytes,
                                               out.ctypes.data, out.nbytes))
         return out
