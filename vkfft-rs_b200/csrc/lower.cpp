@@ -8,6 +8,7 @@
 // reference's own f64 expression) and rounded to f32 for f32 passes.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "lower.hpp"
@@ -597,6 +598,17 @@ static bool four_step_split(size_t N, size_t &N1, size_t &N2) {
     return true;
 }
 
+// The register kernels are not part of the CPU emulation build (their threads
+// exchange data inside one op); B200FFT_DISABLE_REG=1 forces the generic pass kernel.
+static bool reg_kernels_enabled() {
+#ifdef B200FFT_EMULATE
+    return false;
+#else
+    const char *e = std::getenv("B200FFT_DISABLE_REG");
+    return !(e && e[0] == '1');
+#endif
+}
+
 void lower_c2c_axis(Program &prog, const AxisJob &job) {
     const bool inv = job.inverse;
     const size_t N = job.N;
@@ -621,6 +633,33 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
                                        make_side(job.out_os, 1, 0, S, job.out_real, 1, 0, 1), job.in_buf, job.in_off,
                                        job.out_buf, job.out_off, "copy"));
         return;
+    }
+
+    // Fast path: contiguous power-of-two Stockham lines run in the register-resident
+    // kernel (one global read and write, two shared-memory exchanges).
+    if (alg->kind == AlgorithmKind::Stockham && !strided && !job.in_real && !job.in_herm && !job.out_real &&
+        out_count == N && is_pow2(N) && reg_kernels_enabled()) {
+        const int rv = reg_variant_for(prog.is_double, N);
+        if (rv >= 0) {
+            PassPlan pp{};
+            pp.kernel = KERNEL_REG;
+            pp.reg_variant = rv;
+            pp.reg_table = table_twiddle(prog, N);
+            pp.rp.nlines = no;
+            pp.rp.in_stride = job.in_os;
+            pp.rp.out_stride = job.out_os;
+            pp.rp.scale = scale;
+            pp.rp.conj = inv ? 1 : 0;
+            pp.rp.n = (int32_t)N;
+            pp.src_buf = job.in_buf;
+            pp.src_off = job.in_off;
+            pp.dst_buf = job.out_buf;
+            pp.dst_off = job.out_off;
+            pp.label = "register stockham";
+            for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
+            prog.passes.push_back(pp);
+            return;
+        }
     }
 
     if (alg->kind != AlgorithmKind::Bluestein) {

@@ -11,6 +11,7 @@
 
 #include "core.hpp"
 #include "pass_desc.hpp"
+#include "reg_kernels.hpp"
 
 namespace b200fft {
 
@@ -24,7 +25,13 @@ struct HostTable {
     size_t bytes(bool dbl) const { return is_int ? i.size() * 4 : c.size() * (dbl ? 16 : 8); }
 };
 
+enum KernelKind : int { KERNEL_PASS = 0, KERNEL_REG = 1 };
+
 struct PassPlan {
+    int kernel = KERNEL_PASS;     // KERNEL_REG: register-resident Stockham (reg_kernels.cu)
+    RegParams rp{};               // KERNEL_REG parameters (pointers patched at launch)
+    int reg_variant = -1;
+    int reg_table = -1;           // twiddle table id of a KERNEL_REG pass
     PassParams p{};               // device pointers are patched at upload / launch
     int op_tables[kMaxOps][3];    // table ids per op (lut, lut2, lut3) or -1
     int src_buf = BUF_IN, dst_buf = BUF_OUT;

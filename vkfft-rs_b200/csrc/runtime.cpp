@@ -12,6 +12,8 @@ namespace b200fft {
 int kernel_variant_for(bool is_double);
 cudaError_t launch_pass(int variant, const PassParams &p, int64_t grid, int threads, size_t smem, cudaStream_t stream);
 void set_kernel_smem_limits();
+void set_reg_kernel_smem_limits();
+cudaError_t launch_reg(int variant, const RegParams &rp, cudaStream_t stream);
 
 // ---- host-side fault injection (no GPU fault is ever provoked) ------------------
 // B200FFT_FAULT=alloc:<n> or launch:<n> makes the n-th device allocation or kernel
@@ -88,6 +90,7 @@ Context *context_create(int device) {
         d.subgroup.shuffle_relative_supported = d.subgroup.compute_full_subgroups = true;
         ctx->profile = d;
         set_kernel_smem_limits();
+        set_reg_kernel_smem_limits();
     } catch (...) {
         if (ctx->stream) cudaStreamDestroy(ctx->stream);
         if (ctx->d_err) cudaFree(ctx->d_err);
@@ -194,6 +197,15 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scr ? scr + prog.scratch_offset(k) : nullptr;
     const int variant = kernel_variant_for(prog.is_double);
     for (const PassPlan &pp : prog.passes) {
+        if (pp.kernel == KERNEL_REG) {
+            RegParams rp = pp.rp;
+            rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * esz;
+            rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * esz;
+            rp.tw = dt.ptrs[pp.reg_table];
+            if (injected("launch", g_launch_count)) fail_runtime("kernel launch failed: injected launch fault");
+            check(launch_reg(pp.reg_variant, rp, stream), "kernel launch");
+            continue;
+        }
         PassParams p = pp.p;
         for (int k = 0; k < p.nops; k++) {
             const void **slots[3] = {&p.ops[k].lut, &p.ops[k].lut2, &p.ops[k].lut3};
