@@ -216,30 +216,33 @@ def run_ours(args):
     total_transforms = 2 * BATCH * ws
     value = total_transforms * FLOP_PER_TRANSFORM / (ms_per_step * 1e-3) / 1e9
 
+    if args.skip_e2e:
+        e2e_value = None
     # e2e through the host API with pinned host arrays
     def pinned():
         t = torch.empty((BATCH * N * 2,), dtype=torch.float32, pin_memory=True)
         return t, t.numpy().view(np.complex64)
 
-    host_in_t, x_host = pinned()
-    host_spec_t, spec = pinned()
-    host_back_t, back = pinned()
-    host_in_t.copy_(a.reshape(-1).cpu())
-    e2e_steps = max(1, min(args.steps, 3))
-    ctx.execute_transform(fwd, x_host, out=spec)  # warm the staging buffers
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        ctx.execute_transform(fwd, x_host, out=spec)
-        ctx.execute_transform(inv, spec, out=back)
-    e2e_s = (time.perf_counter() - t0) / e2e_steps
-    if dist:
-        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t[0])
-    e2e_value = total_transforms * FLOP_PER_TRANSFORM / e2e_s / 1e9
+    if not args.skip_e2e:
+        host_in_t, x_host = pinned()
+        host_spec_t, spec = pinned()
+        host_back_t, back = pinned()
+        host_in_t.copy_(a.reshape(-1).cpu())
+        e2e_steps = max(1, min(args.steps, 3))
+        ctx.execute_transform(fwd, x_host, out=spec)  # warm the staging buffers
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            ctx.execute_transform(fwd, x_host, out=spec)
+            ctx.execute_transform(inv, spec, out=back)
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+        if dist:
+            t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t[0])
+        e2e_value = total_transforms * FLOP_PER_TRANSFORM / e2e_s / 1e9
     bytes_one = BATCH * N * 8
 
     peak, peak_kind = load_peaks()
@@ -255,14 +258,14 @@ def run_ours(args):
                    "l2": "inputs (2 GiB per rank) larger than L2; no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": peak_kind,
-                     "kernel": "fft_pass_kernel<float> (forward, one launch per transform direction)"},
-        "e2e": {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": 2 * bytes_one,
+                     "kernel": "reg_fft_kernel<float,4096> (register-resident Stockham, one launch per transform direction)"},
+        "e2e": None if e2e_value is None else {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": 2 * bytes_one,
                 "d2h_bytes_per_step": 2 * bytes_one, "path": "execute_transform (host arrays, pinned)"},
         "gpu_launches": args.steps * (fwd.launch_count + inv.launch_count),
         "clocks": clk.summary(),
     }
     if rank == 0:
-        line["cpu_baseline"] = cpu_baseline(1, budget_s=12.0) if ws == 1 else None
+        line["cpu_baseline"] = cpu_baseline(1, budget_s=12.0) if (ws == 1 and not args.skip_cpu) else None
         print(json.dumps(line))
     if dist:
         dist.barrier()
@@ -277,7 +280,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=BATCH, help="transforms per rank (profiling runs use fewer)")
+    ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: resident timing only")
+    ap.add_argument("--skip-cpu", action="store_true", help="profiling runs: no CPU baseline")
     args = ap.parse_args()
+    global BATCH
+    BATCH = args.batch
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
