@@ -275,6 +275,7 @@ def run_ours(args):
 
 
 def main():
+    global BATCH
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -284,7 +285,6 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: resident timing only")
     ap.add_argument("--skip-cpu", action="store_true", help="profiling runs: no CPU baseline")
     args = ap.parse_args()
-    global BATCH
     BATCH = args.batch
     if args.impl == "reference":
         return run_reference(args)
