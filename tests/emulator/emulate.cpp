@@ -127,3 +127,6 @@ extern "C" int b200fft_emu_run(const b200fft_config *cfg, int direction, const b
 namespace b200fft {
 int reg_variant_for(bool, size_t) { return -1; }
 }  // namespace b200fft
+namespace b200fft {
+int reg_variant_radices(int, int *) { return 0; }
+}  // namespace b200fft

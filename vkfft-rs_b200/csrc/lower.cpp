@@ -53,6 +53,28 @@ int table_twiddle(Program &prog, size_t n) {
     return add_table(prog, key, std::move(t));
 }
 
+// Stage twiddles of a register-kernel variant: for every stage s > 0 (span P, radix R)
+// a transposed block tw[(q-1)*P + j] = W_{P R}^{j q}, q = 1..R-1, j = 0..P-1, blocks in
+// stage order (reg_kernels.cu reads them at compile-time offsets).
+int table_reg_twiddles(Program &prog, size_t n, int variant) {
+    std::string key = "regtw" + std::to_string(n);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    int rad[8];
+    const int ns = reg_variant_radices(variant, rad);
+    HostTable t;
+    size_t P = 1;
+    for (int s = 0; s < ns; s++) {
+        const size_t R = (size_t)rad[s];
+        if (P > 1)
+            for (size_t q = 1; q < R; q++)
+                for (size_t j = 0; j < P; j++) t.c.push_back(root(j * q, P * R));
+        P *= R;
+    }
+    if (t.c.empty()) t.c.push_back({1.0, 0.0});
+    return add_table(prog, key, std::move(t));
+}
+
 // Bluestein chirp exactly as the reference evaluates it (reference.rs:121-125,
 // lut.rs:295-299): angle = sign * PI * (i as f64) * (i as f64) / (n as f64), not
 // reduced modulo 2n, then libm cos / sin.  Forward sign (-1); inverse transforms
@@ -644,7 +666,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
             PassPlan pp{};
             pp.kernel = KERNEL_REG;
             pp.reg_variant = rv;
-            pp.reg_table = table_twiddle(prog, N);
+            pp.reg_table = table_reg_twiddles(prog, N, rv);
             pp.rp.nlines = no;
             pp.rp.in_stride = job.in_os;
             pp.rp.out_stride = job.out_os;

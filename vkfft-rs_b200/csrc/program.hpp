@@ -64,6 +64,7 @@ FastDiv make_fastdiv(uint32_t d);
 
 // Tables (host f64).  All roots are forward: W_N^m = exp(-2 pi i m / N).
 int table_twiddle(Program &prog, size_t n);
+int table_reg_twiddles(Program &prog, size_t n, int variant);
 int table_bluestein_chirp(Program &prog, size_t n);
 int table_bluestein_spectrum(Program &prog, size_t n, size_t m);
 void host_fft_inplace(std::vector<std::complex<double>> &x, bool inverse);

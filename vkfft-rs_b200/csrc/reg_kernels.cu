@@ -8,7 +8,7 @@
 // global memory is read and written once, warp-coalesced (32 consecutive
 // threads touch 32 consecutive complex values), with no shared-memory staging.
 // Only the middle stages exchange through one padded shared-memory buffer.
-// Twiddles W_N^m come from a forward table read through the read-only cache.
+// Twiddles come from per-stage transposed tables read through the read-only cache.
 // Inverse transforms conjugate on load and store (the table stays forward).
 #include <cuda_runtime.h>
 
@@ -40,13 +40,16 @@ struct LineIO {
     bool valid;
 };
 
-// One radix-R stage with span P (product of the radices before it).
-template <typename T, int N, int E, int R, int P, bool FIRST, bool LAST>
+// One radix-R stage with span P (product of the radices before it).  Its twiddles
+// W_{P R}^{j q} are read from the stage's transposed table (row q-1 holds the P values
+// of j, so a warp's loads are contiguous) at offset OFF; only the power-of-two rows
+// are read and w_q = w_{q - lowbit(q)} * w_{lowbit(q)} forms the rest (at most three
+// products deep).
+template <typename T, int N, int E, int R, int P, int OFF, bool FIRST, bool LAST>
 __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, const cplx<T> *tw, const RegParams &rp,
                                       const LineIO &io) {
     constexpr int TT = N / E;
     constexpr int NB = E / R;  // butterflies per thread
-    constexpr int TSTEP = N / (P * R);
     if (!FIRST) {
         __syncthreads();  // previous stage's outputs are visible
 #pragma unroll
@@ -63,8 +66,18 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
         const int b = t + k * TT;
         const int j = b % P;
         if (P > 1) {
+            cplx<T> w[R];
 #pragma unroll
-            for (int q = 1; q < R; q++) x[q] = mul(x[q], tw_load(tw, j * q * TSTEP));
+            for (int q = 1; q < R; q++) {
+                if ((q & (q - 1)) == 0) {
+                    w[q] = tw_load(tw, OFF + (q - 1) * P + j);
+                } else {
+                    const int lb = q & (-q);
+                    w[q] = mul(w[q - lb], w[lb]);
+                }
+            }
+#pragma unroll
+            for (int q = 1; q < R; q++) x[q] = mul(x[q], w[q]);
         }
         dft<R, T>(x);
         if (LAST) {
@@ -88,12 +101,14 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
     }
 }
 
-template <typename T, int N, int E, int P, bool FIRST, int R, int... Rest>
+template <typename T, int N, int E, int P, int OFF, bool FIRST, int R, int... Rest>
 __device__ __forceinline__ void stages(cplx<T> (&v)[E], int t, cplx<T> *sline, const cplx<T> *tw, const RegParams &rp,
                                        const LineIO &io) {
     constexpr bool LAST = sizeof...(Rest) == 0;
-    stage<T, N, E, R, P, FIRST, LAST>(v, t, sline, tw, rp, io);
-    if constexpr (!LAST) stages<T, N, E, P * R, false, Rest...>(v, t, sline, tw, rp, io);
+    stage<T, N, E, R, P, OFF, FIRST, LAST>(v, t, sline, tw, rp, io);
+    // the first stage (P = 1) has no twiddles and no table rows
+    constexpr int NEXT_OFF = OFF + (P > 1 ? (R - 1) * P : 0);
+    if constexpr (!LAST) stages<T, N, E, P * R, NEXT_OFF, false, Rest...>(v, t, sline, tw, rp, io);
 }
 
 template <typename T, int N, int E, int G, int... Rs>
@@ -122,7 +137,7 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
 #pragma unroll
         for (int m = 0; m < E; m++) v[m] = {T(0), T(0)};
     }
-    stages<T, N, E, 1, true, Rs...>(v, t, sline, tw, rp, io);
+    stages<T, N, E, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
 }
 
 }  // namespace regk
@@ -133,11 +148,12 @@ struct RegVariant {
     int is_double, n, threads, g;
     size_t smem;
     const void *fn;
+    int radices[8];
 };
 
 #define RV(T, N, E, G, ...)                                                                                 \
     {sizeof(T) == 8, N, G *(N / E), G, (size_t)G *(N + N / 16 + 1) * sizeof(T) * 2,                       \
-     (const void *)regk::reg_fft_kernel<T, N, E, G, __VA_ARGS__>}
+     (const void *)regk::reg_fft_kernel<T, N, E, G, __VA_ARGS__>, {__VA_ARGS__}}
 
 static const RegVariant kRegVariants[] = {
     RV(float, 16, 16, 64, 16),          RV(float, 32, 16, 64, 16, 2),     RV(float, 64, 16, 32, 16, 4),
@@ -155,6 +171,16 @@ int reg_variant_for(bool is_double, size_t n) {
     for (int i = 0; i < (int)(sizeof(kRegVariants) / sizeof(kRegVariants[0])); i++)
         if (kRegVariants[i].is_double == (int)is_double && (size_t)kRegVariants[i].n == n) return i;
     return -1;
+}
+
+// Radix sequence of a variant (0-terminated in the table); returns the stage count.
+int reg_variant_radices(int v, int *out) {
+    int n = 0;
+    while (n < 8 && kRegVariants[v].radices[n]) {
+        out[n] = kRegVariants[v].radices[n];
+        n++;
+    }
+    return n;
 }
 
 void reg_variant_shape(int v, int *threads, int *lines_per_cta, size_t *smem) {
