@@ -125,7 +125,7 @@ extern "C" int b200fft_emu_run(const b200fft_config *cfg, int direction, const b
 // The register-resident kernels are not emulated (their threads exchange data inside
 // one op); the lowering never selects them in this build.
 namespace b200fft {
-int reg_variant_for(bool, size_t) { return -1; }
+int reg_variant_for(bool, size_t, int, bool) { return -1; }
 }  // namespace b200fft
 namespace b200fft {
 int reg_variant_radices(int, int *) { return 0; }

@@ -657,22 +657,31 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         return;
     }
 
-    // Fast path: contiguous power-of-two Stockham lines run in the register-resident
-    // kernel (one global read and write, two shared-memory exchanges).
-    if (alg->kind == AlgorithmKind::Stockham && !strided && !job.in_real && !job.in_herm && !job.out_real &&
-        out_count == N && is_pow2(N) && reg_kernels_enabled()) {
-        const int rv = reg_variant_for(prog.is_double, N);
+    // Fast path: power-of-two Stockham lines run in the register-resident kernels
+    // (one global read and write, shared memory only between the middle stages).
+    if (alg->kind == AlgorithmKind::Stockham && is_pow2(N) && reg_kernels_enabled()) {
+        int mode = -1;
+        if (!job.in_real && !job.in_herm && !job.out_real && out_count == N)
+            mode = REG_C2C;
+        else if (job.in_real && !job.out_real && out_count == N / 2 + 1 && !strided)
+            mode = REG_R2C_FULL;
+        else if (job.in_herm && job.out_real && out_count == N && !strided)
+            mode = REG_C2R_FULL;
+        const int rv = mode >= 0 ? reg_variant_for(prog.is_double, N, mode, strided) : -1;
         if (rv >= 0) {
             PassPlan pp{};
             pp.kernel = KERNEL_REG;
             pp.reg_variant = rv;
             pp.reg_table = table_reg_twiddles(prog, N, rv);
-            pp.rp.nlines = no;
-            pp.rp.in_stride = job.in_os;
-            pp.rp.out_stride = job.out_os;
+            pp.rp.nlines = no * S;
+            pp.rp.ni = S;
+            pp.rp.src = RegSide{job.in_os, strided ? 1 : 0, S};
+            pp.rp.dst = RegSide{job.out_os, strided ? 1 : 0, S};
             pp.rp.scale = scale;
-            pp.rp.conj = inv ? 1 : 0;
+            pp.rp.conj = (mode == REG_C2C && inv) ? 1 : 0;
             pp.rp.n = (int32_t)N;
+            pp.reg_in_real = mode == REG_R2C_FULL;
+            pp.reg_out_real = mode == REG_C2R_FULL;
             pp.src_buf = job.in_buf;
             pp.src_off = job.in_off;
             pp.dst_buf = job.out_buf;

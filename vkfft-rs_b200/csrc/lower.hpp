@@ -34,7 +34,7 @@ struct RealAxisJob {
 };
 
 std::vector<int> radix_schedule(size_t L);
-int reg_variant_for(bool is_double, size_t n);  // reg_kernels.cu (-1: none)
+int reg_variant_for(bool is_double, size_t n, int mode, bool strided);  // reg_kernels.cu (-1: none)
 int reg_variant_radices(int v, int *out);
 bool line_fits_on_chip(bool dbl, size_t L, const AxisAlgorithm *alg, bool strided);
 void lower_c2c_axis(Program &prog, const AxisJob &job);

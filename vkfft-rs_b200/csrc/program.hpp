@@ -32,6 +32,7 @@ struct PassPlan {
     RegParams rp{};               // KERNEL_REG parameters (pointers patched at launch)
     int reg_variant = -1;
     int reg_table = -1;           // twiddle table id of a KERNEL_REG pass
+    bool reg_in_real = false, reg_out_real = false;
     PassParams p{};               // device pointers are patched at upload / launch
     int op_tables[kMaxOps][3];    // table ids per op (lut, lut2, lut3) or -1
     int src_buf = BUF_IN, dst_buf = BUF_OUT;

@@ -1,15 +1,21 @@
-// Register-resident Stockham kernel for batched contiguous power-of-two C2C lines
-// (the BASELINE config 1/2 hot path).
+// Register-resident Stockham kernels for batched power-of-two lines (the BASELINE
+// config 1/2 hot path, the higher axes of the 3D and 2D-convolution configs, and the
+// FullComplex real transforms).
 //
 // A line of N points is owned by TT = N / E threads, each holding E points in
-// registers.  With the load pattern "thread t holds positions t + m*TT", the
-// first radix stage's butterflies are formed entirely from the thread's own
-// registers and the last stage's outputs land on positions t + m*TT again, so
-// global memory is read and written once, warp-coalesced (32 consecutive
-// threads touch 32 consecutive complex values), with no shared-memory staging.
-// Only the middle stages exchange through one padded shared-memory buffer.
+// registers.  With the load pattern "thread t holds positions t + m*TT", the first
+// radix stage's butterflies are formed entirely from the thread's own registers and
+// the last stage's outputs land on positions t + m*TT again, so global memory is read
+// and written exactly once.  Only the middle stages exchange through one padded
+// shared-memory buffer (odd line stride, one pad slot per 16 points: conflict-free).
+//
+// Layouts: contiguous lines put the TT threads of a line next to each other (a warp
+// touches 32 consecutive complex values); strided lines (STRIDED) put the G lines of a
+// CTA next to each other instead, so a warp touches G neighbouring lines of the same
+// position -- the coalesced access of an ND higher axis without any transpose pass.
+//
 // Twiddles come from per-stage transposed tables read through the read-only cache.
-// Inverse transforms conjugate on load and store (the table stays forward).
+// Inverse transforms conjugate on load and store (tables stay forward).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -34,18 +40,41 @@ template <typename T> __device__ __forceinline__ cplx<T> tw_load(const cplx<T> *
     auto v = __ldg(reinterpret_cast<const typename vec2<T>::type *>(tw) + idx);
     return {v.x, v.y};
 }
+template <typename T> __device__ __forceinline__ cplx<T> ld_c(const void *base, int64_t idx) {
+    const auto w = __ldcs(reinterpret_cast<const typename vec2<T>::type *>(base) + idx);
+    return {w.x, w.y};
+}
+template <typename T> __device__ __forceinline__ void st_c(void *base, int64_t idx, cplx<T> v) {
+    typename vec2<T>::type w;
+    w.x = v.x;
+    w.y = v.y;
+    __stcs(reinterpret_cast<typename vec2<T>::type *>(base) + idx, w);
+}
 
 struct LineIO {
-    int64_t in_off, out_off;
+    int64_t in_base, out_base;
     bool valid;
 };
+
+// Store of one output point at line position p (last stage), per data mode.
+template <typename T, int N, int MODE>
+__device__ __forceinline__ void store_point(const RegParams &rp, const LineIO &io, int p, cplx<T> y) {
+    if (MODE == REG_C2C) {
+        const T s = T(rp.scale);
+        st_c<T>(rp.out, io.out_base + (int64_t)p * rp.dst.es, cplx<T>{y.x * s, rp.conj ? -y.y * s : y.y * s});
+    } else if (MODE == REG_R2C_FULL) {
+        if (p <= N / 2) st_c<T>(rp.out, io.out_base + (int64_t)p * rp.dst.es, y);
+    } else {
+        __stcs(reinterpret_cast<T *>(rp.out) + io.out_base + (int64_t)p * rp.dst.es, y.x * T(rp.scale));
+    }
+}
 
 // One radix-R stage with span P (product of the radices before it).  Its twiddles
 // W_{P R}^{j q} are read from the stage's transposed table (row q-1 holds the P values
 // of j, so a warp's loads are contiguous) at offset OFF; only the power-of-two rows
 // are read and w_q = w_{q - lowbit(q)} * w_{lowbit(q)} forms the rest (at most three
 // products deep).
-template <typename T, int N, int E, int R, int P, int OFF, bool FIRST, bool LAST>
+template <typename T, int N, int E, int MODE, int R, int P, int OFF, bool FIRST, bool LAST>
 __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, const cplx<T> *tw, const RegParams &rp,
                                       const LineIO &io) {
     constexpr int TT = N / E;
@@ -83,15 +112,7 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
         if (LAST) {
             if (io.valid) {
 #pragma unroll
-                for (int q = 0; q < R; q++) {
-                    cplx<T> y = x[q];
-                    y.x *= T(rp.scale);
-                    y.y *= rp.conj ? -T(rp.scale) : T(rp.scale);
-                    typename vec2<T>::type w;
-                    w.x = y.x;
-                    w.y = y.y;
-                    __stcs(reinterpret_cast<typename vec2<T>::type *>(rp.out) + io.out_off + b + q * (N / R), w);
-                }
+                for (int q = 0; q < R; q++) store_point<T, N, MODE>(rp, io, b + q * (N / R), x[q]);
             }
         } else {
             const int e0 = (b - j) * R + j;
@@ -101,43 +122,63 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
     }
 }
 
-template <typename T, int N, int E, int P, int OFF, bool FIRST, int R, int... Rest>
+template <typename T, int N, int E, int MODE, int P, int OFF, bool FIRST, int R, int... Rest>
 __device__ __forceinline__ void stages(cplx<T> (&v)[E], int t, cplx<T> *sline, const cplx<T> *tw, const RegParams &rp,
                                        const LineIO &io) {
     constexpr bool LAST = sizeof...(Rest) == 0;
-    stage<T, N, E, R, P, OFF, FIRST, LAST>(v, t, sline, tw, rp, io);
+    stage<T, N, E, MODE, R, P, OFF, FIRST, LAST>(v, t, sline, tw, rp, io);
     // the first stage (P = 1) has no twiddles and no table rows
     constexpr int NEXT_OFF = OFF + (P > 1 ? (R - 1) * P : 0);
-    if constexpr (!LAST) stages<T, N, E, P * R, NEXT_OFF, false, Rest...>(v, t, sline, tw, rp, io);
+    if constexpr (!LAST) stages<T, N, E, MODE, P * R, NEXT_OFF, false, Rest...>(v, t, sline, tw, rp, io);
 }
 
-template <typename T, int N, int E, int G, int... Rs>
+template <typename T, int N, int E, int G, int MODE, bool STRIDED, int... Rs>
 __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_constant__ RegParams rp) {
     constexpr int TT = N / E;
     constexpr int LS = N + N / 16 + 1;  // padded line stride in shared memory
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int g = threadIdx.x / TT;
-    const int t = threadIdx.x - g * TT;
+    int g, t;
+    if (STRIDED) {
+        g = threadIdx.x % G;
+        t = threadIdx.x / G;
+    } else {
+        g = threadIdx.x / TT;
+        t = threadIdx.x - g * TT;
+    }
     const int64_t line = (int64_t)blockIdx.x * G + g;
     LineIO io;
     io.valid = line < rp.nlines;
-    io.in_off = line * rp.in_stride;
-    io.out_off = line * rp.out_stride;
+    {
+        const int64_t o = rp.ni == 1 ? line : line / rp.ni;
+        const int64_t i = line - o * rp.ni;
+        io.in_base = o * rp.src.os + i * rp.src.is;
+        io.out_base = o * rp.dst.os + i * rp.dst.is;
+    }
     cplx<T> *sline = reinterpret_cast<cplx<T> *>(smem_raw) + g * LS;
     const cplx<T> *tw = reinterpret_cast<const cplx<T> *>(rp.tw);
     cplx<T> v[E];
     if (io.valid) {
-        const auto *src = reinterpret_cast<const typename vec2<T>::type *>(rp.in) + io.in_off + t;
 #pragma unroll
         for (int m = 0; m < E; m++) {
-            const auto w = __ldcs(src + m * TT);
-            v[m] = {w.x, rp.conj ? -w.y : w.y};
+            const int p = t + m * TT;
+            if (MODE == REG_C2C) {
+                const cplx<T> w = ld_c<T>(rp.in, io.in_base + (int64_t)p * rp.src.es);
+                v[m] = {w.x, rp.conj ? -w.y : w.y};
+            } else if (MODE == REG_R2C_FULL) {
+                v[m] = {__ldcs(reinterpret_cast<const T *>(rp.in) + io.in_base + (int64_t)p * rp.src.es), T(0)};
+            } else {
+                // Hermitian mirror X[p] = conj(X[N - p]) for p > N/2; the inverse transform
+                // runs on conj(X), so the stored half is conjugated and the mirror is not
+                const int q = p <= N / 2 ? p : N - p;
+                const cplx<T> w = ld_c<T>(rp.in, io.in_base + (int64_t)q * rp.src.es);
+                v[m] = {w.x, p <= N / 2 ? -w.y : w.y};
+            }
         }
     } else {
 #pragma unroll
         for (int m = 0; m < E; m++) v[m] = {T(0), T(0)};
     }
-    stages<T, N, E, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
+    stages<T, N, E, MODE, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
 }
 
 }  // namespace regk
@@ -145,31 +186,51 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
 // ---- variant table ----------------------------------------------------------------
 
 struct RegVariant {
-    int is_double, n, threads, g;
+    int is_double, n, mode, strided, threads, g;
     size_t smem;
     const void *fn;
     int radices[8];
 };
 
-#define RV(T, N, E, G, ...)                                                                                 \
-    {sizeof(T) == 8, N, G *(N / E), G, (size_t)G *(N + N / 16 + 1) * sizeof(T) * 2,                       \
-     (const void *)regk::reg_fft_kernel<T, N, E, G, __VA_ARGS__>, {__VA_ARGS__}}
+#define RV(T, MODE, STR, N, E, G, ...)                                                                      \
+    {sizeof(T) == 8, N, MODE, STR, G *(N / E), G, (size_t)G *(N + N / 16 + 1) * sizeof(T) * 2,             \
+     (const void *)regk::reg_fft_kernel<T, N, E, G, MODE, STR, __VA_ARGS__>, {__VA_ARGS__}}
+
+// contiguous lines, all modes
+#define RV_CONTIG(T, MODE)                                                                                  \
+    RV(T, MODE, false, 16, 16, 64, 16), RV(T, MODE, false, 32, 16, 64, 16, 2),                            \
+        RV(T, MODE, false, 64, 16, 32, 16, 4), RV(T, MODE, false, 128, 16, 16, 16, 8),                   \
+        RV(T, MODE, false, 256, 16, 16, 16, 16), RV(T, MODE, false, 512, 16, 8, 16, 16, 2),              \
+        RV(T, MODE, false, 1024, 16, 4, 16, 16, 4), RV(T, MODE, false, 2048, 16, 2, 16, 16, 8),          \
+        RV(T, MODE, false, 4096, 16, 1, 16, 16, 16), RV(T, MODE, false, 8192, 16, 1, 16, 16, 16, 2)
 
 static const RegVariant kRegVariants[] = {
-    RV(float, 16, 16, 64, 16),          RV(float, 32, 16, 64, 16, 2),     RV(float, 64, 16, 32, 16, 4),
-    RV(float, 128, 16, 16, 16, 8),      RV(float, 256, 16, 16, 16, 16),   RV(float, 512, 16, 8, 16, 16, 2),
-    RV(float, 1024, 16, 4, 16, 16, 4),  RV(float, 2048, 16, 2, 16, 16, 8), RV(float, 4096, 16, 1, 16, 16, 16),
-    RV(float, 8192, 16, 1, 16, 16, 16, 2),
-    RV(double, 16, 16, 64, 16),         RV(double, 32, 16, 64, 16, 2),    RV(double, 64, 16, 32, 16, 4),
-    RV(double, 128, 16, 16, 16, 8),     RV(double, 256, 16, 16, 16, 16),  RV(double, 512, 16, 8, 16, 16, 2),
-    RV(double, 1024, 16, 4, 16, 16, 4), RV(double, 2048, 16, 2, 16, 16, 8), RV(double, 4096, 16, 1, 16, 16, 16),
-    RV(double, 8192, 16, 1, 16, 16, 16, 2),
+    RV_CONTIG(float, REG_C2C),
+    RV_CONTIG(double, REG_C2C),
+    RV_CONTIG(float, REG_R2C_FULL),
+    RV_CONTIG(double, REG_R2C_FULL),
+    RV_CONTIG(float, REG_C2R_FULL),
+    RV_CONTIG(double, REG_C2R_FULL),
+    // strided (higher-axis) C2C lines: G neighbouring lines per CTA
+    RV(float, REG_C2C, true, 16, 16, 32, 16), RV(float, REG_C2C, true, 32, 16, 32, 16, 2),
+    RV(float, REG_C2C, true, 64, 16, 32, 16, 4), RV(float, REG_C2C, true, 128, 16, 32, 16, 8),
+    RV(float, REG_C2C, true, 256, 16, 16, 16, 16), RV(float, REG_C2C, true, 512, 16, 16, 16, 16, 2),
+    RV(float, REG_C2C, true, 1024, 16, 16, 16, 16, 4), RV(float, REG_C2C, true, 2048, 16, 8, 16, 16, 8),
+    RV(float, REG_C2C, true, 4096, 16, 4, 16, 16, 16),
+    RV(double, REG_C2C, true, 16, 16, 32, 16), RV(double, REG_C2C, true, 32, 16, 32, 16, 2),
+    RV(double, REG_C2C, true, 64, 16, 16, 16, 4), RV(double, REG_C2C, true, 128, 16, 16, 16, 8),
+    RV(double, REG_C2C, true, 256, 16, 16, 16, 16), RV(double, REG_C2C, true, 512, 16, 8, 16, 16, 2),
+    RV(double, REG_C2C, true, 1024, 16, 4, 16, 16, 4), RV(double, REG_C2C, true, 2048, 16, 4, 16, 16, 8),
+    RV(double, REG_C2C, true, 4096, 16, 2, 16, 16, 16),
 };
+#undef RV_CONTIG
 #undef RV
 
-int reg_variant_for(bool is_double, size_t n) {
-    for (int i = 0; i < (int)(sizeof(kRegVariants) / sizeof(kRegVariants[0])); i++)
-        if (kRegVariants[i].is_double == (int)is_double && (size_t)kRegVariants[i].n == n) return i;
+int reg_variant_for(bool is_double, size_t n, int mode, bool strided) {
+    for (int i = 0; i < (int)(sizeof(kRegVariants) / sizeof(kRegVariants[0])); i++) {
+        const RegVariant &v = kRegVariants[i];
+        if (v.is_double == (int)is_double && (size_t)v.n == n && v.mode == mode && v.strided == (int)strided) return i;
+    }
     return -1;
 }
 
@@ -183,11 +244,7 @@ int reg_variant_radices(int v, int *out) {
     return n;
 }
 
-void reg_variant_shape(int v, int *threads, int *lines_per_cta, size_t *smem) {
-    *threads = kRegVariants[v].threads;
-    *lines_per_cta = kRegVariants[v].g;
-    *smem = kRegVariants[v].smem;
-}
+int reg_variant_lines_per_cta(int v) { return kRegVariants[v].g; }
 
 void set_reg_kernel_smem_limits() {
     static unsigned long long done_mask = 0;

@@ -1,16 +1,29 @@
-// Parameters of the register-resident Stockham kernel (reg_kernels.cu).
+// Parameters of the register-resident Stockham kernels (reg_kernels.cu).
 #pragma once
 #include <cstdint>
 
 namespace b200fft {
 
+// Register-kernel data modes.
+enum RegMode : int32_t {
+    REG_C2C = 0,      // complex in, complex out
+    REG_R2C_FULL = 1, // real in (promoted on load), first N/2+1 bins out (RealFftAlgorithm::FullComplex)
+    REG_C2R_FULL = 2, // N/2+1 Hermitian bins in (mirrored on load), real part out
+};
+
+// Line l = o * ni + i; element p of the line is at o*os + i*is + p*es (units of the
+// side's element: complex, or scalar for a real side).
+struct RegSide {
+    int64_t os, is, es;
+};
+
 struct RegParams {
     const void *in;
     void *out;
-    const void *tw;      // forward W_N table of the pass precision
+    const void *tw;      // per-stage transposed twiddle tables (reg_kernels.cu)
     int64_t nlines;      // transforms in this launch
-    int64_t in_stride;   // complex elements between consecutive lines
-    int64_t out_stride;
+    int64_t ni;          // inner line count (1 for contiguous lines)
+    RegSide src, dst;
     double scale;        // applied on store
     int32_t conj;        // inverse: conjugate on load and on store
     int32_t n;

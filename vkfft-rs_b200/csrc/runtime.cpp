@@ -199,8 +199,8 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
     for (const PassPlan &pp : prog.passes) {
         if (pp.kernel == KERNEL_REG) {
             RegParams rp = pp.rp;
-            rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * esz;
-            rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * esz;
+            rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * (pp.reg_in_real ? esz / 2 : esz);
+            rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * (pp.reg_out_real ? esz / 2 : esz);
             rp.tw = dt.ptrs[pp.reg_table];
             if (injected("launch", g_launch_count)) fail_runtime("kernel launch failed: injected launch fault");
             check(launch_reg(pp.reg_variant, rp, stream), "kernel launch");
