@@ -9,6 +9,8 @@ import emulator
 pytestmark = pytest.mark.skipif(not emulator.available(), reason="AddressSanitizer runtime not installed")
 
 TOL = {"F32": 2e-6, "F64": 1e-13}
+REC = dict(min_rader_direct_prime=17, max_rader_direct_prime=89, min_rader_fft_prime=17, max_rader_fft_prime=16384,
+           allow_recursive_fft_rader=True)
 
 CASES = [
     dict(kind="c2c", dims=[1024], batch=3, prec="F32"),
@@ -36,6 +38,17 @@ CASES = [
     dict(kind="c2r", dims=[206], batch=2, prec="F64", normalize=True),
     dict(kind="c2r", dims=[45], batch=2, prec="F64", normalize=True),
     dict(kind="c2r", dims=[12, 30], batch=1, prec="F64", normalize=True),
+    # nested and pass-level Rader (recursive tuning), Rader four-step, f64 CT x Bluestein
+    dict(kind="c2c", dims=[107], batch=3, prec="F64", tuning=REC),
+    dict(kind="c2c", dims=[683], batch=2, prec="F32", tuning=REC),
+    dict(kind="c2c", dims=[4099], batch=2, prec="F32", tuning=REC),
+    dict(kind="r2c", dims=[8704], batch=1, prec="F64"),
+    dict(kind="c2r", dims=[8704], batch=1, prec="F64", normalize=True),
+    dict(kind="r2c", dims=[4106], batch=1, prec="F64"),
+    dict(kind="c2r", dims=[4106], batch=1, prec="F64", normalize=True),
+    dict(kind="c2c", dims=[4106], batch=1, prec="F64", inverse=True, normalize=True),
+    dict(kind="c2c", dims=[17 * 4096], batch=1, prec="F32"),
+    dict(kind="c2r", dims=[3, 206], batch=1, prec="F64", normalize=True),
 ]
 
 

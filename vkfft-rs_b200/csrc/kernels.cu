@@ -62,7 +62,7 @@ template <typename T>
 __device__ __forceinline__ cplx<T> apply_mul(cplx<T> v, const Op &op, int c, int e, int n) {
     if (op.flags & F_CONJ_IN) v = cconj(v);
     if (op.mul != MUL_NONE) {
-        const int idx = op.mul == MUL_LUT_N ? n : c * e;
+        const int idx = (op.flags & F_OWN_INDEX) ? c * op.cm + e * op.em : (op.mul == MUL_LUT_N ? n : c * e);
         cplx<T> w = ld_ro<T>(op.lut, idx);
         if (op.flags & F_CONJ_LUT) w = cconj(w);
         v = cmul(v, w);
@@ -113,11 +113,21 @@ __device__ __forceinline__ void op_load(const PassParams &p, const Op &op, cplx<
                 const int c = lm.col[g];
                 const int n = c * s.cm + e * s.em;
                 if (g < lm.nl && n < s.count) {
-                    const int64_t a = lm.ib[g] + (int64_t)e * s.es;
+                    int64_t a = lm.ib[g] + (int64_t)e * s.es;
+                    bool mirrored = false;
+                    if (s.herm && n > s.herm / 2) {
+                        // Hermitian input: X[n] = conj(X[N - n]), N - n < N/2 is stored
+                        const int n2 = s.herm - n;
+                        const int e2 = n2 / s.em;
+                        const int c2 = s.cm ? n2 - e2 * s.em : c;
+                        a = lm.ib[g] + (int64_t)(c2 - c) * s.cs + (int64_t)e2 * s.es;
+                        mirrored = true;
+                    }
                     if (s.real) {
                         v[u].x = __ldcs(reinterpret_cast<const T *>(p.src) + a);
                     } else {
                         v[u] = ld_data<T>(p.src, a);
+                        if (mirrored) v[u].y = -v[u].y;
                     }
                     v[u] = apply_mul(v[u], op, c, e, n);
                 }
@@ -399,6 +409,60 @@ __device__ __forceinline__ void op_herm_expand(const PassParams &p, const Op &op
     }
 }
 
+// Pass-level Rader gather: dst[m] = src[g^m mod p] for m < p-1 and dst[p-1] = src[0]
+// (the line layout of the convolution scratch is [a_0 .. a_{p-2}, x0, A0]).
+template <typename T>
+__device__ __forceinline__ void op_permute_gather(const Op &op, cplx<T> *sm) {
+    const int pr = op.radix;
+    const int *perm = reinterpret_cast<const int *>(op.lut2);
+    const int total = op.nsub * pr;
+    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+        const int g = fdiv(f, op.div_c);
+        const int m = f - g * pr;
+        const int q = m < pr - 1 ? __ldg(perm + m) : 0;
+        sm[op.dst_base + g * op.sub_stride + spad(m)] = sm[op.src_base + g * op.sub_stride + spad(q)];
+    }
+}
+
+// line[slot] = line[0] for every line of the src region.
+template <typename T>
+__device__ __forceinline__ void op_save_dc(const Op &op, cplx<T> *sm) {
+    for (int g = threadIdx.x; g < op.nsub; g += blockDim.x)
+        sm[op.src_base + g * op.sub_stride + spad(op.nfull)] = sm[op.src_base + g * op.sub_stride];
+}
+
+// Pass-level Rader scatter: from [c_0 .. c_{p-2}, x0, A0] (c conjugated when F_CONJ_IN),
+// dst[g^-m] = x0 + c[m], dst[0] = x0 + A0, then F_SCALE / F_CONJ_OUT.
+template <typename T>
+__device__ __forceinline__ void op_permute_scatter(const Op &op, cplx<T> *sm) {
+    const int pr = op.radix;
+    const int *ginv = reinterpret_cast<const int *>(op.lut3);
+    const int total = op.nsub * pr;
+    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+        const int g = fdiv(f, op.div_c);
+        const int m = f - g * pr;
+        const cplx<T> *src = sm + op.src_base + g * op.sub_stride;
+        const cplx<T> x0 = src[spad(pr - 1)];
+        cplx<T> acc;
+        int k;
+        if (m < pr - 1) {
+            acc = src[spad(m)];
+            if (op.flags & F_CONJ_IN) acc = cconj(acc);
+            k = __ldg(ginv + m);
+        } else {
+            acc = src[spad(pr)];
+            k = 0;
+        }
+        cplx<T> y = {x0.x + acc.x, x0.y + acc.y};
+        if (op.flags & F_SCALE) {
+            y.x *= T(op.scale);
+            y.y *= T(op.scale);
+        }
+        if (op.flags & F_CONJ_OUT) y = cconj(y);
+        sm[op.dst_base + g * op.sub_stride + spad(k)] = y;
+    }
+}
+
 // Per-thread prologue: copy the op program into shared memory (after the line
 // metadata, so the dynamic op index below reads shared memory rather than the
 // parameter block) and resolve every line's global base addresses.
@@ -445,6 +509,9 @@ __device__ __forceinline__ void run_op(const PassParams &p, const Op &op, cplx<T
         case OP_RADER_GATHER: op_rader_gather<T>(op, sm); break;
         case OP_RADER_SCATTER: op_rader_scatter<T>(op, sm); break;
         case OP_HERM_EXPAND: op_herm_expand<T>(p, op, sm); break;
+        case OP_PERMUTE_GATHER: op_permute_gather<T>(op, sm); break;
+        case OP_PERMUTE_SCATTER: op_permute_scatter<T>(op, sm); break;
+        case OP_SAVE_DC: op_save_dc<T>(op, sm); break;
         default: raise_error(p.err, 4); break;
     }
 }

@@ -254,9 +254,16 @@ struct StageSpec {
     bool rader = false;
     bool direct = false;
     size_t generator = 0;
+    std::vector<StageSpec> sub;  // FFT-convolution Rader: stages of the (p-1)-point sub-transform
+    bool ok = true;              // false when some factor has no kernel (nested Bluestein)
 };
 
-// Stages of a line of length L for an axis algorithm (Stockham radices, Rader primes).
+static const PlannerTuning *g_tuning = nullptr;  // tuning of the axis being lowered
+
+// Stages of a line of length L for an axis algorithm: Stockham radices first, then one
+// Rader stage per Rader prime occurrence.  An FFT-convolution Rader prime p carries the
+// stages of its (p-1)-point convolution, planned with the axis tuning (the recursive
+// tuning can make that convolution Rader again, planner.rs:512-529).
 std::vector<StageSpec> line_stages(size_t L, const AxisAlgorithm *alg) {
     std::vector<StageSpec> out;
     size_t smooth = L;
@@ -269,18 +276,66 @@ std::vector<StageSpec> line_stages(size_t L, const AxisAlgorithm *alg) {
                 s.rader = true;
                 s.direct = !rp.fft_convolution;
                 s.generator = rp.generator;
+                if (!s.direct) {
+                    const PlannerTuning t = g_tuning ? *g_tuning : PlannerTuning::portable();
+                    AxisAlgorithm nested = plan_axis_algorithm(rp.prime - 1, t);
+                    if (nested.kind == AlgorithmKind::Bluestein) {
+                        s.ok = false;
+                    } else {
+                        s.sub = line_stages(rp.prime - 1, &nested);
+                        for (auto &x : s.sub) s.ok = s.ok && x.ok;
+                    }
+                }
                 rader.push_back(s);
                 smooth /= rp.prime;
             }
         }
+    }
+    if (!is_kernel_smooth(smooth)) {
+        StageSpec bad;
+        bad.radix = 0;
+        bad.ok = false;
+        out.push_back(bad);
+        return out;
     }
     for (int r : radix_schedule(smooth)) out.push_back(StageSpec{r});
     for (auto &s : rader) out.push_back(s);
     return out;
 }
 
+static bool stages_ok(const std::vector<StageSpec> &st) {
+    for (auto &s : st)
+        if (!s.ok) return false;
+    return true;
+}
+
+// Extra shared memory (complex elements) of the Rader stages of a stage list applied to
+// nsub sub-lines of length L whose line regions have stride ls.  A Rader stage gathers
+// from the current buffer into W, which reuses the free ping-pong partner when it fits,
+// runs its sub-transform between W and W2, and scatters back into the current buffer.
+// Stages at one level run one after another, so they share the same region.
+static size_t rader_extra(size_t L, const std::vector<StageSpec> &stages, size_t nsub, size_t ls) {
+    size_t best = 0;
+    for (auto &st : stages) {
+        if (!st.rader) continue;
+        const size_t p = (size_t)st.radix;
+        const size_t nb = nsub * (L / p);
+        const size_t ws = (size_t)line_stride_for((int)(p - 1));
+        const bool w_in_partner = nb * ws <= nsub * ls;
+        size_t need = 2 * nb;  // X0 pairs
+        if (!st.direct) {
+            need += nb * ws;  // W2
+            need += rader_extra(p - 1, st.sub, nb, ws);
+        }
+        if (!w_in_partner) need += nb * ws;
+        best = std::max(best, need);
+    }
+    return best;
+}
+
 struct PassShape {
-    int G = 1, threads = 64, ls = 1, ws = 1, nbw = 0;
+    int G = 1, threads = 64, ls = 1;
+    size_t extra = 0;  // Rader region elements
     size_t smem = 0, meta_off = 0;
 };
 
@@ -290,22 +345,17 @@ static size_t budget_bytes() { return 200 * 1024; }
 // line does not fit on chip.
 static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bool strided, int64_t nlines,
                        int nops, PassShape &sh) {
+    if (!stages_ok(stages)) return false;
     const size_t esz = dbl ? 16 : 8;
     sh.ls = line_stride_for(L);
-    int pmin = 0, pmax = 0;
-    for (auto &s : stages)
-        if (s.rader) {
-            pmin = pmin ? std::min(pmin, s.radix) : s.radix;
-            pmax = std::max(pmax, s.radix);
-        }
-    sh.ws = pmax ? line_stride_for(pmax - 1) : 0;
+    auto data_for = [&](int G) {
+        size_t data = (2 * (size_t)G * sh.ls + rader_extra((size_t)L, stages, (size_t)G, (size_t)sh.ls)) * esz;
+        return (data + 15) & ~size_t(15);
+    };
     auto bytes_for = [&](int G) {
-        size_t nbw = pmin ? (size_t)G * L / pmin : 0;
-        size_t data = (2 * (size_t)G * sh.ls + 2 * nbw * sh.ws + 2 * nbw) * esz;
-        data = (data + 15) & ~size_t(15);
         size_t meta = (size_t)G * 16 + (size_t)((G + 3) & ~3) * 4;
         meta = (meta + 15) & ~size_t(15);
-        return data + meta + (size_t)nops * sizeof(Op);
+        return data_for(G) + meta + (size_t)nops * sizeof(Op);
     };
     const int gmin = strided ? (dbl ? 4 : 8) : 1;
     int G = std::max(gmin, (int)((2048 + L - 1) / L));
@@ -315,11 +365,8 @@ static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bo
     while (G > 1 && bytes_for(G) > budget_bytes()) G--;
     if (bytes_for(G) > budget_bytes()) return false;
     sh.G = G;
-    sh.nbw = pmin ? G * L / pmin : 0;
-    size_t nbw = sh.nbw;
-    size_t data = (2 * (size_t)G * sh.ls + 2 * nbw * sh.ws + 2 * nbw) * esz;
-    data = (data + 15) & ~size_t(15);
-    sh.meta_off = data;
+    sh.extra = rader_extra((size_t)L, stages, (size_t)G, (size_t)sh.ls);
+    sh.meta_off = data_for(G);
     sh.smem = bytes_for(G);
     const int maxt = dbl ? 512 : 1024;
     int64_t work = (int64_t)G * L / 8;
@@ -337,17 +384,8 @@ static bool line_capacity_ok(bool dbl, size_t L) {
 
 bool line_fits_on_chip(bool dbl, size_t L, const AxisAlgorithm *alg, bool strided) {
     if (L > (1u << 20)) return false;
-    if (alg && alg->kind == AlgorithmKind::Rader) {
-        for (auto &rp : alg->primes)
-            if (rp.fft_convolution && !is_kernel_smooth(rp.prime - 1)) return false;
-    }
-    size_t smooth = L;
-    if (alg && alg->kind == AlgorithmKind::Rader)
-        for (auto &rp : alg->primes)
-            for (size_t k = 0; k < rp.multiplicity; k++) smooth /= rp.prime;
-    if (!is_kernel_smooth(smooth)) return false;
     PassShape sh;
-    return shape_pass(dbl, (int)L, line_stages(L, alg), strided, 1 << 20, 16, sh);
+    return shape_pass(dbl, (int)L, line_stages(L, alg), strided, 1 << 20, kMaxOps, sh);
 }
 
 // Builds the op program of one pass.
@@ -355,13 +393,11 @@ class PassBuilder {
    public:
     PassBuilder(Program &prog, int L, std::vector<StageSpec> stages, bool strided, int64_t nlines, int nops_hint)
         : prog_(prog), L_(L), stages_(std::move(stages)) {
-        if (!shape_pass(prog.is_double, L, stages_, strided, nlines, nops_hint, sh_))
+        if (!shape_pass(prog.is_double, L, stages_, strided, nlines, std::max(nops_hint, (int)kMaxOps), sh_))
             fail_resource("B200 FFT pass shared memory", (size_t)L * (prog.is_double ? 32 : 16), budget_bytes());
         A_ = 0;
         B_ = sh_.G * sh_.ls;
-        W_ = 2 * sh_.G * sh_.ls;
-        W2_ = W_ + sh_.nbw * sh_.ws;
-        X0_ = W2_ + sh_.nbw * sh_.ws;
+        extra_base_ = 2 * sh_.G * sh_.ls;
         cur_ = A_;
         other_ = B_;
         for (auto &row : plan_.op_tables) row[0] = row[1] = row[2] = -1;
@@ -381,11 +417,13 @@ class PassBuilder {
         plan_.op_tables[nops_ - 1][2] = c;
     }
 
-    // global -> line region A
-    void load(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0) {
+    // global -> line region A.  own_em > 0: the table index of the multiply is e*own_em
+    // (instead of the side's logical index).
+    void load(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0, int own_em = 0) {
         Op &o = push(OP_LOAD);
         o.len = len;
-        o.flags = flags;
+        o.flags = flags | (own_em ? F_OWN_INDEX : 0);
+        o.em = own_em;
         o.mul = mul;
         o.dst_base = A_;
         o.sub_stride = sh_.ls;
@@ -397,36 +435,7 @@ class PassBuilder {
     }
 
     // the full FFT network of the line (length L_) on the current region
-    void fft() {
-        const int tw = table_twiddle(prog_, (size_t)L_);
-        int P = 1;
-        for (auto &st : stages_) {
-            if (!st.rader) {
-                Op &o = push(OP_STAGE);
-                o.radix = st.radix;
-                o.P = P;
-                o.len = L_;
-                o.nsub = sh_.G;
-                o.src_base = cur_;
-                o.dst_base = other_;
-                o.sub_stride = sh_.ls;
-                o.div_a = make_fastdiv((uint32_t)(L_ / st.radix));
-                o.div_b = make_fastdiv((uint32_t)P);
-                set_tables(tw);
-            } else {
-                emit_rader(st, P, tw);
-            }
-            std::swap(cur_, other_);
-            P *= st.radix;
-        }
-    }
-
-    void herm_expand(int n) {
-        Op &o = push(OP_HERM_EXPAND);
-        o.src_base = cur_;
-        o.sub_stride = sh_.ls;
-        o.nfull = n;
-    }
+    void fft() { emit_stages((size_t)L_, stages_, (size_t)sh_.G, sh_.ls, cur_, other_, extra_base_); }
 
     void mul_region(int table, int flags, int cm, int em, int count = 0) {
         Op &o = push(OP_MUL);
@@ -441,6 +450,13 @@ class PassBuilder {
         o.flags = flags;
         o.div_a = make_fastdiv((uint32_t)L_);
         set_tables(table);
+    }
+
+    void herm_expand(int n) {
+        Op &o = push(OP_HERM_EXPAND);
+        o.src_base = cur_;
+        o.sub_stride = sh_.ls;
+        o.nfull = n;
     }
 
     void r2c_post(int h, int wn_table) {
@@ -463,10 +479,45 @@ class PassBuilder {
         set_tables(-1, wn_table);
     }
 
-    void store(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0) {
+    // Rader pass-level permutations (rader_ir.rs gather / scatter dispatches): see
+    // OP_PERMUTE_GATHER / OP_PERMUTE_SCATTER in pass_desc.hpp.
+    void permute_gather(int p, int perm_table) {
+        Op &o = push(OP_PERMUTE_GATHER);
+        o.radix = p;
+        o.nsub = sh_.G;
+        o.src_base = cur_;
+        o.dst_base = other_;
+        o.sub_stride = sh_.ls;
+        o.div_c = make_fastdiv((uint32_t)(p + 1));
+        set_tables(-1, perm_table);
+        std::swap(cur_, other_);
+    }
+    void permute_scatter(int p, int ginv_table, int flags, double scale) {
+        Op &o = push(OP_PERMUTE_SCATTER);
+        o.radix = p;
+        o.nsub = sh_.G;
+        o.src_base = cur_;
+        o.dst_base = other_;
+        o.sub_stride = sh_.ls;
+        o.flags = flags;
+        o.scale = scale;
+        o.div_c = make_fastdiv((uint32_t)p);
+        set_tables(-1, -1, ginv_table);
+        std::swap(cur_, other_);
+    }
+    void save_dc(int slot) {
+        Op &o = push(OP_SAVE_DC);
+        o.nsub = sh_.G;
+        o.src_base = cur_;
+        o.sub_stride = sh_.ls;
+        o.nfull = slot;
+    }
+
+    void store(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0, int own_em = 0) {
         Op &o = push(OP_STORE);
         o.len = len;
-        o.flags = flags;
+        o.flags = flags | (own_em ? F_OWN_INDEX : 0);
+        o.em = own_em;
         o.mul = mul;
         o.src_base = cur_;
         o.sub_stride = sh_.ls;
@@ -505,80 +556,100 @@ class PassBuilder {
     }
 
    private:
-    void emit_rader(const StageSpec &st, int P, int tw) {
+    // Stages of a transform of length L on nsub sub-lines (stride ls) held in region cur;
+    // other is its free partner, extra the first free element for Rader work regions.
+    // On return cur holds the result.
+    void emit_stages(size_t L, const std::vector<StageSpec> &stages, size_t nsub, int ls, int &cur, int &other,
+                     size_t extra) {
+        const int tw = table_twiddle(prog_, L);
+        int P = 1;
+        for (auto &st : stages) {
+            if (!st.rader) {
+                Op &o = push(OP_STAGE);
+                o.radix = st.radix;
+                o.P = P;
+                o.len = (int)L;
+                o.nsub = (int)nsub;
+                o.src_base = cur;
+                o.dst_base = other;
+                o.sub_stride = ls;
+                o.div_a = make_fastdiv((uint32_t)(L / st.radix));
+                o.div_b = make_fastdiv((uint32_t)P);
+                set_tables(tw);
+                std::swap(cur, other);
+            } else {
+                emit_rader(st, L, nsub, ls, P, tw, cur, other, extra);
+            }
+            P *= st.radix;
+        }
+    }
+
+    void emit_rader(const StageSpec &st, size_t L, size_t nsub, int ls, int P, int tw, int cur, int other,
+                    size_t extra) {
         const int p = st.radix;
-        const int nb = sh_.G * (L_ / p);
+        const size_t nb = nsub * (L / p);
+        const int ws = line_stride_for(p - 1);
+        const bool w_in_partner = nb * (size_t)ws <= nsub * (size_t)ls;
+        size_t at = extra;
+        const int W = w_in_partner ? other : (int)at;
+        if (!w_in_partner) at += nb * ws;
+        int W2 = 0;
+        if (!st.direct) {
+            W2 = (int)at;
+            at += nb * ws;
+        }
+        const int X0 = (int)at;
+        at += 2 * nb;
         RaderTables rt = table_rader(prog_, (size_t)p, st.generator, !st.direct);
         {
             Op &o = push(OP_RADER_GATHER);
             o.radix = p;
             o.P = P;
-            o.len = L_;
-            o.nsub = sh_.G;
-            o.src_base = cur_;
-            o.sub_stride = sh_.ls;
-            o.w_base = W_;
-            o.w_stride = sh_.ws;
-            o.x0_base = X0_;
-            o.div_a = make_fastdiv((uint32_t)(L_ / p));
+            o.len = (int)L;
+            o.nsub = (int)nsub;
+            o.src_base = cur;
+            o.sub_stride = ls;
+            o.w_base = W;
+            o.w_stride = ws;
+            o.x0_base = X0;
+            o.div_a = make_fastdiv((uint32_t)(L / p));
             o.div_b = make_fastdiv((uint32_t)P);
             o.div_c = make_fastdiv((uint32_t)p);
             set_tables(tw, rt.perm);
         }
-        int wcur = W_;
+        int wcur = W;
         if (!st.direct) {
-            const int n1 = p - 1;
-            const int tw1 = table_twiddle(prog_, (size_t)n1);
-            auto sub = [&](int wsrc) {
-                int s = wsrc, d = (wsrc == W_) ? W2_ : W_;
-                int PP = 1;
-                for (int r : radix_schedule((size_t)n1)) {
-                    Op &o = push(OP_STAGE);
-                    o.radix = r;
-                    o.P = PP;
-                    o.len = n1;
-                    o.nsub = nb;
-                    o.src_base = s;
-                    o.dst_base = d;
-                    o.sub_stride = sh_.ws;
-                    o.div_a = make_fastdiv((uint32_t)(n1 / r));
-                    o.div_b = make_fastdiv((uint32_t)PP);
-                    set_tables(tw1);
-                    std::swap(s, d);
-                    PP *= r;
-                }
-                return s;
-            };
-            wcur = sub(W_);
+            int wother = W2;
+            emit_stages((size_t)(p - 1), st.sub, nb, ws, wcur, wother, at);
             {
                 Op &o = push(OP_MUL);
-                o.len = n1;
-                o.nsub = nb;
+                o.len = p - 1;
+                o.nsub = (int)nb;
                 o.src_base = wcur;
-                o.sub_stride = sh_.ws;
+                o.sub_stride = ws;
                 o.mul = MUL_LUT_N;
                 o.cm = 0;
                 o.em = 1;
-                o.x0_base = X0_;
+                o.x0_base = X0;
                 o.flags = F_SAVE_DC | F_CONJ_OUT;
-                o.div_a = make_fastdiv((uint32_t)n1);
+                o.div_a = make_fastdiv((uint32_t)(p - 1));
                 set_tables(rt.kernel);
             }
-            wcur = sub(wcur);
+            emit_stages((size_t)(p - 1), st.sub, nb, ws, wcur, wother, at);
         }
         {
             Op &o = push(OP_RADER_SCATTER);
             o.radix = p;
             o.P = P;
-            o.len = L_;
-            o.nsub = sh_.G;
-            o.dst_base = other_;
-            o.sub_stride = sh_.ls;
+            o.len = (int)L;
+            o.nsub = (int)nsub;
+            o.dst_base = cur;  // the gathered line buffer is free again
+            o.sub_stride = ls;
             o.w_base = wcur;
-            o.w_stride = sh_.ws;
-            o.x0_base = X0_;
+            o.w_stride = ws;
+            o.x0_base = X0;
             o.flags = st.direct ? F_DIRECT : F_CONJ_IN;
-            o.div_a = make_fastdiv((uint32_t)(L_ / p));
+            o.div_a = make_fastdiv((uint32_t)(L / p));
             o.div_b = make_fastdiv((uint32_t)P);
             o.div_c = make_fastdiv((uint32_t)p);
             set_tables(rt.kernel, -1, rt.ginv);
@@ -591,10 +662,12 @@ class PassBuilder {
     PassShape sh_;
     PassPlan plan_{};
     int nops_ = 0;
-    int A_, B_, W_, W2_, X0_, cur_, other_;
+    int A_, B_, cur_, other_;
+    size_t extra_base_;
 };
 
-static Side make_side(int64_t os, int64_t is, int64_t cs, int64_t es, bool real, int64_t count, int cm, int em) {
+static Side make_side(int64_t os, int64_t is, int64_t cs, int64_t es, bool real, int64_t count, int cm, int em,
+                      int herm = 0) {
     Side s{};
     s.os = os;
     s.is = is;
@@ -604,20 +677,59 @@ static Side make_side(int64_t os, int64_t is, int64_t cs, int64_t es, bool real,
     s.count = (int32_t)std::min<int64_t>(count, INT32_MAX);
     s.cm = cm;
     s.em = em;
+    s.herm = herm;
     return s;
 }
 
 // ---- axis lowering ----------------------------------------------------------------
 
-// Split a smooth length into N1 (columns pass, strided) x N2 (rows pass).
-static bool four_step_split(size_t N, size_t &N1, size_t &N2) {
+// The part of an axis algorithm that applies to a factor n of the axis: the Rader
+// primes dividing n (with the multiplicity they have in n), Stockham otherwise.
+static AxisAlgorithm restrict_algorithm(const AxisAlgorithm &alg, size_t n) {
+    AxisAlgorithm r;
+    r.kind = AlgorithmKind::Stockham;
+    if (alg.kind != AlgorithmKind::Rader) return r;
+    for (const RaderPrimePlan &rp : alg.primes) {
+        size_t m = 0, v = n;
+        while (v % rp.prime == 0) v /= rp.prime, m++;
+        if (!m) continue;
+        RaderPrimePlan c = rp;
+        c.multiplicity = std::min(m, rp.multiplicity);
+        r.primes.push_back(c);
+        r.kind = AlgorithmKind::Rader;
+    }
+    return r;
+}
+
+// Four-step split N = N1 (columns, strided) x N2 (rows) with both factors executable in
+// one CTA; the most balanced such split.
+static bool four_step_split(bool dbl, size_t N, const AxisAlgorithm &alg, size_t &N1, size_t &N2) {
     size_t best = 0;
-    for (size_t d = 2; d * d <= N; d++)
-        if (N % d == 0 && is_kernel_smooth(d) && is_kernel_smooth(N / d)) best = d;
+    double best_score = 1e300;
+    for (size_t d = 2; d * d <= N; d++) {
+        if (N % d) continue;
+        for (int flip = 0; flip < 2; flip++) {
+            const size_t a = flip ? N / d : d, b = N / a;
+            AxisAlgorithm ra = restrict_algorithm(alg, a), rb = restrict_algorithm(alg, b);
+            if (!line_fits_on_chip(dbl, a, &ra, true) || !line_fits_on_chip(dbl, b, &rb, true)) continue;
+            const double score = std::fabs(std::log((double)a) - std::log((double)b)) + (flip ? 1e-9 : 0);
+            if (score < best_score) {
+                best_score = score;
+                best = a;
+            }
+        }
+    }
     if (!best) return false;
     N1 = best;
     N2 = N / best;
     return true;
+}
+
+static size_t small_prime_part(size_t n) {
+    size_t a = 1;
+    for (size_t p : {2, 3, 5, 7, 11, 13})
+        while (n % p == 0) n /= p, a *= p;
+    return a;
 }
 
 // The register kernels are not part of the CPU emulation build (their threads
@@ -632,6 +744,13 @@ static bool reg_kernels_enabled() {
 }
 
 void lower_c2c_axis(Program &prog, const AxisJob &job) {
+    const PlannerTuning *saved_tuning = g_tuning;
+    g_tuning = &job.tuning;
+    struct Restore {
+        const PlannerTuning *t;
+        ~Restore() { g_tuning = t; }
+    } restore{saved_tuning};
+    const bool dbl = prog.is_double;
     const bool inv = job.inverse;
     const size_t N = job.N;
     const AxisAlgorithm *alg = job.alg;
@@ -644,13 +763,12 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     const double scale = job.scale;
     const int fscale = scale != 1.0 ? F_SCALE : 0;
     const size_t out_count = job.out_count ? job.out_count : N;
-    const size_t in_count = job.in_herm ? N / 2 + 1 : N;
-    const int in_len = (int)in_count;
+    const int herm = job.in_herm ? (int)N : 0;
 
     if (N == 1) {
         PassBuilder b(prog, 1, {}, strided, no * S, 4);
-        b.load(1, 0);
-        b.store(1, fscale, MUL_NONE, -1, scale);
+        b.load(1, cin);
+        b.store(1, cout | fscale, MUL_NONE, -1, scale);
         prog.passes.push_back(b.finish(no, S, 1, make_side(job.in_os, 1, 0, S, job.in_real, 1, 0, 1),
                                        make_side(job.out_os, 1, 0, S, job.out_real, 1, 0, 1), job.in_buf, job.in_off,
                                        job.out_buf, job.out_off, "copy"));
@@ -667,7 +785,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
             mode = REG_R2C_FULL;
         else if (job.in_herm && job.out_real && out_count == N && !strided)
             mode = REG_C2R_FULL;
-        const int rv = mode >= 0 ? reg_variant_for(prog.is_double, N, mode, strided) : -1;
+        const int rv = mode >= 0 ? reg_variant_for(dbl, N, mode, strided) : -1;
         if (rv >= 0) {
             PassPlan pp{};
             pp.kernel = KERNEL_REG;
@@ -693,100 +811,182 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         }
     }
 
+    const Side in_line = make_side(job.in_os, 1, 0, S, job.in_real, N, 0, 1, herm);
+    const Side out_line = make_side(job.out_os, 1, 0, S, job.out_real, out_count, 0, 1);
+
     if (alg->kind != AlgorithmKind::Bluestein) {
-        if (line_fits_on_chip(prog.is_double, N, alg, strided)) {
-            PassBuilder b(prog, (int)N, line_stages(N, alg), strided, no * S, 24);
-            b.load(in_len, cin);
-            if (job.in_herm) b.herm_expand((int)N);
+        // one pass: Stockham radices and Rader stages (nested when the convolution is
+        // itself Rader) on chip
+        if (line_fits_on_chip(dbl, N, alg, strided)) {
+            PassBuilder b(prog, (int)N, line_stages(N, alg), strided, no * S, kMaxOps);
+            b.load((int)N, cin);
             b.fft();
             b.store((int)out_count, cout | fscale, MUL_NONE, -1, scale);
-            prog.passes.push_back(b.finish(no, S, 1, make_side(job.in_os, 1, 0, S, job.in_real, in_count, 0, 1),
-                                           make_side(job.out_os, 1, 0, S, job.out_real, out_count, 0, 1), job.in_buf,
-                                           job.in_off, job.out_buf, job.out_off, "stockham"));
+            prog.passes.push_back(b.finish(no, S, 1, in_line, out_line, job.in_buf, job.in_off, job.out_buf,
+                                           job.out_off, alg->kind == AlgorithmKind::Rader ? "rader" : "stockham"));
             return;
         }
-        // four-step through scratch 0: columns (N1, stride N2), then rows (N2)
+        // four-step through scratch 0: columns (N1, stride N2) with the twiddle W_N^{n2 k1}
+        // fused into their store, then rows (N2) with the transposed store
         size_t N1, N2;
-        if (job.in_herm) fail_unsupported("B200 engine: multi-pass Hermitian (C2R full-complex) axis");
-        if (alg->kind == AlgorithmKind::Rader || !four_step_split(N, N1, N2))
-            fail_unsupported("B200 engine: axis too large for one CTA and not four-step decomposable");
-        if (!line_fits_on_chip(prog.is_double, N1, nullptr, true) ||
-            !line_fits_on_chip(prog.is_double, N2, nullptr, true))
-            fail_unsupported("B200 engine: four-step factors exceed on-chip capacity");
-        const int tw = table_twiddle(prog, N);
-        const int64_t scr_os = (int64_t)N * S;
-        prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * N * S));
-        {
-            PassBuilder b(prog, (int)N1, line_stages(N1, nullptr), true, no * S * N2, 8);
-            b.load((int)N1, cin);
-            b.fft();
-            b.store((int)N1, 0, MUL_TWIDDLE_CE, tw);
-            prog.passes.push_back(b.finish(no, S, (int64_t)N2,
-                                           make_side(job.in_os, 1, S, (int64_t)N2 * S, job.in_real, N, 1, (int)N2),
-                                           make_side(scr_os, 1, S, (int64_t)N2 * S, false, N, 1, (int)N2), job.in_buf,
-                                           job.in_off, BUF_SCRATCH0, 0, "four-step columns"));
+        if (four_step_split(dbl, N, *alg, N1, N2)) {
+            const AxisAlgorithm a1 = restrict_algorithm(*alg, N1), a2 = restrict_algorithm(*alg, N2);
+            const int tw = table_twiddle(prog, N);
+            const int64_t scr_os = (int64_t)N * S;
+            prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * N * S));
+            {
+                PassBuilder b(prog, (int)N1, line_stages(N1, &a1), true, no * S * N2, kMaxOps);
+                b.load((int)N1, cin);
+                b.fft();
+                b.store((int)N1, 0, MUL_TWIDDLE_CE, tw);
+                prog.passes.push_back(b.finish(
+                    no, S, (int64_t)N2, make_side(job.in_os, 1, S, (int64_t)N2 * S, job.in_real, N, 1, (int)N2, herm),
+                    make_side(scr_os, 1, S, (int64_t)N2 * S, false, N, 1, (int)N2), job.in_buf, job.in_off,
+                    BUF_SCRATCH0, 0, "four-step columns"));
+            }
+            {
+                PassBuilder b(prog, (int)N2, line_stages(N2, &a2), true, no * S * N1, kMaxOps);
+                b.load((int)N2, 0);
+                b.fft();
+                b.store((int)N2, cout | fscale, MUL_NONE, -1, scale);
+                prog.passes.push_back(
+                    b.finish(no, S, (int64_t)N1, make_side(scr_os, 1, (int64_t)N2 * S, S, false, N, (int)N2, 1),
+                             make_side(job.out_os, 1, S, (int64_t)N1 * S, job.out_real, out_count, 1, (int)N1),
+                             BUF_SCRATCH0, 0, job.out_buf, job.out_off, "four-step rows"));
+            }
+            return;
         }
-        {
-            PassBuilder b(prog, (int)N2, line_stages(N2, nullptr), true, no * S * N1, 8);
-            b.load((int)N2, 0);
-            b.fft();
-            b.store((int)N2, cout | fscale, MUL_NONE, -1, scale);
-            prog.passes.push_back(
-                b.finish(no, S, (int64_t)N1, make_side(scr_os, 1, (int64_t)N2 * S, S, false, N, (int)N2, 1),
-                         make_side(job.out_os, 1, S, (int64_t)N1 * S, job.out_real, out_count, 1, (int)N1),
-                         BUF_SCRATCH0, 0, job.out_buf, job.out_off, "four-step rows"));
+        // pass-level Rader for a prime axis whose convolution does not fit one CTA
+        // (rader_ir.rs:706-1957: gather -> FFT(p-1) -> multiply -> FFT(p-1) -> scatter)
+        if (alg->kind == AlgorithmKind::Rader && alg->primes.size() == 1 && alg->primes[0].prime == N &&
+            alg->primes[0].fft_convolution && !job.in_nested_rader) {
+            const size_t p = N;
+            const RaderPrimePlan &rp = alg->primes[0];
+            RaderTables rt = table_rader(prog, p, rp.generator, true);
+            const AxisAlgorithm nested = plan_axis_algorithm(p - 1, job.tuning);
+            const int64_t Ls = (int64_t)(p + 1);  // [a_0 .. a_{p-2}, x0, A0]
+            const int64_t scr_os = Ls * S;
+            prog.scratch_elems[3] = std::max(prog.scratch_elems[3], (size_t)(no * Ls * S));
+            const Side scr_line = make_side(scr_os, 1, 0, S, false, Ls, 0, 1);
+            {
+                PassBuilder b(prog, (int)Ls, {}, strided, no * S, 4);
+                b.load((int)p, cin);
+                b.permute_gather((int)p, rt.perm);
+                b.store((int)p, 0);
+                prog.passes.push_back(b.finish(no, S, 1, in_line, scr_line, job.in_buf, job.in_off, BUF_SCRATCH3, 0,
+                                               "rader gather"));
+            }
+            AxisJob sub;
+            sub.N = p - 1;
+            sub.alg = &nested;
+            sub.tuning = job.tuning;
+            sub.no = no;
+            sub.S = S;
+            sub.in_buf = sub.out_buf = BUF_SCRATCH3;
+            sub.in_os = sub.out_os = scr_os;
+            sub.in_nested_rader = true;
+            lower_c2c_axis(prog, sub);
+            {
+                PassBuilder b(prog, (int)Ls, {}, strided, no * S, 4);
+                b.load((int)Ls, 0);
+                b.save_dc((int)p);
+                b.mul_region(rt.kernel, F_CONJ_OUT, 0, 1, (int)(p - 1));
+                b.store((int)Ls, 0);
+                prog.passes.push_back(
+                    b.finish(no, S, 1, scr_line, scr_line, BUF_SCRATCH3, 0, BUF_SCRATCH3, 0, "rader multiply"));
+            }
+            lower_c2c_axis(prog, sub);
+            {
+                PassBuilder b(prog, (int)Ls, {}, strided, no * S, 4);
+                b.load((int)Ls, 0);
+                b.permute_scatter((int)p, rt.ginv, F_CONJ_IN | cout | fscale, scale);
+                b.store((int)out_count, 0);
+                prog.passes.push_back(b.finish(no, S, 1, scr_line, out_line, BUF_SCRATCH3, 0, job.out_buf,
+                                               job.out_off, "rader scatter"));
+            }
+            return;
         }
-        return;
+        fail_unsupported("B200 engine: axis too large for one CTA and not four-step decomposable");
     }
 
     // Bluestein (bluestein_ir.rs:436-933): chirp, zero-pad to M, FFT_M, x spectrum, IFFT_M,
     // chirp and take N.  With the conjugation trick the inverse uses the forward chirp.
     const size_t M = alg->convolution_len;
     const int chirp = table_bluestein_chirp(prog, N);
-    const int spec = table_bluestein_spectrum(prog, N, M);
-    if (line_fits_on_chip(prog.is_double, M, nullptr, strided)) {
-        PassBuilder b(prog, (int)M, line_stages(M, nullptr), strided, no * S, 24);
-        if (job.in_herm) {
-            // load the N/2+1 bins and zero-fill the rest of the M-length line, then expand
-            b.load((int)M, cin);
-            b.herm_expand((int)N);
-            b.mul_region(chirp, 0, 0, 1, (int)N);
-        } else {
-            b.load((int)M, cin, MUL_LUT_N, chirp);
-        }
+    if (line_fits_on_chip(dbl, M, nullptr, strided)) {
+        const int spec = table_bluestein_spectrum(prog, N, M);
+        PassBuilder b(prog, (int)M, line_stages(M, nullptr), strided, no * S, kMaxOps);
+        b.load((int)M, cin, MUL_LUT_N, chirp);
         b.fft();
         b.mul_region(spec, F_CONJ_OUT, 0, 1);
         b.fft();
         // store: conj (undo the inner inverse trick), multiply chirp, conj again if inverse
         b.store((int)out_count, F_CONJ_IN | cout | fscale, MUL_LUT_N, chirp, scale);
-        prog.passes.push_back(b.finish(no, S, 1, make_side(job.in_os, 1, 0, S, job.in_real, in_count, 0, 1),
-                                       make_side(job.out_os, 1, 0, S, job.out_real, out_count, 0, 1), job.in_buf,
-                                       job.in_off, job.out_buf, job.out_off, "bluestein fused"));
+        prog.passes.push_back(b.finish(no, S, 1, in_line, out_line, job.in_buf, job.in_off, job.out_buf, job.out_off,
+                                       "bluestein fused"));
         return;
     }
-    if (job.in_herm) fail_unsupported("B200 engine: multi-pass Hermitian (C2R full-complex) Bluestein axis");
+    // f64: when N has small prime factors A (B = N / A), the reference's CPU path splits
+    // them off first and runs Bluestein on B only (reference.rs:60-75); its unreduced-chirp
+    // error is then that of B.  Mirror that structure so the f64 result stays within 1e-13
+    // of it: columns = Bluestein(B) with chirp(B) and the four-step twiddle, rows = FFT(A).
+    const size_t A = small_prime_part(N), B = N / A;
+    if (dbl && A > 1 && B > 1) {
+        const size_t MB = next_smooth_at_least(2 * B - 1, {2, 3, 5, 7});
+        if (line_fits_on_chip(dbl, MB, nullptr, true) && line_fits_on_chip(dbl, A, nullptr, true)) {
+            const int chirpB = table_bluestein_chirp(prog, B);
+            const int specB = table_bluestein_spectrum(prog, B, MB);
+            const int tw = table_twiddle(prog, N);
+            const int64_t scr_os = (int64_t)N * S;
+            prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * N * S));
+            {
+                PassBuilder b(prog, (int)MB, line_stages(MB, nullptr), true, no * S * A, kMaxOps);
+                b.load((int)MB, cin, MUL_LUT_N, chirpB, 1.0, 1);
+                b.fft();
+                b.mul_region(specB, F_CONJ_OUT, 0, 1);
+                b.fft();
+                b.mul_region(chirpB, F_CONJ_IN, 0, 1, (int)B);
+                b.store((int)B, 0, MUL_TWIDDLE_CE, tw);
+                prog.passes.push_back(b.finish(
+                    no, S, (int64_t)A, make_side(job.in_os, 1, S, (int64_t)A * S, job.in_real, N, 1, (int)A, herm),
+                    make_side(scr_os, 1, S, (int64_t)A * S, false, N, 1, (int)A), job.in_buf, job.in_off,
+                    BUF_SCRATCH0, 0, "bluestein(B) columns"));
+            }
+            {
+                PassBuilder b(prog, (int)A, line_stages(A, nullptr), true, no * S * B, kMaxOps);
+                b.load((int)A, 0);
+                b.fft();
+                b.store((int)A, cout | fscale, MUL_NONE, -1, scale);
+                prog.passes.push_back(
+                    b.finish(no, S, (int64_t)B, make_side(scr_os, 1, (int64_t)A * S, S, false, N, (int)A, 1),
+                             make_side(job.out_os, 1, S, (int64_t)B * S, job.out_real, out_count, 1, (int)B),
+                             BUF_SCRATCH0, 0, job.out_buf, job.out_off, "small-prime rows"));
+            }
+            return;
+        }
+    }
     size_t M1, M2;
-    if (!four_step_split(M, M1, M2)) fail_unsupported("B200 engine: Bluestein length not decomposable");
-    if (!line_fits_on_chip(prog.is_double, M1, nullptr, true) || !line_fits_on_chip(prog.is_double, M2, nullptr, true))
-        fail_unsupported("B200 engine: Bluestein four-step factors exceed on-chip capacity");
+    AxisAlgorithm smooth;
+    if (!four_step_split(dbl, M, smooth, M1, M2)) fail_unsupported("B200 engine: Bluestein length not decomposable");
+    const int spec = table_bluestein_spectrum(prog, N, M);
     const int twM = table_twiddle(prog, M);
     const int64_t scr_os = (int64_t)M * S;
     prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * M * S));
     // pass A: columns n2: x[n2 + M2 n1] * chirp (n < N, else 0), FFT over n1, * W_M^{n2 k1}
     {
-        PassBuilder b(prog, (int)M1, line_stages(M1, nullptr), true, no * S * M2, 8);
+        PassBuilder b(prog, (int)M1, line_stages(M1, nullptr), true, no * S * M2, kMaxOps);
         b.load((int)M1, cin, MUL_LUT_N, chirp);
         b.fft();
         b.store((int)M1, 0, MUL_TWIDDLE_CE, twM);
         prog.passes.push_back(b.finish(no, S, (int64_t)M2,
-                                       make_side(job.in_os, 1, S, (int64_t)M2 * S, job.in_real, N, 1, (int)M2),
+                                       make_side(job.in_os, 1, S, (int64_t)M2 * S, job.in_real, N, 1, (int)M2, herm),
                                        make_side(scr_os, 1, S, (int64_t)M2 * S, false, M, 1, (int)M2), job.in_buf,
                                        job.in_off, BUF_SCRATCH0, 0, "bluestein columns"));
     }
     // pass B: rows k1: FFT over n2 -> k2, * spectrum[k1 + M1 k2], inverse FFT over k2 -> n2,
     // * conj(W_M^{n2 k1}), in place in scratch
     {
-        PassBuilder b(prog, (int)M2, line_stages(M2, nullptr), true, no * S * M1, 8);
+        PassBuilder b(prog, (int)M2, line_stages(M2, nullptr), true, no * S * M1, kMaxOps);
         b.load((int)M2, 0);
         b.fft();
         b.mul_region(spec, F_CONJ_OUT, 1, (int)M1);
@@ -799,7 +999,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     }
     // pass C: columns n2: inverse FFT over k1 -> n1, * chirp[n2 + M2 n1], keep n < out_count
     {
-        PassBuilder b(prog, (int)M1, line_stages(M1, nullptr), true, no * S * M2, 8);
+        PassBuilder b(prog, (int)M1, line_stages(M1, nullptr), true, no * S * M2, kMaxOps);
         b.load((int)M1, F_CONJ_OUT);
         b.fft();
         b.store((int)M1, F_CONJ_IN | cout | fscale, MUL_LUT_N, chirp, scale);
@@ -815,9 +1015,23 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
 // one pass when the half-length child runs on chip, otherwise the child transform writes
 // scratch 2 and a post-processing pass produces the bins.  FullComplex: the real line is
 // promoted on load and the complex child keeps the first N/2+1 bins.
+// f64 even-half with a Bluestein child cannot stay within 1e-13 of the reference's CPU
+// path: that path transforms the even and odd samples separately, and Bluestein with the
+// reference's unreduced chirp is not exactly Hermitian-symmetric, so the even-half
+// extraction differs from it at ~1e-12.  Those f64 lines use the full complex transform.
+static bool even_half_usable(const Program &prog, const RealAxisJob &job) {
+    return !(prog.is_double && job.alg->kind == AlgorithmKind::Bluestein);
+}
+
 void lower_r2c_axis(Program &prog, const RealAxisJob &job) {
     const size_t N = job.N;
-    if (!job.full_complex && N % 2 == 0 && N >= 2) {
+    const PlannerTuning *saved = g_tuning;
+    g_tuning = &job.tuning;
+    struct Restore {
+        const PlannerTuning *t;
+        ~Restore() { g_tuning = t; }
+    } restore{saved};
+    if (!job.full_complex && N % 2 == 0 && N >= 2 && even_half_usable(prog, job)) {
         const size_t h = N / 2;
         const int wn = table_twiddle(prog, N);
         const bool fused = job.alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.is_double, h, job.alg, false) &&
@@ -839,6 +1053,7 @@ void lower_r2c_axis(Program &prog, const RealAxisJob &job) {
         AxisJob a;
         a.N = h;
         a.alg = job.alg;
+        a.tuning = job.tuning;
         a.no = job.lines;
         a.in_buf = job.in_buf;
         a.in_off = job.in_off;
@@ -857,7 +1072,15 @@ void lower_r2c_axis(Program &prog, const RealAxisJob &job) {
     }
     AxisJob a;
     a.N = N;
-    a.alg = job.alg;
+    AxisAlgorithm full_alg;
+    if (!job.full_complex) {
+        // even-half was planned (child of length N/2) but is not usable: plan the full length
+        full_alg = plan_axis_algorithm(N, job.tuning);
+        a.alg = &full_alg;
+    } else {
+        a.alg = job.alg;
+    }
+    a.tuning = job.tuning;
     a.no = job.lines;
     a.S = 1;
     a.in_buf = job.in_buf;
@@ -877,7 +1100,13 @@ void lower_r2c_axis(Program &prog, const RealAxisJob &job) {
 // FullComplex: Hermitian expansion on chip, inverse complex transform, real part.
 void lower_c2r_axis(Program &prog, const RealAxisJob &job) {
     const size_t N = job.N;
-    if (!job.full_complex && N % 2 == 0 && N >= 2) {
+    const PlannerTuning *saved = g_tuning;
+    g_tuning = &job.tuning;
+    struct Restore {
+        const PlannerTuning *t;
+        ~Restore() { g_tuning = t; }
+    } restore{saved};
+    if (!job.full_complex && N % 2 == 0 && N >= 2 && even_half_usable(prog, job)) {
         const size_t h = N / 2;
         const int wn = table_twiddle(prog, N);
         const bool fused = job.alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.is_double, h, job.alg, false) &&
@@ -909,6 +1138,7 @@ void lower_c2r_axis(Program &prog, const RealAxisJob &job) {
         AxisJob a;
         a.N = h;
         a.alg = job.alg;
+        a.tuning = job.tuning;
         a.no = job.lines;
         a.inverse = true;
         a.scale = job.normalize ? 1.0 / (double)h : 1.0;
@@ -922,7 +1152,14 @@ void lower_c2r_axis(Program &prog, const RealAxisJob &job) {
     }
     AxisJob a;
     a.N = N;
-    a.alg = job.alg;
+    AxisAlgorithm full_alg;
+    if (!job.full_complex) {
+        full_alg = plan_axis_algorithm(N, job.tuning);
+        a.alg = &full_alg;
+    } else {
+        a.alg = job.alg;
+    }
+    a.tuning = job.tuning;
     a.no = job.lines;
     a.S = 1;
     a.inverse = true;

@@ -20,6 +20,8 @@ struct AxisJob {
     bool in_herm = false;   // input holds N/2+1 Hermitian bins (FullComplex C2R)
     bool out_real = false;  // keep the real part (FullComplex C2R)
     size_t out_count = 0;   // bins stored per line (0: N)
+    PlannerTuning tuning;   // tuning of the plan (nested Rader convolutions are planned with it)
+    bool in_nested_rader = false;  // inside a pass-level Rader convolution
 };
 
 // Real transform of the contiguous axis: lines of N reals <-> N/2+1 complex bins.
@@ -29,6 +31,7 @@ struct RealAxisJob {
     bool normalize = false;
     bool full_complex = false;  // RealFftAlgorithm::FullComplex
     const AxisAlgorithm *alg = nullptr;  // algorithm of the executed complex child
+    PlannerTuning tuning;
     int in_buf = BUF_IN, out_buf = BUF_OUT;
     int64_t in_off = 0, out_off = 0;
 };

@@ -22,6 +22,9 @@ enum OpType : int32_t {
     OP_RADER_GATHER = 7,   // radix-p Rader step: twiddle, generator permutation into the W region
     OP_RADER_SCATTER = 8,  // radix-p Rader step: x0 + convolution -> Stockham output positions
     OP_HERM_EXPAND = 9,    // fill slots N/2+1..N-1 of a Hermitian half spectrum with conj(X[N-k])
+    OP_PERMUTE_GATHER = 10,   // pass-level Rader: dst[m] = src[g^m] (m < p-1), dst[p-1] = src[0]
+    OP_PERMUTE_SCATTER = 11,  // pass-level Rader: dst[g^-m] = x0 + c[m], dst[0] = x0 + A0
+    OP_SAVE_DC = 12,          // line[slot] = line[0] (keeps the convolution's DC term)
 };
 
 enum MulKind : int32_t {
@@ -37,6 +40,7 @@ enum OpFlags : int32_t {
     F_SAVE_DC = 8,    // OP_MUL: copy element 0 of every sub-line into the X0 region (slot 1) first
     F_DIRECT = 16,    // OP_RADER_SCATTER: direct O(p^2) convolution instead of the FFT result
     F_SCALE = 32,     // apply Op::scale
+    F_OWN_INDEX = 64, // LOAD/STORE multiply: table index = c*op.cm + e*op.em (not the side's n)
 };
 
 // Fast unsigned division by a run-time constant (round-up multiply-shift, valid for n < 2^31).
@@ -55,6 +59,9 @@ struct Side {
     int32_t real;
     int32_t count;
     int32_t cm, em;
+    int32_t herm;  // input only: N when the side stores N/2+1 Hermitian bins; logical
+                   // n > N/2 reads bin N-n conjugated (cm must be 0 or 1)
+    int32_t _pad;
 };
 
 struct alignas(16) Op {

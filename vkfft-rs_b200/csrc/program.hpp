@@ -15,8 +15,8 @@
 
 namespace b200fft {
 
-enum BufId : int { BUF_IN = 0, BUF_OUT = 1, BUF_SCRATCH0 = 2, BUF_SCRATCH1 = 3, BUF_SCRATCH2 = 4 };
-constexpr int kScratchBuffers = 3;
+enum BufId : int { BUF_IN = 0, BUF_OUT = 1, BUF_SCRATCH0 = 2, BUF_SCRATCH1 = 3, BUF_SCRATCH2 = 4, BUF_SCRATCH3 = 5 };
+constexpr int kScratchBuffers = 4;
 
 struct HostTable {
     bool is_int = false;
@@ -48,7 +48,7 @@ struct Program {
     std::vector<PassPlan> passes;
     std::vector<HostTable> tables;
     std::map<std::string, int> table_cache;
-    size_t scratch_elems[kScratchBuffers] = {0, 0, 0};  // complex elements of the compute precision
+    size_t scratch_elems[kScratchBuffers] = {0, 0, 0, 0};  // complex elements of the compute precision
     size_t input_elems = 0, output_elems = 0;
     bool input_real = false, output_real = false;
     double algorithmic_flops = 0;  // 5 N log2 N per complex transform (for reports)

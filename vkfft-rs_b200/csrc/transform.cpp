@@ -75,6 +75,7 @@ std::unique_ptr<Transform> build_transform(const FftConfig &config_in, int direc
             job.inverse = inverse;
             job.scale = (inverse && c.normalize_inverse) ? 1.0 / (double)n : 1.0;
             job.in_os = job.out_os = (int64_t)n;
+            job.tuning = c.tuning;
             lower_c2c_axis(prog, job);
             return t;
         }
@@ -104,6 +105,7 @@ std::unique_ptr<Transform> build_transform(const FftConfig &config_in, int direc
             job.in_buf = first ? BUF_IN : BUF_OUT;
             job.out_buf = BUF_OUT;
             job.in_os = job.out_os = (int64_t)(len * inner);
+            job.tuning = c.tuning;
             lower_c2c_axis(prog, job);
             first = false;
         }
@@ -143,6 +145,7 @@ std::unique_ptr<Transform> build_transform(const FftConfig &config_in, int direc
     rj.normalize = !r2c && c.normalize_inverse;
     rj.full_complex = t->real_algorithm == RealAlgorithm::FullComplex;
     rj.alg = &t->children[rank - 1]->axes[0].algorithm;
+    rj.tuning = c.tuning;
 
     t->family = rank == 1 ? B200FFT_FAMILY_REAL : B200FFT_FAMILY_REAL_ND;
     // complex axes on the compact tensor (always strided: the real axis is the last one)
@@ -174,6 +177,7 @@ std::unique_ptr<Transform> build_transform(const FftConfig &config_in, int direc
         job.in_buf = in_buf;
         job.out_buf = out_buf;
         job.in_os = job.out_os = (int64_t)(len * inner);
+        job.tuning = c.tuning;
         lower_c2c_axis(prog, job);
     };
     if (r2c) {
