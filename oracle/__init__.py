@@ -138,3 +138,29 @@ def c2r_nd(x, shape_last, ndim, normalize=False, threads=None):
 
 def next_smooth_at_least(target):
     return int(lib().oracle_next_smooth_at_least(target))
+
+
+def convolve_nd(x, kernel_spectrum, dims, coordinates=1, kernels=1, conjugate_sequence=False,
+                cross_power=False, threads=None):
+    """ND real FFT convolution (NdRealConvolutionIr, convolution_ir.rs:3867-4250): R2C of the
+    ``coordinates`` images, per output system (k, c) the product
+    policy(seq[c]) * kernel[k*C + c] (convolution_ir.rs:36-86; sequence conjugation and
+    cross-power normalisation p / |p| as vulkan.rs:17846-17873 emits it), then a normalised
+    C2R of the K*C systems.  ``kernel_spectrum`` holds K*C compact spectra or one that every
+    system shares."""
+    dims = tuple(dims)
+    C, K = coordinates, kernels
+    seq = r2c_nd(np.asarray(x, dtype=np.float64).reshape((C,) + dims), len(dims), threads=threads)
+    seq = seq.reshape(C, -1)
+    L = seq.shape[1]
+    ker = np.asarray(kernel_spectrum, dtype=np.complex128).reshape(-1, L)
+    out = np.empty((K * C, L), dtype=np.complex128)
+    for k in range(K):
+        for c in range(C):
+            s = np.conj(seq[c]) if conjugate_sequence else seq[c]
+            p = s * (ker[k * C + c] if ker.shape[0] > 1 else ker[0])
+            if cross_power:
+                p = p / np.sqrt(p.real * p.real + p.imag * p.imag)
+            out[k * C + c] = p
+    half = dims[:-1] + (dims[-1] // 2 + 1,)
+    return c2r_nd(out.reshape((K * C,) + half), dims[-1], len(dims), normalize=True, threads=threads)

@@ -51,7 +51,9 @@ static void run_program(const Program &prog, const void *in, void *out) {
     std::vector<std::vector<unsigned char>> tables;
     for (const HostTable &t : prog.tables) {
         std::vector<unsigned char> v(t.bytes(prog.is_double));
-        if (t.is_int) {
+        if (t.is_raw) {
+            std::memcpy(v.data(), t.raw.data(), v.size());
+        } else if (t.is_int) {
             std::memcpy(v.data(), t.i.data(), v.size());
         } else if (prog.is_double) {
             std::memcpy(v.data(), t.c.data(), v.size());
@@ -113,6 +115,37 @@ extern "C" int b200fft_emu_run(const b200fft_config *cfg, int direction, const b
         std::vector<unsigned char> dout(out_need, 0xff);
         run_program(prog, din.data(), dout.data());
         std::memcpy(out, dout.data(), out_need);
+        if (launches) *launches = (int)prog.passes.size();
+        return 0;
+    } catch (const FftError &e) {
+        std::strncpy(errbuf, e.message.c_str(), errlen - 1);
+        errbuf[errlen - 1] = 0;
+        return e.code;
+    }
+}
+
+extern "C" int b200fft_emu_convolution_run(const b200fft_config *cfg, const b200fft_device_profile *dev,
+                                           const void *spectrum, uint64_t copies, const void *in, size_t in_bytes,
+                                           void *out, size_t out_bytes, char *errbuf, size_t errlen, int *launches) {
+    try {
+        DeviceProfile d;
+        d.backend = static_cast<Backend>(dev->backend);
+        d.vendor = static_cast<Vendor>(dev->vendor);
+        d.shared_memory_bytes = dev->shared_memory_bytes;
+        d.shared_memory_pow2_bytes = dev->shared_memory_pow2_bytes;
+        d.max_threads_per_block = dev->max_threads_per_block;
+        for (int i = 0; i < 3; i++) d.max_workgroup_size[i] = dev->max_workgroup_size[i];
+        d.coalesced_memory_bytes = dev->coalesced_memory_bytes;
+        d.supports_f64 = dev->supports_f64;
+        auto c = build_convolution(FftConfig::from_c(*cfg), d, spectrum, copies);
+        const Program &prog = c->prog;
+        const size_t esz = prog.is_double ? 8 : 4;
+        if (in_bytes != prog.input_elems * esz || out_bytes != prog.output_elems * esz)
+            fail_input_length(prog.input_elems, in_bytes / esz);
+        std::vector<unsigned char> din((const unsigned char *)in, (const unsigned char *)in + in_bytes);
+        std::vector<unsigned char> dout(out_bytes, 0xff);
+        run_program(prog, din.data(), dout.data());
+        std::memcpy(out, dout.data(), out_bytes);
         if (launches) *launches = (int)prog.passes.size();
         return 0;
     } catch (const FftError &e) {

@@ -54,6 +54,8 @@ def run(case, V, lib):
         cfg = cfg.with_transform(V.TransformKind.R2C)
         ref = oracle.r2c_nd(x.astype(np.float64), len(dims), threads=4)
         y, n = emulate(V, lib, cfg, V.Direction.FORWARD, dev, x, ref.size, cdt)
+    elif kind == "conv":
+        return run_conv(case, V, lib, dev, cfg, rng, cdt, rdt)
     else:
         x = rng.uniform(-1, 1, shape)
         spec = oracle.r2c_nd(x, len(dims), threads=4).astype(cdt)
@@ -62,6 +64,37 @@ def run(case, V, lib):
                             threads=4)
         y, n = emulate(V, lib, cfg, V.Direction.INVERSE, dev, spec, ref.size, rdt)
     return {"err": rel_l2(y, ref), "launches": n}
+
+
+def run_conv(case, V, lib, dev, cfg, rng, cdt, rdt):
+    import ctypes
+    dims = case["dims"]
+    C, K = case.get("coords", 1), case.get("kernels", 1)
+    copies = case.get("copies", K * C)
+    cfg = (cfg.with_transform(V.TransformKind.R2C).with_convolution(True).with_coordinate_features(C)
+           .with_convolution_kernel_count(K))
+    if case.get("conj"):
+        cfg = cfg.with_convolution_conjugation(1)
+    if case.get("cross"):
+        cfg = cfg.with_cross_power_spectrum_normalization(True)
+    x = rng.uniform(-1, 1, (C,) + tuple(dims)).astype(rdt)
+    L = int(np.prod(dims[:-1])) * (dims[-1] // 2 + 1)
+    ker = (rng.uniform(-1, 1, copies * L) + 1j * rng.uniform(-1, 1, copies * L)).astype(cdt)
+    ref = oracle.convolve_nd(x, ker, dims, C, K, case.get("conj", False), case.get("cross", False), threads=4)
+    out = np.empty(ref.size, dtype=rdt)
+    err = ctypes.create_string_buffer(512)
+    launches = ctypes.c_int(0)
+    fn = lib.b200fft_emu_convolution_run
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p,
+                   ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t,
+                   ctypes.c_void_p]
+    d = dev._c()
+    st = fn(ctypes.addressof(cfg._s), ctypes.addressof(d), ker.ctypes.data, copies, x.ctypes.data, x.nbytes,
+            out.ctypes.data, out.nbytes, err, 512, ctypes.addressof(launches))
+    if st != 0:
+        raise V.VkFftError(st, err.value.decode())
+    return {"err": rel_l2(out, ref), "launches": launches.value}
 
 
 def main():

@@ -49,6 +49,15 @@ CASES = [
     dict(kind="c2c", dims=[4106], batch=1, prec="F64", inverse=True, normalize=True),
     dict(kind="c2c", dims=[17 * 4096], batch=1, prec="F32"),
     dict(kind="c2r", dims=[3, 206], batch=1, prec="F64", normalize=True),
+    # FFT convolution: fused outermost axis (K = 1), K > 1 fan-out, conjugation + cross power,
+    # broadcast kernel, Rader / Bluestein / four-step outer axes
+    dict(kind="conv", dims=[32, 48], batch=1, prec="F32", coords=3),
+    dict(kind="conv", dims=[16, 12, 20], batch=1, prec="F64", coords=2, copies=1),
+    dict(kind="conv", dims=[32, 48], batch=1, prec="F64", coords=2, kernels=3),
+    dict(kind="conv", dims=[30, 34], batch=1, prec="F64", coords=2, conj=True, cross=True),
+    dict(kind="conv", dims=[97, 40], batch=1, prec="F64", coords=1),
+    dict(kind="conv", dims=[4099, 6], batch=1, prec="F32", coords=1),
+    dict(kind="conv", dims=[8192, 6], batch=1, prec="F32", coords=1, kernels=2),
 ]
 
 

@@ -1,0 +1,89 @@
+"""FFT convolution (NdRealConvolutionIr, convolution_ir.rs:3867-4250) on the B200 against
+the oracle's R2C -> policy multiply -> normalised C2R restatement."""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_l2
+
+TOL = {"F32": 2e-6, "F64": 1e-13}
+NP = {"F32": (np.complex64, np.float32), "F64": (np.complex128, np.float64)}
+
+
+def conv_config(V, dims, prec, coords, kernels, conj=False, cross=False):
+    cfg = (V.FftConfig(dims).with_transform(V.TransformKind.R2C).with_precision(V.Precision[prec])
+           .with_convolution(True).with_coordinate_features(coords).with_convolution_kernel_count(kernels))
+    if conj:
+        cfg = cfg.with_convolution_conjugation(V.ConvolutionConjugation.SEQUENCE)
+    if cross:
+        cfg = cfg.with_cross_power_spectrum_normalization(True)
+    return cfg
+
+
+def run_conv(V, ctx, dims, prec, coords=1, kernels=1, copies=None, conj=False, cross=False, seed=0):
+    cdt, rdt = NP[prec]
+    copies = kernels * coords if copies is None else copies
+    rng = np.random.default_rng(seed)
+    L = int(np.prod(dims[:-1])) * (dims[-1] // 2 + 1)
+    ker = (rng.uniform(-1, 1, copies * L) + 1j * rng.uniform(-1, 1, copies * L)).astype(cdt)
+    x = rng.uniform(-1, 1, (coords,) + tuple(dims)).astype(rdt)
+    ir = V.NdRealConvolutionIr.build_from_spectrum(conv_config(V, dims, prec, coords, kernels, conj, cross), ker,
+                                                   ctx.device_profile())
+    y = ctx.execute_nd_real_convolution(ir, x)
+    ref = oracle.convolve_nd(x, ker, dims, coords, kernels, conj, cross)
+    return rel_l2(y, ref)
+
+
+CASES = [
+    dict(dims=[32, 48], prec="F32", coords=3),
+    dict(dims=[32, 48], prec="F64", coords=3),
+    dict(dims=[16, 12, 20], prec="F64", coords=2, copies=1),
+    dict(dims=[32, 48], prec="F32", coords=2, kernels=3),
+    dict(dims=[30, 34], prec="F64", coords=2, conj=True, cross=True),
+    dict(dims=[97, 40], prec="F64"),
+    dict(dims=[4099, 6], prec="F32"),
+    dict(dims=[8192, 6], prec="F32", kernels=2),
+    dict(dims=[256, 256], prec="F32", coords=3),
+    dict(dims=[64, 64, 64], prec="F32", coords=2, conj=True),
+    dict(dims=[1024, 1024], prec="F32"),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES, ids=[str(c) for c in CASES])
+def test_convolution_matches_oracle(V, ctx, case):
+    err = run_conv(V, ctx, **case)
+    assert err <= TOL[case["prec"]], (case, err)
+
+
+@pytest.mark.gpu
+def test_convolution_resident_matches_host(V, ctx):
+    import torch
+    dims, C = [64, 96], 2
+    rng = np.random.default_rng(3)
+    L = 64 * 49
+    ker = (rng.uniform(-1, 1, C * L) + 1j * rng.uniform(-1, 1, C * L)).astype(np.complex64)
+    x = rng.uniform(-1, 1, (C, 64, 96)).astype(np.float32)
+    ir = V.NdRealConvolutionIr.build_from_spectrum(conv_config(V, dims, "F32", C, 1), ker, ctx.device_profile())
+    host = ctx.execute_nd_real_convolution(ir, x)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty(ir.output_elements, dtype=torch.float32, device="cuda")
+    ws = torch.empty(max(ir.workspace_bytes, 1), dtype=torch.uint8, device="cuda")
+    s = torch.cuda.current_stream()
+    ctx.execute_nd_real_convolution_resident(ir, xd.data_ptr(), yd.data_ptr(), ws.data_ptr(), s.cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(yd.cpu().numpy(), host)
+
+
+def test_convolution_build_validation(V):
+    """Builds are host-only: policy errors match the reference's validation."""
+    dev = V.DeviceProfile.generic(V.Backend.CUDA, V.GpuVendor.NVIDIA)
+    ker = np.zeros(32 * 25, dtype=np.complex64)
+    with pytest.raises(V.VkFftError):
+        V.NdRealConvolutionIr.build_from_spectrum(V.FftConfig([32, 48]).with_transform(V.TransformKind.R2C), ker,
+                                                  dev)
+    cfg = conv_config(V, [32, 48], "F32", 2, 1)
+    with pytest.raises(V.VkFftError):  # 3 copies for 2 systems
+        V.NdRealConvolutionIr.build_from_spectrum(cfg, np.zeros(3 * 32 * 25, dtype=np.complex64), dev)
+    ir = V.NdRealConvolutionIr.build_from_spectrum(cfg, np.zeros(2 * 32 * 25, dtype=np.complex64), dev)
+    assert ir.input_elements == 2 * 32 * 48 and ir.output_elements == 2 * 32 * 48

@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 #endif
 
+#include <cmath>
 #include <cstdint>
 
 #include "dft_codelets.cuh"
@@ -79,7 +80,8 @@ struct LineMeta {
     const int64_t *ib;
     const int64_t *ob;
     const int *col;
-    int nl;  // valid lines in this CTA
+    const int *oidx;  // outer index o of each line
+    int nl;           // valid lines in this CTA
 };
 
 constexpr int kLoadUnroll = 8;
@@ -234,7 +236,30 @@ __device__ __forceinline__ void op_mul(const Op &op, cplx<T> *sm, const LineMeta
         const int c = op.cm ? lm.col[s] : 0;
         const int n = c * op.cm + e * op.em;
         if (op.nfull && n >= op.nfull) continue;
-        *ptr = apply_mul(v, op, c, e, n);
+        if (op.om || op.lut_off) {
+            // table index with the outer term (one table copy per outer index)
+            cplx<T> x = v;
+            if (op.flags & F_CONJ_IN) x = cconj(x);
+            cplx<T> w = ld_ro<T>(op.lut, (int64_t)n + (int64_t)lm.oidx[s] * op.om + op.lut_off);
+            if (op.flags & F_CONJ_LUT) w = cconj(w);
+            x = cmul(x, w);
+            if (op.flags & F_NORMALIZE) {
+                const T r = T(1) / sqrt(x.x * x.x + x.y * x.y);
+                x.x *= r;
+                x.y *= r;
+            }
+            if (op.flags & F_CONJ_OUT) x = cconj(x);
+            *ptr = x;
+            continue;
+        }
+        cplx<T> r = apply_mul(v, op, c, e, n);
+        if (op.flags & F_NORMALIZE) {
+            const cplx<T> x = (op.flags & F_CONJ_OUT) ? cconj(r) : r;
+            const T k = T(1) / sqrt(x.x * x.x + x.y * x.y);
+            r.x *= k;
+            r.y *= k;
+        }
+        *ptr = r;
     }
 }
 
@@ -471,7 +496,8 @@ __device__ __forceinline__ LineMeta pass_prologue(const PassParams &p, unsigned 
     int64_t *ib = reinterpret_cast<int64_t *>(smem_raw + p.meta_off);
     int64_t *ob = ib + p.G;
     int *col = reinterpret_cast<int *>(ob + p.G);
-    Op *s_ops = reinterpret_cast<Op *>(col + ((p.G + 3) & ~3));
+    int *oidx = col + ((p.G + 3) & ~3);
+    Op *s_ops = reinterpret_cast<Op *>(oidx + ((p.G + 3) & ~3));
     {
         const int words = p.nops * (int)(sizeof(Op) / sizeof(int4));
         const int4 *src = reinterpret_cast<const int4 *>(&p.ops[0]);
@@ -480,7 +506,7 @@ __device__ __forceinline__ LineMeta pass_prologue(const PassParams &p, unsigned 
     }
     const int64_t l0 = (int64_t)blockIdx.x * p.G;
     const int64_t rem = p.nlines - l0;
-    LineMeta lm{ib, ob, col, (int)(rem < p.G ? rem : p.G)};
+    LineMeta lm{ib, ob, col, oidx, (int)(rem < p.G ? rem : p.G)};
     for (int g = threadIdx.x; g < p.G; g += blockDim.x) {
         int64_t l = l0 + g;
         if (g >= lm.nl) l = l0;  // padding lines: any valid address, never read or written
@@ -491,6 +517,7 @@ __device__ __forceinline__ LineMeta pass_prologue(const PassParams &p, unsigned 
         ib[g] = o * p.in.os + i * p.in.is + c * p.in.cs;
         ob[g] = o * p.out.os + i * p.out.is + c * p.out.cs;
         col[g] = (int)c;
+        oidx[g] = (int)o;
     }
     *ops_out = s_ops;
     return lm;

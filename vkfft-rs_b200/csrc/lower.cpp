@@ -353,7 +353,7 @@ static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bo
         return (data + 15) & ~size_t(15);
     };
     auto bytes_for = [&](int G) {
-        size_t meta = (size_t)G * 16 + (size_t)((G + 3) & ~3) * 4;
+        size_t meta = (size_t)G * 16 + (size_t)((G + 3) & ~3) * 8;
         meta = (meta + 15) & ~size_t(15);
         return data_for(G) + meta + (size_t)nops * sizeof(Op);
     };
@@ -437,8 +437,10 @@ class PassBuilder {
     // the full FFT network of the line (length L_) on the current region
     void fft() { emit_stages((size_t)L_, stages_, (size_t)sh_.G, sh_.ls, cur_, other_, extra_base_); }
 
-    void mul_region(int table, int flags, int cm, int em, int count = 0) {
+    void mul_region(int table, int flags, int cm, int em, int count = 0, int64_t om = 0, int64_t lut_off = 0) {
         Op &o = push(OP_MUL);
+        o.om = om;
+        o.lut_off = lut_off;
         o.nfull = count;
         o.len = L_;
         o.nsub = sh_.G;
@@ -547,7 +549,7 @@ class PassBuilder {
         plan_.grid = (p.nlines + sh_.G - 1) / sh_.G;
         plan_.threads = sh_.threads;
         // shared memory = data regions + per-line metadata + the op program actually emitted
-        size_t meta = (size_t)sh_.G * 16 + (size_t)((sh_.G + 3) & ~3) * 4;
+        size_t meta = (size_t)sh_.G * 16 + (size_t)((sh_.G + 3) & ~3) * 8;
         meta = (meta + 15) & ~size_t(15);
         plan_.smem = sh_.meta_off + meta + (size_t)nops_ * sizeof(Op);
         if (plan_.smem > 232448) fail_resource("B200 FFT pass shared memory", plan_.smem, 232448);
@@ -1173,6 +1175,71 @@ void lower_c2r_axis(Program &prog, const RealAxisJob &job) {
     a.out_os = (int64_t)N;
     a.out_real = true;
     lower_c2c_axis(prog, a);
+}
+
+// Convolution multiply pass (convolution_ir.rs:4235-4246) for K kernels: for every kernel k
+// and coordinate c, out[(k C + c) L + i] = policy(in[c L + i]) * ker[(k C + c) L + i]
+// (ker[i] when one spectrum copy is broadcast).  Lines are chunks of the compact tensor.
+void lower_convolution_multiply(Program &prog, int64_t L, int64_t C, int64_t K, int in_buf, int out_buf,
+                                int spec_table, int64_t spec_copies, bool conj_sequence, bool cross_power) {
+    int64_t chunk = 1;
+    for (int64_t d = std::min<int64_t>(L, 4096); d >= 1; d--)
+        if (L % d == 0) {
+            chunk = d;
+            break;
+        }
+    const int mflags = (conj_sequence ? F_CONJ_IN : 0) | (cross_power ? F_NORMALIZE : 0);
+    const Side side = make_side(L, 0, chunk, 1, false, L, (int)chunk, 1);
+    for (int64_t k = 0; k < K; k++) {
+        PassBuilder b(prog, (int)chunk, {}, false, C * (L / chunk), 4);
+        b.load((int)chunk, 0);
+        b.mul_region(spec_table, mflags, (int)chunk, 1, 0, spec_copies > 1 ? L : 0, spec_copies > 1 ? k * C * L : 0);
+        b.store((int)chunk, 0);
+        prog.passes.push_back(b.finish(C, 1, L / chunk, side, side, in_buf, 0, out_buf, k * C * L, "convolution multiply"));
+    }
+}
+
+// Fused outermost convolution axis (convolution_ir.rs:4185-4250 multiply, here between the
+// forward and the inverse transform of the same lines): forward FFT of length H, multiply by
+// the kernel spectrum ker[o*om + c + e*inner] (policy: sequence conjugation, cross-power
+// normalisation), inverse FFT, scale.  In place on `buf`.
+void lower_convolution_axis0(Program &prog, size_t H, const AxisAlgorithm *alg, const PlannerTuning &tuning,
+                             int64_t systems, int64_t inner, int buf, int spec_table, int64_t spec_outer_stride,
+                             bool conj_sequence, bool cross_power, double scale) {
+    const PlannerTuning *saved = g_tuning;
+    g_tuning = &tuning;
+    struct Restore {
+        const PlannerTuning *t;
+        ~Restore() { g_tuning = t; }
+    } restore{saved};
+    const int mflags = (conj_sequence ? F_CONJ_IN : 0) | (cross_power ? F_NORMALIZE : 0) | F_CONJ_OUT;
+    const Side side = make_side((int64_t)H * inner, 0, 1, inner, false, (int64_t)H * inner, 1, (int)inner);
+    if (alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.is_double, H, alg, true)) {
+        PassBuilder b(prog, (int)H, line_stages(H, alg), true, systems * inner, kMaxOps);
+        b.load((int)H, 0);
+        b.fft();
+        b.mul_region(spec_table, mflags, 1, (int)inner, 0, spec_outer_stride);
+        b.fft();
+        b.store((int)H, F_CONJ_OUT | F_SCALE, MUL_NONE, -1, scale);
+        prog.passes.push_back(b.finish(systems, 1, inner, side, side, buf, 0, buf, 0, "convolution axis fused"));
+        return;
+    }
+    // unfused: forward axis, multiply pass, inverse axis
+    AxisJob job;
+    job.N = H;
+    job.alg = alg;
+    job.tuning = tuning;
+    job.no = systems;
+    job.S = inner;
+    job.in_buf = job.out_buf = buf;
+    job.in_os = job.out_os = (int64_t)H * inner;
+    lower_c2c_axis(prog, job);
+    const int64_t L = (int64_t)H * inner;
+    lower_convolution_multiply(prog, L, systems, 1, buf, buf, spec_table, spec_outer_stride ? systems : 1,
+                               conj_sequence, cross_power);
+    job.inverse = true;
+    job.scale = scale;
+    lower_c2c_axis(prog, job);
 }
 
 }  // namespace b200fft

@@ -41,6 +41,7 @@ enum OpFlags : int32_t {
     F_DIRECT = 16,    // OP_RADER_SCATTER: direct O(p^2) convolution instead of the FFT result
     F_SCALE = 32,     // apply Op::scale
     F_OWN_INDEX = 64, // LOAD/STORE multiply: table index = c*op.cm + e*op.em (not the side's n)
+    F_NORMALIZE = 128,  // OP_MUL: divide the product by its modulus (cross-power spectrum)
 };
 
 // Fast unsigned division by a run-time constant (round-up multiply-shift, valid for n < 2^31).
@@ -87,6 +88,8 @@ struct alignas(16) Op {
     const void *lut2;   // RADER: generator powers (int32) ; R2C/C2R: W_N table
     const void *lut3;   // RADER: inverse generator powers (int32)
     double scale;
+    int64_t om;         // MUL: table index += (line's outer index o) * om
+    int64_t lut_off;    // MUL: table index += lut_off
 };
 
 struct PassParams {

@@ -20,9 +20,14 @@ constexpr int kScratchBuffers = 4;
 
 struct HostTable {
     bool is_int = false;
+    bool is_raw = false;  // already in the pass precision (user-supplied convolution spectra)
     std::vector<std::complex<double>> c;
     std::vector<int32_t> i;
-    size_t bytes(bool dbl) const { return is_int ? i.size() * 4 : c.size() * (dbl ? 16 : 8); }
+    std::vector<unsigned char> raw;
+    size_t bytes(bool dbl) const {
+        if (is_raw) return raw.size();
+        return is_int ? i.size() * 4 : c.size() * (dbl ? 16 : 8);
+    }
 };
 
 enum KernelKind : int { KERNEL_PASS = 0, KERNEL_REG = 1 };

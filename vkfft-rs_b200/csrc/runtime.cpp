@@ -148,7 +148,9 @@ static DeviceTables &ensure_tables(Context *ctx, uint64_t id, const Program &pro
     for (size_t k = 0; k < prog.tables.size(); k++) {
         const HostTable &t = prog.tables[k];
         unsigned char *dst = host.data() + offs[k];
-        if (t.is_int) {
+        if (t.is_raw) {
+            std::memcpy(dst, t.raw.data(), t.raw.size());
+        } else if (t.is_int) {
             std::memcpy(dst, t.i.data(), t.i.size() * 4);
         } else if (prog.is_double) {
             std::memcpy(dst, t.c.data(), t.c.size() * 16);

@@ -665,6 +665,56 @@ class TransformIr:
         return _np_dtype[(self.config.precision, self.output_is_real)]
 
 
+class ConvolutionConjugation(enum.IntEnum):
+    NONE = 0
+    SEQUENCE = 1
+    KERNEL = 2
+
+
+class NdRealConvolutionIr:
+    """convolution_ir.rs:3867-4183 (independent coordinates): build_from_spectrum(config,
+    kernel_spectrum, device).  kernel_spectrum holds K*C copies of the compact R2C spectrum
+    (the reference layout) or one copy broadcast to every coordinate."""
+
+    def __init__(self, handle, config, precision, in_elems, out_elems):
+        self._h = handle
+        self.config = config
+        self.precision = precision
+        self.input_elements = in_elems
+        self.output_elements = out_elems
+
+    @classmethod
+    def build_from_spectrum(cls, config, kernel_spectrum, device):
+        prec = config.precision
+        cdt = np.complex64 if prec == Precision.F32 else np.complex128
+        spec = np.ascontiguousarray(kernel_spectrum, dtype=cdt).ravel()
+        dims = config.dimensions
+        compact = int(np.prod(dims[:-1])) * (dims[-1] // 2 + 1)
+        if spec.size % compact:
+            raise VkFftError(Status.InputLengthMismatch,
+                             f"input contains {spec.size} complex elements but kernel expects a multiple of {compact}")
+        h = ctypes.c_void_p()
+        _check(library().b200fft_convolution_build(ctypes.byref(config._s), ctypes.byref(device._c()),
+                                                   spec.ctypes.data, spec.size // compact, ctypes.byref(h)))
+        c = config._s.coordinate_features
+        k = config._s.convolution_kernel_count
+        full = int(np.prod(dims))
+        return cls(h, config, prec, c * full, k * c * full)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h and _lib is not None:
+            _lib.b200fft_convolution_destroy(h)
+            self._h = None
+
+    @property
+    def workspace_bytes(self):
+        return int(library().b200fft_convolution_workspace_bytes(self._h))
+
+    def real_dtype(self):
+        return np.float32 if self.precision == Precision.F32 else np.float64
+
+
 # ---- backend/cuda/runtime.rs --------------------------------------------------------
 
 def probe():
@@ -719,6 +769,21 @@ class CudaExecutionContext:
 
     def execute_transform_f64(self, ir, data):
         return self.execute_transform(ir, data)
+
+    def execute_nd_real_convolution(self, ir, data, out=None):
+        """execute_nd_real_convolution_f32/f64 (native_runtime.rs:257-337): host arrays."""
+        x = np.ascontiguousarray(data, dtype=ir.real_dtype()).ravel()
+        if out is None:
+            out = np.empty(ir.output_elements, dtype=ir.real_dtype())
+        _check(library().b200fft_execute_convolution_host(self._h, ir._h, x.ctypes.data, x.nbytes,
+                                                          out.ctypes.data, out.nbytes))
+        return out
+
+    def execute_nd_real_convolution_resident(self, ir, input_ptr, output_ptr, workspace_ptr=0, stream=0):
+        _check(library().b200fft_execute_convolution(self._h, ir._h, ctypes.c_void_p(input_ptr),
+                                                     ctypes.c_void_p(output_ptr),
+                                                     ctypes.c_void_p(workspace_ptr or None),
+                                                     ctypes.c_void_p(stream or None)))
 
     def execute_resident(self, ir, input_ptr, output_ptr, workspace_ptr=0, stream=0):
         """Stream-ordered execution on device pointers (resident chain "into" path)."""
