@@ -282,6 +282,26 @@ b200fft_status b200fft_context_device_name(const b200fft_context *context, char 
 b200fft_status b200fft_execute(b200fft_context *context, b200fft_transform *transform,
                                const void *input, void *output, void *workspace, void *stream);
 
+/* Resident execution that allocates nothing.  No counterpart in the reference: it is
+ * an addition of this engine for callers that cannot allocate device memory at call
+ * time -- code running under a framework allocator that has reserved the device's
+ * memory (a cudaMalloc there can fail), and latency-critical loops, where the
+ * implicit device-wide synchronisation of cudaFree stalls other streams.
+ * The transform's tables and scratch live in one library-owned device region of
+ * B200FFT_STATIC_WORKSPACE_BYTES per device; its address is looked up on the first call
+ * on each device.  A transform whose tables plus scratch
+ * (b200fft_transform_workspace_bytes covers the scratch part) exceed the region is
+ * rejected with B200FFT_RESOURCE_LIMIT_EXCEEDED and a message giving both sizes.
+ * Nothing in the region has to start at zero.  The first call on a device, and the
+ * first call after another transform used the region, copy the tables in from host
+ * memory; make the first call before any stream capture.  Calls whose GPU work can
+ * overlap -- on different streams, contexts or threads of one process -- share the
+ * region and race: order them on one stream.  in and out as for b200fft_execute;
+ * stream: a cudaStream_t, or NULL for the context's stream. */
+#define B200FFT_STATIC_WORKSPACE_BYTES (16u << 20)
+b200fft_status b200fft_execute_static_workspace(b200fft_context *context, b200fft_transform *transform,
+                                                const void *input, void *output, void *stream);
+
 /* Host execution with copy semantics: NativeRuntime::execute_transform_f32 / _f64
  * (native_runtime.rs:339-359).  Element type follows the precision (float or double);
  * real transforms take / return real arrays (NativeTransformInput32::Real).  Sizes in

@@ -312,6 +312,18 @@ b200fft_status b200fft_execute(b200fft_context *context, b200fft_transform *tran
     });
 }
 
+b200fft_status b200fft_execute_static_workspace(b200fft_context *context, b200fft_transform *transform,
+                                                const void *input, void *output, void *stream) {
+    return guarded([&] {
+        need(context, "context");
+        need(transform, "transform");
+        need(input, "input");
+        need(output, "output");
+        execute_program_static(context->ctx, transform->t->id, transform->t->prog, input, output,
+                               static_cast<cudaStream_t>(stream));
+    });
+}
+
 b200fft_status b200fft_execute_host(b200fft_context *context, b200fft_transform *transform, const void *input,
                                     size_t input_bytes, void *output, size_t output_bytes) {
     return guarded([&] {

@@ -41,6 +41,9 @@ void forget_program(uint64_t id);  // drop uploaded tables of a destroyed transf
 // Stream-ordered execution of a program on device pointers.
 void execute_program(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out, void *workspace,
                      cudaStream_t stream);
+// Stream-ordered execution out of the library's static device region (allocates nothing).
+void execute_program_static(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out,
+                            cudaStream_t stream);
 // Synchronous host-buffer execution with copy semantics.
 void execute_program_host(Context *ctx, uint64_t id, const Program &prog, const void *in, size_t in_bytes, void *out,
                           size_t out_bytes);

@@ -1,0 +1,130 @@
+// Execution out of a fixed, library-owned device region: the engine of
+// b200fft_execute_static_workspace.  No device memory is allocated or freed here.
+//
+// The region is one file-scope __device__ array.  Its address is looked up once per
+// device with cudaGetSymbolAddress (with that device current) and cached.  A call lays
+// the region out as [packed tables | scratch buffers], uploads the transform's tables
+// when the region last held another transform's tables, and launches the same passes
+// as execute_program.  Nothing in the region has to start at zero: every pass writes
+// each scratch element before a later pass reads it, and the tables are copied in
+// before the first launch that reads them.  The kernels' error word is the context's.
+#include <cstring>
+#include <mutex>
+
+#include "runtime.hpp"
+
+namespace b200fft {
+
+int kernel_variant_for(bool is_double);
+cudaError_t launch_pass(int variant, const PassParams &p, int64_t grid, int threads, size_t smem, cudaStream_t stream);
+cudaError_t launch_reg(int variant, const RegParams &rp, cudaStream_t stream);
+
+constexpr size_t kStaticWorkspaceBytes = size_t(16) << 20;  // B200FFT_STATIC_WORKSPACE_BYTES
+constexpr int kMaxStaticDevices = 64;
+constexpr size_t kMaxStaticTables = 512;
+
+static __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
+
+namespace {
+struct StaticRegion {
+    unsigned char *base = nullptr;  // device address of g_static_workspace on this device
+    uint64_t owner = 0;             // program whose tables the region holds (0: none)
+};
+std::mutex g_static_mu;
+StaticRegion g_static[kMaxStaticDevices];
+unsigned char g_table_image[kStaticWorkspaceBytes];  // host staging of the packed tables
+}  // namespace
+
+static void check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) fail_runtime(std::string(what) + " failed: " + cudaGetErrorString(e));
+}
+
+static size_t round256(size_t v) { return (v + 255) & ~size_t(255); }
+
+void execute_program_static(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out,
+                            cudaStream_t stream) {
+    if (ctx->device < 0 || ctx->device >= kMaxStaticDevices)
+        throw FftError(B200FFT_RESOURCE_LIMIT_EXCEEDED, "static workspace supports CUDA device ordinals below " +
+                                                            std::to_string(kMaxStaticDevices));
+    if (prog.tables.size() > kMaxStaticTables)
+        throw FftError(B200FFT_RESOURCE_LIMIT_EXCEEDED, "static workspace execution supports at most " +
+                                                            std::to_string(kMaxStaticTables) + " tables per transform");
+    size_t table_bytes = 0;
+    for (auto &t : prog.tables) table_bytes += round256(t.bytes(prog.is_double));
+    const size_t scratch_bytes = prog.scratch_bytes();
+    if (table_bytes + scratch_bytes > kStaticWorkspaceBytes)
+        throw FftError(B200FFT_RESOURCE_LIMIT_EXCEEDED,
+                       "static workspace holds " + std::to_string(kStaticWorkspaceBytes) +
+                           " bytes but this transform needs " + std::to_string(table_bytes + scratch_bytes) +
+                           " (tables " + std::to_string(table_bytes) + ", scratch " + std::to_string(scratch_bytes) +
+                           "); execute it with b200fft_execute and a workspace instead");
+    check(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (!stream) stream = ctx->stream;
+    std::lock_guard<std::mutex> g(g_static_mu);
+    StaticRegion &r = g_static[ctx->device];
+    if (!r.base) {
+        void *p = nullptr;
+        check(cudaGetSymbolAddress(&p, g_static_workspace), "cudaGetSymbolAddress of the static workspace");
+        r.base = static_cast<unsigned char *>(p);
+    }
+    const void *tables[kMaxStaticTables];
+    size_t off = 0;
+    for (size_t k = 0; k < prog.tables.size(); k++) {
+        tables[k] = r.base + off;
+        off += round256(prog.tables[k].bytes(prog.is_double));
+    }
+    if (r.owner != id && table_bytes > 0) {
+        // Pack in the pass precision (as the context's table upload does), then one
+        // stream-ordered copy.  The copy is from pageable memory: it has returned only
+        // once the source was consumed, so the staging image can be reused at once.
+        off = 0;
+        for (const HostTable &t : prog.tables) {
+            unsigned char *dst = g_table_image + off;
+            if (t.is_raw) {
+                std::memcpy(dst, t.raw.data(), t.raw.size());
+            } else if (t.is_int) {
+                std::memcpy(dst, t.i.data(), t.i.size() * 4);
+            } else if (prog.is_double) {
+                std::memcpy(dst, t.c.data(), t.c.size() * 16);
+            } else {
+                float *f = reinterpret_cast<float *>(dst);
+                for (size_t m = 0; m < t.c.size(); m++) {
+                    f[2 * m] = (float)t.c[m].real();
+                    f[2 * m + 1] = (float)t.c[m].imag();
+                }
+            }
+            off += round256(t.bytes(prog.is_double));
+        }
+        r.owner = 0;
+        check(cudaMemcpyAsync(r.base, g_table_image, table_bytes, cudaMemcpyHostToDevice, stream),
+              "static workspace table upload");
+    }
+    r.owner = id;
+    unsigned char *scr = r.base + table_bytes;
+    const size_t esz = prog.is_double ? 16 : 8;
+    void *bufs[2 + kScratchBuffers] = {const_cast<void *>(in), out};
+    for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scr + prog.scratch_offset(k);
+    const int variant = kernel_variant_for(prog.is_double);
+    for (const PassPlan &pp : prog.passes) {
+        if (pp.kernel == KERNEL_REG) {
+            RegParams rp = pp.rp;
+            rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * (pp.reg_in_real ? esz / 2 : esz);
+            rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * (pp.reg_out_real ? esz / 2 : esz);
+            rp.tw = tables[pp.reg_table];
+            check(launch_reg(pp.reg_variant, rp, stream), "kernel launch");
+            continue;
+        }
+        PassParams p = pp.p;
+        for (int k = 0; k < p.nops; k++) {
+            const void **slots[3] = {&p.ops[k].lut, &p.ops[k].lut2, &p.ops[k].lut3};
+            for (int s = 0; s < 3; s++) *slots[s] = pp.op_tables[k][s] >= 0 ? tables[pp.op_tables[k][s]] : nullptr;
+        }
+        const size_t in_sz = p.in.real ? esz / 2 : esz, out_sz = p.out.real ? esz / 2 : esz;
+        p.src = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * in_sz;
+        p.dst = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * out_sz;
+        p.err = ctx->d_err;
+        check(launch_pass(variant, p, pp.grid, pp.threads, pp.smem, stream), "kernel launch");
+    }
+}
+
+}  // namespace b200fft

@@ -239,6 +239,7 @@ def library():
         "b200fft_context_device_profile": ([vp, P(_Device)], i32),
         "b200fft_context_device_name": ([vp, ctypes.c_char_p, ctypes.c_size_t], i32),
         "b200fft_execute": ([vp, vp, vp, vp, vp, vp], i32),
+        "b200fft_execute_static_workspace": ([vp, vp, vp, vp, vp], i32),
         "b200fft_execute_host": ([vp, vp, vp, ctypes.c_size_t, vp, ctypes.c_size_t], i32),
         "b200fft_convolution_build": ([P(_Config), P(_Device), vp, u64, P(vp)], i32),
         "b200fft_convolution_destroy": ([vp], None),
@@ -791,6 +792,17 @@ class CudaExecutionContext:
                                          ctypes.c_void_p(output_ptr),
                                          ctypes.c_void_p(workspace_ptr or None),
                                          ctypes.c_void_p(stream or None)))
+
+    def execute_static_workspace(self, ir, input_ptr, output_ptr, stream=0):
+        """b200fft_execute_static_workspace: resident execution that allocates no device
+        memory (tables and scratch in the library's fixed per-device region of
+        STATIC_WORKSPACE_BYTES; calls that overlap on the GPU race)."""
+        _check(library().b200fft_execute_static_workspace(self._h, ir._h, ctypes.c_void_p(input_ptr),
+                                                          ctypes.c_void_p(output_ptr),
+                                                          ctypes.c_void_p(stream or None)))
+
+
+STATIC_WORKSPACE_BYTES = 16 << 20
 
 
 def exported_symbols():
