@@ -274,6 +274,152 @@ def run_ours(args):
     return 0
 
 
+# The other BASELINE configs (config 1, config 2 real, 3, 4, 5) as single-GPU measurement
+# lines: `python bench.py --workload <name>`.  A step is one forward + one normalised
+# inverse transform over the whole workload (one convolution for "conv-2048").  GFLOP/s
+# counts 5 N log2 N per complex transform and 2.5 N log2 N per real one (N = product of
+# the dims); the roofline fraction is the logical bytes (one read + one write of the
+# tensors per direction) over the measured time of the whole transform, so extra passes
+# and scratch round trips show up as a lower fraction.
+REC_TUNING = dict(min_rader_direct_prime=17, max_rader_direct_prime=89, min_rader_fft_prime=17,
+                  max_rader_fft_prime=16384, allow_recursive_fft_rader=True)
+WORKLOADS = {
+    "c2c-1024x8": dict(kind="c2c", dims=[1024], batch=8, prec="F32", config=1),
+    "r2c-4096": dict(kind="r2c", dims=[4096], batch=65536, prec="F32", config=2),
+    "c2c-512^3": dict(kind="c2c", dims=[512, 512, 512], batch=1, prec="F32", config=3),
+    "r2c-1024^3": dict(kind="r2c", dims=[1024, 1024, 1024], batch=1, prec="F32", config=3),
+    "c2c-1024x17x65537-f32": dict(kind="c2c", dims=[1024, 17, 65537], batch=1, prec="F32", config=4),
+    "c2c-1024x17x65537-f64": dict(kind="c2c", dims=[1024, 17, 65537], batch=1, prec="F64", config=4),
+    "c2c-4099-f32": dict(kind="c2c", dims=[4099], batch=16384, prec="F32", config=4),
+    "c2c-4099-f64": dict(kind="c2c", dims=[4099], batch=16384, prec="F64", config=4),
+    "c2c-4099-rader-f32": dict(kind="c2c", dims=[4099], batch=16384, prec="F32", config=4, tuning=REC_TUNING),
+    "c2c-4099-rader-f64": dict(kind="c2c", dims=[4099], batch=16384, prec="F64", config=4, tuning=REC_TUNING),
+    "c2c-65537-f32": dict(kind="c2c", dims=[65537], batch=2048, prec="F32", config=4),
+    "c2c-65537-f64": dict(kind="c2c", dims=[65537], batch=2048, prec="F64", config=4),
+    "conv-2048": dict(kind="conv", dims=[2048, 2048], batch=64, prec="F32", config=5),
+}
+
+
+def gaussian_spectrum(dims, sigma=8.0):
+    """R2C spectrum of a centred Gaussian (sum 1), circularly shifted to the origin (input
+    preparation, untimed)."""
+    h, w = dims
+    yy = np.minimum(np.arange(h), h - np.arange(h))[:, None].astype(np.float64)
+    xx = np.minimum(np.arange(w), w - np.arange(w))[None, :].astype(np.float64)
+    g = np.exp(-(yy * yy + xx * xx) / (2 * sigma * sigma))
+    g /= g.sum()
+    return np.fft.rfft2(g).astype(np.complex64)
+
+
+def run_workload(args):
+    import torch
+    import vkfft_rs as V
+    wl = WORKLOADS[args.workload]
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    ctx = V.CudaExecutionContext(local)
+    dev = ctx.device_profile()
+    kind, dims, batch, prec = wl["kind"], wl["dims"], wl["batch"], wl["prec"]
+    dbl = prec == "F64"
+    tdt = torch.float64 if dbl else torch.float32
+    rsz = 8 if dbl else 4
+    n = int(np.prod(dims))
+    half = int(np.prod(dims[:-1])) * (dims[-1] // 2 + 1)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(wl["config"] + rank)
+    if kind == "conv":
+        cfg = (V.FftConfig(dims).with_transform(V.TransformKind.R2C).with_convolution(True)
+               .with_coordinate_features(batch))
+        conv = V.NdRealConvolutionIr.build_from_spectrum(cfg, gaussian_spectrum(dims), dev)
+        a = torch.rand((batch * n,), device="cuda", generator=gen, dtype=tdt)
+        b = torch.empty_like(a)
+        wsb = torch.empty((max(conv.workspace_bytes, 1),), dtype=torch.uint8, device="cuda")
+        launches = [lambda sp: ctx.execute_nd_real_convolution_resident(conv, a.data_ptr(), b.data_ptr(),
+                                                                        wsb.data_ptr(), sp)]
+        flop = 2 * 2.5 * n * math.log2(n) * batch
+        alg_bytes = [2 * batch * n * rsz + half * 2 * rsz]
+        n_launch = None
+    else:
+        cfg = V.FftConfig(dims).with_batch_count(batch).with_precision(V.Precision[prec])
+        cfg = cfg.with_inverse_normalization(True)
+        if wl.get("tuning"):
+            cfg = cfg.with_tuning(V.PlannerTuning(**wl["tuning"]))
+        if kind == "c2c":
+            fwd = V.TransformIr.build(cfg, V.Direction.FORWARD, dev)
+            inv = V.TransformIr.build(cfg, V.Direction.INVERSE, dev)
+            a = torch.rand((batch * n * 2,), device="cuda", generator=gen, dtype=tdt) * 2 - 1
+            b = torch.empty_like(a)
+            flop = 2 * 5.0 * n * math.log2(n) * batch
+            alg_bytes = [2 * batch * n * 2 * rsz] * 2
+        else:
+            fwd = V.TransformIr.build(cfg.with_transform(V.TransformKind.R2C), V.Direction.FORWARD, dev)
+            inv = V.TransformIr.build(cfg.with_transform(V.TransformKind.C2R), V.Direction.INVERSE, dev)
+            a = torch.rand((batch * n,), device="cuda", generator=gen, dtype=tdt) * 2 - 1
+            b = torch.empty((batch * half * 2,), device="cuda", dtype=tdt)
+            flop = 2 * 2.5 * n * math.log2(n) * batch
+            alg_bytes = [batch * (n * rsz + half * 2 * rsz)] * 2
+        wsb = torch.empty((max(fwd.workspace_bytes, inv.workspace_bytes, 1),), dtype=torch.uint8, device="cuda")
+        launches = [lambda sp: ctx.execute_resident(fwd, a.data_ptr(), b.data_ptr(), wsb.data_ptr(), sp),
+                    lambda sp: ctx.execute_resident(inv, b.data_ptr(), a.data_ptr(), wsb.data_ptr(), sp)]
+        n_launch = fwd.launch_count + inv.launch_count
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = stream.cuda_stream
+    for _ in range(max(args.warmup, 3)):
+        for f in launches:
+            f(sp)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in launches]
+           for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for k in range(args.steps):
+            for j, f in enumerate(launches):
+                evs[k][j][0].record(stream)
+                f(sp)
+                evs[k][j][1].record(stream)
+        torch.cuda.synchronize()
+    part_ms = [statistics.mean(evs[k][j][0].elapsed_time(evs[k][j][1]) for k in range(args.steps))
+               for j in range(len(launches))]
+    ms = sum(part_ms)
+    if dist:
+        t = torch.tensor([ms] + part_ms, device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, part_ms = float(t[0]), [float(v) for v in t[1:]]
+    peak, peak_kind = load_peaks()
+    achieved = [alg_bytes[j] / (part_ms[j] * 1e-3) / 1e9 for j in range(len(launches))]
+    value = flop * ws / (ms * 1e-3) / 1e9
+    line = {
+        "metric": f"{args.workload} GFLOP/s (5N*log2N complex, 2.5N*log2N real)", "value": value, "unit": "GFLOP/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": prec.lower(), "data": "synthetic (torch generator)",
+        "config": {"workload": f"BASELINE config {wl['config']}: {kind} {dims} x batch {batch}"
+                               + (" recursive Rader tuning" if wl.get("tuning") else ""),
+                   "global_batch": batch * ws, "parallelism": f"replicas x{ws}" if ws > 1 else "1 GPU"},
+        "parts_ms": part_ms,
+        "roofline": {"bound": "hbm", "achieved": achieved[0], "peak": peak, "unit": "GB/s",
+                     "frac": achieved[0] / peak, "frac_parts": [x / peak for x in achieved], "traffic": None,
+                     "peak_source": peak_kind, "basis": "logical bytes of the whole transform / its time"},
+        "gpu_launches": None if n_launch is None else args.steps * n_launch,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line))
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    return 0
+
+
 def main():
     global BATCH
     ap = argparse.ArgumentParser()
@@ -284,10 +430,14 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH, help="transforms per rank (profiling runs use fewer)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: resident timing only")
     ap.add_argument("--skip-cpu", action="store_true", help="profiling runs: no CPU baseline")
+    ap.add_argument("--workload", default="c2c-4096", choices=["c2c-4096"] + sorted(WORKLOADS),
+                    help="c2c-4096 is the headline (config 2); the others measure the remaining configs")
     args = ap.parse_args()
     BATCH = args.batch
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "c2c-4096":
+        return run_workload(args)
     return run_ours(args)
 
 
