@@ -286,8 +286,8 @@ REC_TUNING = dict(min_rader_direct_prime=17, max_rader_direct_prime=89, min_rade
 WORKLOADS = {
     "c2c-1024x8": dict(kind="c2c", dims=[1024], batch=8, prec="F32", config=1),
     "r2c-4096": dict(kind="r2c", dims=[4096], batch=65536, prec="F32", config=2),
-    "c2c-512^3": dict(kind="c2c", dims=[512, 512, 512], batch=1, prec="F32", config=3),
-    "r2c-1024^3": dict(kind="r2c", dims=[1024, 1024, 1024], batch=1, prec="F32", config=3),
+    "c2c-512^3": dict(kind="c2c", dims=[512, 512, 512], batch=1, prec="F32", config=3, slab=True),
+    "r2c-1024^3": dict(kind="r2c", dims=[1024, 1024, 1024], batch=1, prec="F32", config=3, slab=True),
     "c2c-1024x17x65537-f32": dict(kind="c2c", dims=[1024, 17, 65537], batch=1, prec="F32", config=4),
     "c2c-1024x17x65537-f64": dict(kind="c2c", dims=[1024, 17, 65537], batch=1, prec="F64", config=4),
     "c2c-4099-f32": dict(kind="c2c", dims=[4099], batch=16384, prec="F32", config=4),
@@ -311,6 +311,86 @@ def gaussian_spectrum(dims, sigma=8.0):
     return np.fft.rfft2(g).astype(np.complex64)
 
 
+def run_slab_workload(args, wl, ctx, dev, dist, ws, rank, local):
+    """3D config under torchrun: one slab-decomposed transform over all ranks (strong
+    scaling).  The exchange runs inside the library (peer stores + device barrier)."""
+    import torch
+    import vkfft_rs as V
+    kind, dims = wl["kind"], wl["dims"]
+    n = int(np.prod(dims))
+    cfg = V.FftConfig(dims).with_precision(V.Precision[wl["prec"]]).with_inverse_normalization(True)
+    real = kind == "r2c"
+    fwd = V.SlabTransform.build(cfg.with_transform(V.TransformKind.R2C) if real else cfg, V.Direction.FORWARD,
+                                ws, rank, dev)
+    inv = V.SlabTransform.build(cfg.with_transform(V.TransformKind.C2R) if real else cfg, V.Direction.INVERSE,
+                                ws, rank, dev)
+    fwd.setup(ctx)
+    inv.setup(ctx)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(wl["config"] + rank)
+    in_scalars = fwd.input_elements * (1 if real else 2)
+    a = torch.rand((in_scalars,), device="cuda", generator=gen) * 2 - 1
+    b = torch.empty((fwd.output_elements * 2,), device="cuda")
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = stream.cuda_stream
+    launches = [lambda: ctx.execute_slab(fwd, a.data_ptr(), b.data_ptr(), stream=sp),
+                lambda: ctx.execute_slab(inv, b.data_ptr(), a.data_ptr(), stream=sp)]
+    for _ in range(max(args.warmup, 3)):
+        for f in launches:
+            f()
+    ctx.synchronize(sp)
+    dist.barrier()
+    torch.cuda.synchronize()
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in launches]
+           for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for k in range(args.steps):
+            for j, f in enumerate(launches):
+                evs[k][j][0].record(stream)
+                f()
+                evs[k][j][1].record(stream)
+        torch.cuda.synchronize()
+    ctx.synchronize(sp)
+    part_ms = [statistics.mean(evs[k][j][0].elapsed_time(evs[k][j][1]) for k in range(args.steps))
+               for j in range(len(launches))]
+    t = torch.tensor([sum(part_ms)] + part_ms, device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, part_ms = float(t[0]), [float(v) for v in t[1:]]
+    flop = 2 * (2.5 if real else 5.0) * n * math.log2(n)
+    value = flop / (ms * 1e-3) / 1e9
+    peak, peak_kind = load_peaks()
+    cplx_local = fwd.output_elements * 8
+    in_local = fwd.input_elements * (4 if real else 8)
+    achieved = (in_local + cplx_local) / (part_ms[0] * 1e-3) / 1e9
+    nvlink_bytes = cplx_local * (ws - 1) / ws  # leaves this GPU per direction
+    line = {
+        "metric": f"{args.workload} GFLOP/s (5N*log2N complex, 2.5N*log2N real), slab over {ws} GPUs",
+        "value": value, "unit": "GFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": wl["prec"].lower(), "data": "synthetic (torch generator)",
+        "config": {"workload": f"BASELINE config {wl['config']}: {kind} {dims}, slab decomposition",
+                   "parallelism": f"slab x{ws} (exchange fused into the last local FFT pass)"},
+        "parts_ms": part_ms,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_source": peak_kind,
+                     "basis": "per-rank logical bytes of the forward transform / its time"},
+        "nvlink": {"bytes_per_direction_per_gpu": nvlink_bytes,
+                   "achieved_gbs": nvlink_bytes / (part_ms[0] * 1e-3) / 1e9, "peak_gbs": 770.0},
+        "gpu_launches": args.steps * (fwd.launch_count + inv.launch_count),
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line))
+    fwd.destroy()
+    inv.destroy()
+    dist.barrier()
+    dist.destroy_process_group()
+    ctx.close()
+    return 0
+
+
 def run_workload(args):
     import torch
     import vkfft_rs as V
@@ -325,6 +405,8 @@ def run_workload(args):
     ctx = V.CudaExecutionContext(local)
     dev = ctx.device_profile()
     kind, dims, batch, prec = wl["kind"], wl["dims"], wl["batch"], wl["prec"]
+    if ws > 1 and wl.get("slab"):
+        return run_slab_workload(args, wl, ctx, dev, dist, ws, rank, local)
     dbl = prec == "F64"
     tdt = torch.float64 if dbl else torch.float32
     rsz = 8 if dbl else 4

@@ -333,6 +333,54 @@ b200fft_status b200fft_execute_convolution_host(b200fft_context *context,
                                                 const void *input, size_t input_bytes, void *output,
                                                 size_t output_bytes);
 
+/* ---- multi-GPU slab decomposition ---------------------------------------
+ * No counterpart in the reference (a single-device crate); the multi-GPU form of
+ * TransformIr::build + execute for rank >= 2 C2C and rank >= 3 R2C / C2R tensors, batch 1,
+ * one process per GPU.  Rank g of P owns planes [g D0/P, (g+1) D0/P) of axis 0.
+ *   forward input  [D0/P, D1, ...]        (real for R2C)
+ *   forward output [D0, D1/P, ...']       axis-1 indices [g D1/P, (g+1) D1/P); the last
+ *                                         axis is compact (N/2+1) for R2C
+ *   inverse input / output: the forward output / input layouts.
+ * D0 and D1 must be divisible by P (at most 8).  The exchange (the all-to-all transpose)
+ * is done by the last FFT pass before it, which stores straight into the owner rank's
+ * exchange buffer through CUDA IPC peer mappings, followed by a device-side barrier with
+ * a bounded wait (b200fft_slab_set_timeout; on expiry the context's error word records
+ * it, see b200fft_context_synchronize).  Set-up per rank: build, attach (allocates the
+ * exchange buffers and returns this rank's handle), gather every rank's handle by any
+ * means (e.g. torch.distributed.all_gather_object), connect.  Every rank must execute
+ * the same sequence of slab calls; a slab must be destroyed before its context. */
+#define B200FFT_SLAB_HANDLE_BYTES 128
+typedef struct b200fft_slab b200fft_slab;
+typedef struct b200fft_slab_info {
+    uint32_t nranks, rank;
+    uint64_t planes_per_rank;   /* D0 / nranks */
+    uint64_t columns_per_rank;  /* D1 / nranks */
+    uint64_t input_elements;    /* per rank, elements of the input's type (float/double or complex) */
+    uint64_t output_elements;
+    int32_t input_is_real, output_is_real;
+    uint64_t exchange_bytes;    /* device memory b200fft_slab_attach allocates */
+    uint32_t launch_count;      /* kernel launches of one execution (barrier included) */
+} b200fft_slab_info;
+b200fft_status b200fft_slab_build(const b200fft_config *config, int32_t direction, uint32_t nranks,
+                                  uint32_t rank, const b200fft_device_profile *device,
+                                  b200fft_slab **slab);
+void b200fft_slab_destroy(b200fft_slab *slab);
+b200fft_status b200fft_slab_get_info(const b200fft_slab *slab, b200fft_slab_info *info);
+b200fft_status b200fft_slab_set_timeout(b200fft_slab *slab, uint64_t timeout_ns);
+/* handle: B200FFT_SLAB_HANDLE_BYTES bytes written for this rank. */
+b200fft_status b200fft_slab_attach(b200fft_context *context, b200fft_slab *slab, void *handle);
+/* handles: nranks consecutive handles, rank order.  Fails if two ranks share a GPU. */
+b200fft_status b200fft_slab_connect(b200fft_context *context, b200fft_slab *slab, const void *handles);
+/* Stream ordered, device pointers; input and output must not overlap.  workspace as for
+ * b200fft_execute (NULL: context-owned scratch). */
+b200fft_status b200fft_execute_slab(b200fft_context *context, b200fft_slab *slab, const void *input,
+                                    void *output, void *workspace, void *stream);
+
+/* Waits for the stream (NULL: the context's) and reports any error the context's kernels
+ * recorded since the last check (bounded waits that expired, invalid programs) as
+ * NativeRuntime, clearing it. */
+b200fft_status b200fft_context_synchronize(b200fft_context *context, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

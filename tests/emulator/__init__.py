@@ -14,6 +14,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "libb200fft_emu.so")
 ASAN = "/usr/lib/x86_64-linux-gnu/libasan.so.8"
+LIBSTDCXX = "/usr/lib/x86_64-linux-gnu/libstdc++.so.6"
 
 
 def build():
@@ -51,7 +52,9 @@ def emulate(V, lib, cfg, direction, device, x, out_elems, out_dtype):
 def run_cases(cases, timeout=900):
     """Run a list of case dicts in a child process with ASan preloaded; returns results."""
     env = dict(os.environ)
-    env["LD_PRELOAD"] = ASAN
+    # libstdc++ after the ASan runtime: its __cxa_throw interceptor needs the real symbol
+    # to be resolvable when the host process (python) does not link libstdc++ itself
+    env["LD_PRELOAD"] = ASAN + " " + LIBSTDCXX
     env["ASAN_OPTIONS"] = "detect_leaks=0:verify_asan_link_order=0:abort_on_error=1"
     proc = subprocess.run([sys.executable, os.path.join(HERE, "runner.py")], input=json.dumps(cases),
                           capture_output=True, text=True, env=env, timeout=timeout)

@@ -38,3 +38,4 @@ inline int atomicOr(int *p, int v) {
     return o;
 }
 inline void __syncthreads() {}
+inline void __threadfence_system() {}

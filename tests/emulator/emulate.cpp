@@ -18,6 +18,7 @@ EmuDim threadIdx, blockIdx, blockDim;
 #include <vector>
 
 #include "../../vkfft-rs_b200/csrc/kernels.cu"
+#include "../../vkfft-rs_b200/csrc/slab.hpp"
 #include "../../vkfft-rs_b200/csrc/transform.hpp"
 
 using namespace b200fft;
@@ -46,7 +47,7 @@ static void emu_launch(const PassParams &p, int64_t grid, int threads, size_t sm
     }
 }
 
-static void run_program(const Program &prog, const void *in, void *out) {
+static void run_program(const Program &prog, const void *in, void *out, const PeerStore *peer = nullptr) {
     const size_t esz = prog.is_double ? 16 : 8;
     std::vector<std::vector<unsigned char>> tables;
     for (const HostTable &t : prog.tables) {
@@ -82,6 +83,11 @@ static void run_program(const Program &prog, const void *in, void *out) {
         p.src = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * in_sz;
         p.dst = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * out_sz;
         p.err = &err;
+        if (pp.peer_scatter) {
+            if (!peer) fail_runtime("exchange pass without peers");
+            p.peer = *peer;
+            p.peer.sub = peer->chunk * pp.peer_es;
+        }
         if (pp.threads > 1024 || pp.smem > 232448) fail_invalid_ir("pass launch exceeds sm_100 limits");
         if (prog.is_double)
             emu_launch<double>(p, pp.grid, pp.threads, pp.smem);
@@ -154,6 +160,54 @@ extern "C" int b200fft_emu_convolution_run(const b200fft_config *cfg, const b200
         return e.code;
     }
 }
+
+// All ranks of a slab transform in one process: every rank's pre program (ending in the
+// exchange pass, which scatters into the ranks' exchange buffers), then every post program.
+extern "C" int b200fft_emu_slab_run(const b200fft_config *cfg, int direction, const b200fft_device_profile *dev,
+                                    int nranks, const void *in, size_t in_bytes_per_rank, void *out,
+                                    size_t out_bytes_per_rank, char *errbuf, size_t errlen, int *launches) {
+    try {
+        DeviceProfile d;
+        d.backend = static_cast<Backend>(dev->backend);
+        d.vendor = static_cast<Vendor>(dev->vendor);
+        d.shared_memory_bytes = dev->shared_memory_bytes;
+        d.shared_memory_pow2_bytes = dev->shared_memory_pow2_bytes;
+        d.max_threads_per_block = dev->max_threads_per_block;
+        for (int i = 0; i < 3; i++) d.max_workgroup_size[i] = dev->max_workgroup_size[i];
+        d.coalesced_memory_bytes = dev->coalesced_memory_bytes;
+        d.supports_f64 = dev->supports_f64;
+        std::vector<std::unique_ptr<Slab>> slabs;
+        for (int r = 0; r < nranks; r++) slabs.push_back(build_slab(FftConfig::from_c(*cfg), direction, nranks, r, d));
+        const Slab &s0 = *slabs[0];
+        const size_t esz = s0.pre.is_double ? 16 : 8;
+        const size_t in_need = s0.input_elems * (s0.input_real ? esz / 2 : esz);
+        const size_t out_need = s0.output_elems * (s0.output_real ? esz / 2 : esz);
+        if (in_bytes_per_rank != in_need || out_bytes_per_rank != out_need) fail_input_length(in_need, in_bytes_per_rank);
+        std::vector<std::vector<unsigned char>> ex(nranks), din(nranks), dout(nranks);
+        for (int r = 0; r < nranks; r++) {
+            ex[r].assign(s0.exchange_elems * esz, 0xff);
+            din[r].assign((const unsigned char *)in + r * in_need, (const unsigned char *)in + (r + 1) * in_need);
+            dout[r].assign(out_need, 0xff);
+        }
+        for (int r = 0; r < nranks; r++) {
+            PeerStore ps = slabs[r]->peer;
+            for (int q = 0; q < nranks; q++) ps.ptr[q] = ex[q].data();
+            run_program(slabs[r]->pre, din[r].data(), dout[r].data(), &ps);
+        }
+        for (int r = 0; r < nranks; r++) run_program(slabs[r]->post, ex[r].data(), dout[r].data());
+        for (int r = 0; r < nranks; r++) std::memcpy((unsigned char *)out + r * out_need, dout[r].data(), out_need);
+        if (launches) *launches = (int)(s0.pre.passes.size() + s0.post.passes.size());
+        return 0;
+    } catch (const FftError &e) {
+        std::strncpy(errbuf, e.message.c_str(), errlen - 1);
+        errbuf[errlen - 1] = 0;
+        return e.code;
+    }
+}
+
+namespace b200fft {
+void release_slab_device(Slab *) {}
+}  // namespace b200fft
 
 // The register-resident kernels are not emulated (their threads exchange data inside
 // one op); the lowering never selects them in this build.

@@ -56,6 +56,8 @@ def run(case, V, lib):
         y, n = emulate(V, lib, cfg, V.Direction.FORWARD, dev, x, ref.size, cdt)
     elif kind == "conv":
         return run_conv(case, V, lib, dev, cfg, rng, cdt, rdt)
+    elif kind == "slab":
+        return run_slab(case, V, lib, dev, cfg, rng, cdt, rdt)
     else:
         x = rng.uniform(-1, 1, shape)
         spec = oracle.r2c_nd(x, len(dims), threads=4).astype(cdt)
@@ -92,6 +94,56 @@ def run_conv(case, V, lib, dev, cfg, rng, cdt, rdt):
     d = dev._c()
     st = fn(ctypes.addressof(cfg._s), ctypes.addressof(d), ker.ctypes.data, copies, x.ctypes.data, x.nbytes,
             out.ctypes.data, out.nbytes, err, 512, ctypes.addressof(launches))
+    if st != 0:
+        raise V.VkFftError(st, err.value.decode())
+    return {"err": rel_l2(out, ref), "launches": launches.value}
+
+
+def slab_case_arrays(case, rng, cdt, rdt):
+    """Global input / expected output of a slab case, split into the per-rank layouts:
+    slabs [D0/P, D1, ...] and pencils [D0, D1/P, ...]."""
+    dims, P, mode = case["dims"], case["nranks"], case["mode"]
+    norm = case.get("normalize", False)
+    D0, D1 = dims[0], dims[1]
+    L0, C1 = D0 // P, D1 // P
+    slabs = lambda a: np.concatenate([a[g * L0:(g + 1) * L0].ravel() for g in range(P)])
+    pencils = lambda a: np.concatenate([a[:, g * C1:(g + 1) * C1].ravel() for g in range(P)])
+    if mode == "c2c":
+        x = rng.uniform(-1, 1, dims) + 1j * rng.uniform(-1, 1, dims)
+        return slabs(x).astype(cdt), pencils(oracle.fft_nd(x, len(dims), threads=4))
+    if mode == "c2c_inv":
+        x = rng.uniform(-1, 1, dims) + 1j * rng.uniform(-1, 1, dims)
+        return pencils(x).astype(cdt), slabs(oracle.fft_nd(x, len(dims), inverse=True, normalize=norm, threads=4))
+    if mode == "r2c":
+        x = rng.uniform(-1, 1, dims)
+        return slabs(x).astype(rdt), pencils(oracle.r2c_nd(x, len(dims), threads=4))
+    x = rng.uniform(-1, 1, dims)
+    spec = oracle.r2c_nd(x, len(dims), threads=4)
+    return (pencils(spec).astype(cdt),
+            slabs(oracle.c2r_nd(spec, dims[-1], len(dims), normalize=norm, threads=4)))
+
+
+def run_slab(case, V, lib, dev, cfg, rng, cdt, rdt):
+    import ctypes
+    mode = case["mode"]
+    direction = V.Direction.INVERSE if mode in ("c2c_inv", "c2r") else V.Direction.FORWARD
+    if mode == "r2c":
+        cfg = cfg.with_transform(V.TransformKind.R2C)
+    elif mode == "c2r":
+        cfg = cfg.with_transform(V.TransformKind.C2R)
+    x, ref = slab_case_arrays(case, rng, cdt, rdt)
+    P = case["nranks"]
+    out_dt = rdt if mode == "c2r" else cdt
+    out = np.empty(ref.size, dtype=out_dt)
+    err = ctypes.create_string_buffer(512)
+    launches = ctypes.c_int(0)
+    fn = lib.b200fft_emu_slab_run
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+                   ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_void_p]
+    d = dev._c()
+    st = fn(ctypes.addressof(cfg._s), int(direction), ctypes.addressof(d), P, x.ctypes.data, x.nbytes // P,
+            out.ctypes.data, out.nbytes // P, err, 512, ctypes.addressof(launches))
     if st != 0:
         raise V.VkFftError(st, err.value.decode())
     return {"err": rel_l2(out, ref), "launches": launches.value}

@@ -58,6 +58,20 @@ CASES = [
     dict(kind="conv", dims=[97, 40], batch=1, prec="F64", coords=1),
     dict(kind="conv", dims=[4099, 6], batch=1, prec="F32", coords=1),
     dict(kind="conv", dims=[8192, 6], batch=1, prec="F32", coords=1, kernels=2),
+    # slab decomposition: every rank's programs, the exchange pass scattering into the
+    # ranks' exchange buffers (all ranks emulated in one process)
+    dict(kind="slab", mode="c2c", dims=[8, 12, 10], batch=1, prec="F64", nranks=2),
+    dict(kind="slab", mode="c2c_inv", dims=[8, 12, 10], batch=1, prec="F64", nranks=4, normalize=True),
+    dict(kind="slab", mode="r2c", dims=[8, 16, 12], batch=1, prec="F64", nranks=4),
+    dict(kind="slab", mode="c2r", dims=[8, 16, 12], batch=1, prec="F64", nranks=2, normalize=True),
+    dict(kind="slab", mode="c2c", dims=[16, 24], batch=1, prec="F32", nranks=8),
+    dict(kind="slab", mode="c2c_inv", dims=[16, 24], batch=1, prec="F32", nranks=2),
+    dict(kind="slab", mode="c2c", dims=[34, 18, 17], batch=1, prec="F64", nranks=2),
+    dict(kind="slab", mode="c2c", dims=[4, 4, 6, 10], batch=1, prec="F64", nranks=2),
+    dict(kind="slab", mode="c2r", dims=[4, 4, 6, 10], batch=1, prec="F64", nranks=2, normalize=True),
+    dict(kind="slab", mode="c2c", dims=[8, 8, 8], batch=1, prec="F64", nranks=1),
+    dict(kind="slab", mode="c2c", dims=[4099 * 2, 4, 3], batch=1, prec="F32", nranks=2),
+    dict(kind="slab", mode="c2c_inv", dims=[4099 * 2, 4, 3], batch=1, prec="F32", nranks=2, normalize=True),
 ]
 
 
@@ -67,7 +81,8 @@ def results():
     return emulator.run_cases(CASES)
 
 
-@pytest.mark.parametrize("i", range(len(CASES)), ids=[f"{c['kind']}-{c['dims']}-{c['prec']}" for c in CASES])
+@pytest.mark.parametrize("i", range(len(CASES)), ids=[f"{c['kind']}{'-' + c['mode'] if 'mode' in c else ''}-{c['dims']}-{c['prec']}"
+                              + (f"-P{c['nranks']}" if "nranks" in c else "") for c in CASES])
 def test_emulated_program_matches_oracle(results, i):
     r = results[i]
     assert "error" not in r, r

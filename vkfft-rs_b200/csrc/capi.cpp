@@ -5,6 +5,7 @@
 #include <memory>
 
 #include "runtime.hpp"
+#include "slab.hpp"
 
 using namespace b200fft;
 
@@ -19,6 +20,9 @@ struct b200fft_context {
 };
 struct b200fft_convolution {
     std::unique_ptr<Convolution> c;
+};
+struct b200fft_slab {
+    std::unique_ptr<Slab> s;
 };
 
 static thread_local std::string g_last_error;
@@ -383,3 +387,80 @@ b200fft_status b200fft_execute_convolution_host(b200fft_context *context, b200ff
 }
 
 }  // extern "C"
+
+b200fft_status b200fft_slab_build(const b200fft_config *config, int32_t direction, uint32_t nranks, uint32_t rank,
+                                  const b200fft_device_profile *device, b200fft_slab **slab) {
+    return guarded([&] {
+        need(config, "config");
+        need(device, "device");
+        need(slab, "slab");
+        if (direction != B200FFT_FORWARD && direction != B200FFT_INVERSE) fail_value_range("direction");
+        auto s = build_slab(FftConfig::from_c(*config), direction, (int)nranks, (int)rank, profile_from_c(*device));
+        *slab = new b200fft_slab{std::move(s)};
+    });
+}
+
+void b200fft_slab_destroy(b200fft_slab *slab) { delete slab; }
+
+b200fft_status b200fft_slab_get_info(const b200fft_slab *slab, b200fft_slab_info *info) {
+    return guarded([&] {
+        need(slab, "slab");
+        need(info, "info");
+        const Slab &s = *slab->s;
+        std::memset(info, 0, sizeof(*info));
+        info->nranks = (uint32_t)s.nranks;
+        info->rank = (uint32_t)s.rank;
+        info->planes_per_rank = s.planes_per_rank;
+        info->columns_per_rank = s.columns_per_rank;
+        info->input_elements = s.input_elems;
+        info->output_elements = s.output_elems;
+        info->input_is_real = s.input_real;
+        info->output_is_real = s.output_real;
+        info->exchange_bytes = 256 + 2 * s.buffer_bytes();
+        info->launch_count = (uint32_t)(s.pre.passes.size() + s.post.passes.size() + 1);
+    });
+}
+
+b200fft_status b200fft_slab_set_timeout(b200fft_slab *slab, uint64_t timeout_ns) {
+    return guarded([&] {
+        need(slab, "slab");
+        if (timeout_ns == 0) fail_value_range("timeout_ns");
+        slab->s->timeout_ns = timeout_ns;
+    });
+}
+
+b200fft_status b200fft_slab_attach(b200fft_context *context, b200fft_slab *slab, void *handle) {
+    return guarded([&] {
+        need(context, "context");
+        need(slab, "slab");
+        need(handle, "handle");
+        slab_attach(context->ctx, slab->s.get(), static_cast<unsigned char *>(handle));
+    });
+}
+
+b200fft_status b200fft_slab_connect(b200fft_context *context, b200fft_slab *slab, const void *handles) {
+    return guarded([&] {
+        need(context, "context");
+        need(slab, "slab");
+        need(handles, "handles");
+        slab_connect(context->ctx, slab->s.get(), static_cast<const unsigned char *>(handles));
+    });
+}
+
+b200fft_status b200fft_execute_slab(b200fft_context *context, b200fft_slab *slab, const void *input, void *output,
+                                    void *workspace, void *stream) {
+    return guarded([&] {
+        need(context, "context");
+        need(slab, "slab");
+        need(input, "input");
+        need(output, "output");
+        execute_slab(context->ctx, slab->s.get(), input, output, workspace, static_cast<cudaStream_t>(stream));
+    });
+}
+
+b200fft_status b200fft_context_synchronize(b200fft_context *context, void *stream) {
+    return guarded([&] {
+        need(context, "context");
+        context_synchronize(context->ctx, static_cast<cudaStream_t>(stream));
+    });
+}

@@ -163,14 +163,22 @@ __device__ __forceinline__ void op_store(const PassParams &p, const Op &op, cons
         if (g < lm.nl && n < s.count) {
             cplx<T> v = sm[op.src_base + g * op.sub_stride + spad(e)];
             v = apply_mul(v, op, c, e, n);
-            const int64_t a = lm.ob[g] + (int64_t)e * s.es;
+            int64_t a = lm.ob[g] + (int64_t)e * s.es;
+            void *dst = p.dst;
+            if (p.peer.n) {
+                const int r = (int)fdiv((uint32_t)n, p.peer.div);
+                dst = p.peer.ptr[r];
+                a += p.peer.off - (int64_t)r * p.peer.sub;
+            }
             if (s.real) {
-                __stcs(reinterpret_cast<T *>(p.dst) + a, v.x);
+                __stcs(reinterpret_cast<T *>(dst) + a, v.x);
             } else {
-                st_data<T>(p.dst, a, v);
+                st_data<T>(dst, a, v);
             }
         }
     }
+    // peer stores are visible system-wide before the rank's exchange signal
+    if (p.peer.n) __threadfence_system();
 }
 
 // One radix-R Stockham stage over nsub sub-lines of length len, src -> dst.

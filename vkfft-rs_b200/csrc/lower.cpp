@@ -757,6 +757,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     const size_t N = job.N;
     const AxisAlgorithm *alg = job.alg;
     const int64_t no = job.no, S = job.S;
+    const int64_t So = job.out_S ? job.out_S : S;  // output element stride
     const bool strided = S > 1;
     // inverse = conj(forward(conj(x))): conjugate the raw input before any multiply of
     // the first load and the final value after every multiply of the last store
@@ -772,7 +773,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         b.load(1, cin);
         b.store(1, cout | fscale, MUL_NONE, -1, scale);
         prog.passes.push_back(b.finish(no, S, 1, make_side(job.in_os, 1, 0, S, job.in_real, 1, 0, 1),
-                                       make_side(job.out_os, 1, 0, S, job.out_real, 1, 0, 1), job.in_buf, job.in_off,
+                                       make_side(job.out_os, 1, 0, So, job.out_real, 1, 0, 1), job.in_buf, job.in_off,
                                        job.out_buf, job.out_off, "copy"));
         return;
     }
@@ -796,7 +797,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
             pp.rp.nlines = no * S;
             pp.rp.ni = S;
             pp.rp.src = RegSide{job.in_os, strided ? 1 : 0, S};
-            pp.rp.dst = RegSide{job.out_os, strided ? 1 : 0, S};
+            pp.rp.dst = RegSide{job.out_os, strided ? 1 : 0, So};
             pp.rp.scale = scale;
             pp.rp.conj = (mode == REG_C2C && inv) ? 1 : 0;
             pp.rp.n = (int32_t)N;
@@ -814,7 +815,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     }
 
     const Side in_line = make_side(job.in_os, 1, 0, S, job.in_real, N, 0, 1, herm);
-    const Side out_line = make_side(job.out_os, 1, 0, S, job.out_real, out_count, 0, 1);
+    const Side out_line = make_side(job.out_os, 1, 0, So, job.out_real, out_count, 0, 1);
 
     if (alg->kind != AlgorithmKind::Bluestein) {
         // one pass: Stockham radices and Rader stages (nested when the convolution is
@@ -853,7 +854,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
                 b.store((int)N2, cout | fscale, MUL_NONE, -1, scale);
                 prog.passes.push_back(
                     b.finish(no, S, (int64_t)N1, make_side(scr_os, 1, (int64_t)N2 * S, S, false, N, (int)N2, 1),
-                             make_side(job.out_os, 1, S, (int64_t)N1 * S, job.out_real, out_count, 1, (int)N1),
+                             make_side(job.out_os, 1, So, (int64_t)N1 * So, job.out_real, out_count, 1, (int)N1),
                              BUF_SCRATCH0, 0, job.out_buf, job.out_off, "four-step rows"));
             }
             return;
@@ -961,7 +962,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
                 b.store((int)A, cout | fscale, MUL_NONE, -1, scale);
                 prog.passes.push_back(
                     b.finish(no, S, (int64_t)B, make_side(scr_os, 1, (int64_t)A * S, S, false, N, (int)A, 1),
-                             make_side(job.out_os, 1, S, (int64_t)B * S, job.out_real, out_count, 1, (int)B),
+                             make_side(job.out_os, 1, So, (int64_t)B * So, job.out_real, out_count, 1, (int)B),
                              BUF_SCRATCH0, 0, job.out_buf, job.out_off, "small-prime rows"));
             }
             return;
@@ -1007,7 +1008,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         b.store((int)M1, F_CONJ_IN | cout | fscale, MUL_LUT_N, chirp, scale);
         prog.passes.push_back(
             b.finish(no, S, (int64_t)M2, make_side(scr_os, 1, S, (int64_t)M2 * S, false, M, 1, (int)M2),
-                     make_side(job.out_os, 1, S, (int64_t)M2 * S, job.out_real, out_count, 1, (int)M2), BUF_SCRATCH0,
+                     make_side(job.out_os, 1, So, (int64_t)M2 * So, job.out_real, out_count, 1, (int)M2), BUF_SCRATCH0,
                      0, job.out_buf, job.out_off, "bluestein columns inverse"));
     }
 }

@@ -22,6 +22,7 @@ struct AxisJob {
     size_t out_count = 0;   // bins stored per line (0: N)
     PlannerTuning tuning;   // tuning of the plan (nested Rader convolutions are planned with it)
     bool in_nested_rader = false;  // inside a pass-level Rader convolution
+    int64_t out_S = 0;      // element stride of the output side (0: S, the input's)
 };
 
 // Real transform of the contiguous axis: lines of N reals <-> N/2+1 complex bins.

@@ -92,6 +92,19 @@ struct alignas(16) Op {
     int64_t lut_off;    // MUL: table index += lut_off
 };
 
+// Peer scatter of a pass's final store (the slab exchange fused into the last local FFT
+// pass): the logical element index n of the axis selects the owner rank r = n / chunk and
+// the element goes to ptr[r] at (local address) - r*sub + off.  n == 0 disables it.
+constexpr int kMaxPeers = 8;
+struct PeerStore {
+    void *ptr[kMaxPeers];
+    int64_t sub;    // chunk * (distance between consecutive logical elements)
+    int64_t off;    // this rank's offset inside every destination block
+    int32_t n;      // number of ranks (0: ordinary store)
+    int32_t chunk;  // logical elements per destination rank
+    FastDiv div;    // chunk
+};
+
 struct PassParams {
     int64_t nlines;   // total number of lines in this launch
     int64_t ni, nc;   // line decomposition
@@ -106,6 +119,7 @@ struct PassParams {
     const void *src;
     void *dst;
     int *err;         // device error word (0 = ok), set instead of trapping
+    PeerStore peer;   // STORE ops: optional scatter into the ranks' exchange buffers
     Op ops[kMaxOps];
 };
 

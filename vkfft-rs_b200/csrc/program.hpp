@@ -42,6 +42,8 @@ struct PassPlan {
     int op_tables[kMaxOps][3];    // table ids per op (lut, lut2, lut3) or -1
     int src_buf = BUF_IN, dst_buf = BUF_OUT;
     int64_t src_off = 0, dst_off = 0;  // element offsets (units of the side's element type)
+    bool peer_scatter = false;    // the final store goes to the ranks' exchange buffers
+    int64_t peer_es = 0;          // output distance between consecutive logical elements
     int64_t grid = 0;
     int threads = 0;
     size_t smem = 0;

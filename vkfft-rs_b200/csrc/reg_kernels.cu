@@ -61,7 +61,14 @@ template <typename T, int N, int MODE>
 __device__ __forceinline__ void store_point(const RegParams &rp, const LineIO &io, int p, cplx<T> y) {
     if (MODE == REG_C2C) {
         const T s = T(rp.scale);
-        st_c<T>(rp.out, io.out_base + (int64_t)p * rp.dst.es, cplx<T>{y.x * s, rp.conj ? -y.y * s : y.y * s});
+        void *dst = rp.out;
+        int64_t a = io.out_base + (int64_t)p * rp.dst.es;
+        if (rp.peer.n) {
+            const int r = (int)((__umulhi((uint32_t)p, rp.peer.div.m) + (uint32_t)p) >> rp.peer.div.s);
+            dst = rp.peer.ptr[r];
+            a += rp.peer.off - (int64_t)r * rp.peer.sub;
+        }
+        st_c<T>(dst, a, cplx<T>{y.x * s, rp.conj ? -y.y * s : y.y * s});
     } else if (MODE == REG_R2C_FULL) {
         if (p <= N / 2) st_c<T>(rp.out, io.out_base + (int64_t)p * rp.dst.es, y);
     } else {
@@ -179,6 +186,8 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
         for (int m = 0; m < E; m++) v[m] = {T(0), T(0)};
     }
     stages<T, N, E, MODE, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
+    // peer stores are visible system-wide before the rank's exchange signal
+    if (MODE == REG_C2C && rp.peer.n) __threadfence_system();
 }
 
 }  // namespace regk

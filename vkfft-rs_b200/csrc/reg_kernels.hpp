@@ -2,6 +2,8 @@
 #pragma once
 #include <cstdint>
 
+#include "pass_desc.hpp"
+
 namespace b200fft {
 
 // Register-kernel data modes.
@@ -27,6 +29,7 @@ struct RegParams {
     double scale;        // applied on store
     int32_t conj;        // inverse: conjugate on load and on store
     int32_t n;
+    PeerStore peer;      // REG_C2C: optional scatter of the output into the ranks' buffers
 };
 
 }  // namespace b200fft

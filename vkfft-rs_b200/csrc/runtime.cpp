@@ -185,7 +185,7 @@ static void *ensure_buffer(void *&buf, size_t &have, size_t need, const char *wh
 }
 
 void execute_program(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out, void *workspace,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, const PeerStore *peer) {
     check(cudaSetDevice(ctx->device), "cudaSetDevice");
     std::lock_guard<std::mutex> l(ctx->mu);
     if (!stream) stream = ctx->stream;
@@ -204,6 +204,11 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
             rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * (pp.reg_in_real ? esz / 2 : esz);
             rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * (pp.reg_out_real ? esz / 2 : esz);
             rp.tw = dt.ptrs[pp.reg_table];
+            if (pp.peer_scatter) {
+                if (!peer) fail_runtime("slab exchange pass launched without the ranks' buffers");
+                rp.peer = *peer;
+                rp.peer.sub = peer->chunk * pp.peer_es;
+            }
             if (injected("launch", g_launch_count)) fail_runtime("kernel launch failed: injected launch fault");
             check(launch_reg(pp.reg_variant, rp, stream), "kernel launch");
             continue;
@@ -217,6 +222,11 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
         p.src = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * in_sz;
         p.dst = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * out_sz;
         p.err = ctx->d_err;
+        if (pp.peer_scatter) {
+            if (!peer) fail_runtime("slab exchange pass launched without the ranks' buffers");
+            p.peer = *peer;
+            p.peer.sub = peer->chunk * pp.peer_es;
+        }
         if (injected("launch", g_launch_count)) fail_runtime("kernel launch failed: injected launch fault");
         check(launch_pass(variant, p, pp.grid, pp.threads, pp.smem, stream), "kernel launch");
     }
@@ -246,6 +256,25 @@ void execute_program_host(Context *ctx, uint64_t id, const Program &prog, const 
         cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream);
         cudaStreamSynchronize(ctx->stream);
         fail_runtime("B200 FFT kernel reported error word " + std::to_string(err));
+    }
+}
+
+static std::string describe_error_word(int err) {
+    std::string m = "B200 FFT kernel reported error word " + std::to_string(err);
+    if (err & 32) m += " (slab exchange barrier timed out: a peer rank did not arrive)";
+    if (err & ~32) m += " (invalid pass program)";
+    return m;
+}
+
+void context_synchronize(Context *ctx, cudaStream_t stream) {
+    check(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (!stream) stream = ctx->stream;
+    check(cudaStreamSynchronize(stream), "stream synchronize");
+    int err = 0;
+    check(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost), "error word read");
+    if (err) {
+        check(cudaMemset(ctx->d_err, 0, sizeof(int)), "error word reset");
+        fail_runtime(describe_error_word(err));
     }
 }
 

@@ -38,12 +38,16 @@ Context *context_create(int device);
 void context_destroy(Context *ctx);
 void forget_program(uint64_t id);  // drop uploaded tables of a destroyed transform from every context
 
-// Stream-ordered execution of a program on device pointers.
+// Stream-ordered execution of a program on device pointers.  peer: the exchange
+// buffers of the ranks for passes marked peer_scatter (slab transforms only).
 void execute_program(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out, void *workspace,
-                     cudaStream_t stream);
+                     cudaStream_t stream, const PeerStore *peer = nullptr);
 // Stream-ordered execution out of the library's static device region (allocates nothing).
 void execute_program_static(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out,
                             cudaStream_t stream);
+// Waits for the stream (null: the context's) and turns a recorded kernel error into
+// a NativeRuntime error (clearing it).
+void context_synchronize(Context *ctx, cudaStream_t stream);
 // Synchronous host-buffer execution with copy semantics.
 void execute_program_host(Context *ctx, uint64_t id, const Program &prog, const void *in, size_t in_bytes, void *out,
                           size_t out_bytes);

@@ -179,6 +179,15 @@ class _RaderPrime(ctypes.Structure):
                 ("convolution_factor_count", u32), ("convolution_factors", u64 * MAX_FACTORS)]
 
 
+class _SlabInfo(ctypes.Structure):
+    _fields_ = [("nranks", u32), ("rank", u32), ("planes_per_rank", u64), ("columns_per_rank", u64),
+                ("input_elements", u64), ("output_elements", u64), ("input_is_real", i32),
+                ("output_is_real", i32), ("exchange_bytes", u64), ("launch_count", u32)]
+
+
+SLAB_HANDLE_BYTES = 128
+
+
 class _AxisInfo(ctypes.Structure):
     _fields_ = [("axis", u64), ("logical_len", u64), ("effective_fft_len", u64),
                 ("estimated_scratch_complex", u64), ("algorithm", i32), ("prime_factor_count", u32),
@@ -246,6 +255,14 @@ def library():
         "b200fft_convolution_workspace_bytes": ([vp], u64),
         "b200fft_execute_convolution": ([vp, vp, vp, vp, vp, vp], i32),
         "b200fft_execute_convolution_host": ([vp, vp, vp, ctypes.c_size_t, vp, ctypes.c_size_t], i32),
+        "b200fft_slab_build": ([P(_Config), i32, u32, u32, P(_Device), P(vp)], i32),
+        "b200fft_slab_destroy": ([vp], None),
+        "b200fft_slab_get_info": ([vp, P(_SlabInfo)], i32),
+        "b200fft_slab_set_timeout": ([vp, u64], i32),
+        "b200fft_slab_attach": ([vp, vp, vp], i32),
+        "b200fft_slab_connect": ([vp, vp, vp], i32),
+        "b200fft_execute_slab": ([vp, vp, vp, vp, vp, vp], i32),
+        "b200fft_context_synchronize": ([vp, vp], i32),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -725,18 +742,103 @@ def probe():
     return n.value
 
 
+class SlabTransform:
+    """Slab-decomposed transform over `nranks` processes, one GPU each (no counterpart in
+    the single-device reference).  Rank g owns planes [g D0/P, (g+1) D0/P) of axis 0;
+    the forward output is the pencil layout [D0, D1/P, ...] holding axis-1 indices
+    [g D1/P, (g+1) D1/P) (compact last axis for R2C); the inverse maps it back.  The
+    all-to-all exchange is fused into the last FFT pass before it (peer stores over
+    NVLink through CUDA IPC) and closed by a device barrier with a bounded wait."""
+
+    def __init__(self, handle, config, direction):
+        self._h = handle
+        self.config = config
+        self.direction = direction
+        self._ctx = None
+        info = _SlabInfo()
+        _check(library().b200fft_slab_get_info(handle, ctypes.byref(info)))
+        self.nranks, self.rank = info.nranks, info.rank
+        self.planes_per_rank, self.columns_per_rank = info.planes_per_rank, info.columns_per_rank
+        self.input_elements, self.output_elements = info.input_elements, info.output_elements
+        self.input_is_real, self.output_is_real = bool(info.input_is_real), bool(info.output_is_real)
+        self.exchange_bytes = info.exchange_bytes
+        self.launch_count = info.launch_count
+
+    @classmethod
+    def build(cls, config, direction, nranks, rank, device):
+        h = ctypes.c_void_p()
+        _check(library().b200fft_slab_build(ctypes.byref(config._s), int(direction), int(nranks), int(rank),
+                                            ctypes.byref(device._c()), ctypes.byref(h)))
+        return cls(h, config, direction)
+
+    def destroy(self):
+        h = getattr(self, "_h", None)
+        if h and _lib is not None:
+            _lib.b200fft_slab_destroy(h)
+            self._h = None
+        if self._ctx is not None:
+            self._ctx._slabs.discard(self)
+            self._ctx = None
+
+    def __del__(self):
+        self.destroy()
+
+    def set_timeout(self, seconds):
+        _check(library().b200fft_slab_set_timeout(self._h, int(seconds * 1e9)))
+
+    def attach(self, ctx):
+        """Allocates the exchange buffers on ctx's device; returns this rank's handle."""
+        buf = ctypes.create_string_buffer(SLAB_HANDLE_BYTES)
+        _check(library().b200fft_slab_attach(ctx._h, self._h, buf))
+        self._ctx = ctx
+        ctx._slabs.add(self)
+        return bytes(buf.raw)
+
+    def connect(self, ctx, handles):
+        blob = b"".join(handles)
+        if len(handles) != self.nranks or len(blob) != self.nranks * SLAB_HANDLE_BYTES:
+            raise VkFftError(Status.ValueOutOfRange, "connect needs one handle per rank")
+        _check(library().b200fft_slab_connect(ctx._h, self._h, blob))
+
+    def setup(self, ctx, group=None):
+        """attach + all_gather_object of the handles over torch.distributed + connect."""
+        import torch.distributed as dist
+        mine = self.attach(ctx)
+        handles = [None] * self.nranks
+        dist.all_gather_object(handles, mine, group=group)
+        self.connect(ctx, handles)
+
+    def element_dtypes(self):
+        real = np.float32 if self.config.precision == Precision.F32 else np.float64
+        cplx = np.complex64 if self.config.precision == Precision.F32 else np.complex128
+        return (real if self.input_is_real else cplx), (real if self.output_is_real else cplx)
+
+
 class CudaExecutionContext:
     """backend/cuda/runtime.rs:959-2840"""
 
     def __init__(self, device_index=0):
         self._h = ctypes.c_void_p()
+        self._slabs = set()
         _check(library().b200fft_context_create(int(device_index), ctypes.byref(self._h)))
         self.device_index = device_index
 
     def close(self):
+        for slab in list(getattr(self, "_slabs", ())):
+            slab.destroy()  # slabs hold device memory and peer mappings of this context
         if getattr(self, "_h", None) and _lib is not None:
             _lib.b200fft_context_destroy(self._h)
             self._h = None
+
+    def execute_slab(self, slab, input_ptr, output_ptr, workspace_ptr=0, stream=0):
+        """Stream-ordered slab execution on device pointers (b200fft_execute_slab)."""
+        _check(library().b200fft_execute_slab(self._h, slab._h, ctypes.c_void_p(input_ptr),
+                                              ctypes.c_void_p(output_ptr), ctypes.c_void_p(workspace_ptr or None),
+                                              ctypes.c_void_p(stream or None)))
+
+    def synchronize(self, stream=0):
+        """Waits for the stream and raises NativeRuntime for errors the kernels recorded."""
+        _check(library().b200fft_context_synchronize(self._h, ctypes.c_void_p(stream or None)))
 
     def __del__(self):
         self.close()
