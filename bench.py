@@ -124,6 +124,25 @@ def cpu_baseline(steps_hint=1, budget_s=12.0):
             "sample": f"{done} forward+inverse pairs of N=4096 (f64 oracle) in {dt:.1f}s"}
 
 
+def live_copy_gbs(stream):
+    """Copy bandwidth of this GPU right now (read + write bytes of a 2 GiB device copy,
+    best of 5): context for the roofline fraction, whose peak is the pool's measured one."""
+    import torch
+    a = torch.empty(1 << 29, dtype=torch.float32, device="cuda")
+    b = torch.empty_like(a)
+    best = None
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        b.copy_(a)
+        e1.record(stream)
+        e1.synchronize()
+        t = e0.elapsed_time(e1)
+        best = t if best is None else min(best, t)
+    del a, b
+    return 2 * (1 << 31) / (best * 1e-3) / 1e9
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -208,10 +227,14 @@ def run_ours(args):
     torch.cuda.synchronize()
     elapsed_ms = ev0.elapsed_time(ev1)
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    rank_ms = [elapsed_ms / args.steps]
     if dist:
         t = torch.tensor([elapsed_ms, fwd_ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms, fwd_ms = float(t[0]), float(t[1])
+        every = [torch.zeros_like(t) for _ in range(ws)]
+        dist.all_gather(every, t)
+        rank_ms = [float(v[0]) / args.steps for v in every]
+        elapsed_ms = max(float(v[0]) for v in every)
+        fwd_ms = max(float(v[1]) for v in every)
     ms_per_step = elapsed_ms / args.steps
     total_transforms = 2 * BATCH * ws
     value = total_transforms * FLOP_PER_TRANSFORM / (ms_per_step * 1e-3) / 1e9
@@ -246,6 +269,7 @@ def run_ours(args):
     bytes_one = BATCH * N * 8
 
     peak, peak_kind = load_peaks()
+    box_copy = live_copy_gbs(stream)
     alg_bytes = 2 * N * BATCH * 8  # one read + one write of the tensor per launch
     achieved = alg_bytes / (fwd_ms * 1e-3) / 1e9
     traffic = load_traffic()
@@ -257,12 +281,13 @@ def run_ours(args):
                    "global_batch": BATCH * ws, "seq_len": N, "parallelism": f"batch-sharded x{ws}",
                    "l2": "inputs (2 GiB per rank) larger than L2; no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "peak_source": peak_kind,
+                     "traffic": traffic, "peak_source": peak_kind, "this_gpu_copy_gbs": box_copy,
                      "kernel": "reg_fft_kernel<float,4096> (register-resident Stockham, one launch per transform direction)"},
         "e2e": None if e2e_value is None else {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": 2 * bytes_one,
                 "d2h_bytes_per_step": 2 * bytes_one, "path": "execute_transform (host arrays, pinned)"},
         "gpu_launches": args.steps * (fwd.launch_count + inv.launch_count),
         "clocks": clk.summary(),
+        "rank_ms_per_step": rank_ms,
     }
     if rank == 0:
         line["cpu_baseline"] = cpu_baseline(1, budget_s=12.0) if (ws == 1 and not args.skip_cpu) else None

@@ -61,14 +61,13 @@ template <typename T, int N, int MODE>
 __device__ __forceinline__ void store_point(const RegParams &rp, const LineIO &io, int p, cplx<T> y) {
     if (MODE == REG_C2C) {
         const T s = T(rp.scale);
-        void *dst = rp.out;
-        int64_t a = io.out_base + (int64_t)p * rp.dst.es;
-        if (rp.peer.n) {
-            const int r = (int)((__umulhi((uint32_t)p, rp.peer.div.m) + (uint32_t)p) >> rp.peer.div.s);
-            dst = rp.peer.ptr[r];
-            a += rp.peer.off - (int64_t)r * rp.peer.sub;
-        }
-        st_c<T>(dst, a, cplx<T>{y.x * s, rp.conj ? -y.y * s : y.y * s});
+        st_c<T>(rp.out, io.out_base + (int64_t)p * rp.dst.es, cplx<T>{y.x * s, rp.conj ? -y.y * s : y.y * s});
+    } else if (MODE == REG_C2C_PEER) {
+        // owner rank r of logical position p; the point lands in r's exchange buffer
+        const T s = T(rp.scale);
+        const int r = (int)((__umulhi((uint32_t)p, rp.peer.div.m) + (uint32_t)p) >> rp.peer.div.s);
+        st_c<T>(rp.peer.ptr[r], io.out_base + (int64_t)p * rp.dst.es + rp.peer.off - (int64_t)r * rp.peer.sub,
+                cplx<T>{y.x * s, rp.conj ? -y.y * s : y.y * s});
     } else if (MODE == REG_R2C_FULL) {
         if (p <= N / 2) st_c<T>(rp.out, io.out_base + (int64_t)p * rp.dst.es, y);
     } else {
@@ -168,7 +167,7 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
 #pragma unroll
         for (int m = 0; m < E; m++) {
             const int p = t + m * TT;
-            if (MODE == REG_C2C) {
+            if (MODE == REG_C2C || MODE == REG_C2C_PEER) {
                 const cplx<T> w = ld_c<T>(rp.in, io.in_base + (int64_t)p * rp.src.es);
                 v[m] = {w.x, rp.conj ? -w.y : w.y};
             } else if (MODE == REG_R2C_FULL) {
@@ -187,7 +186,7 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
     }
     stages<T, N, E, MODE, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
     // peer stores are visible system-wide before the rank's exchange signal
-    if (MODE == REG_C2C && rp.peer.n) __threadfence_system();
+    if (MODE == REG_C2C_PEER) __threadfence_system();
 }
 
 }  // namespace regk
@@ -213,6 +212,16 @@ struct RegVariant {
         RV(T, MODE, false, 1024, 16, 4, 16, 16, 4), RV(T, MODE, false, 2048, 16, 2, 16, 16, 8),          \
         RV(T, MODE, false, 4096, 16, 1, 16, 16, 16), RV(T, MODE, false, 8192, 16, 1, 16, 16, 16, 2)
 
+// strided (higher-axis) lines, the slab exchange twins of the strided C2C variants
+#define RV_STRIDED(T, MODE)                                                                                 \
+    RV(T, MODE, true, 16, 16, 32, 16), RV(T, MODE, true, 32, 16, 32, 16, 2),                               \
+        RV(T, MODE, true, 64, 16, (sizeof(T) == 8 ? 16 : 32), 16, 4),                                        \
+        RV(T, MODE, true, 128, 16, (sizeof(T) == 8 ? 16 : 32), 16, 8), RV(T, MODE, true, 256, 16, 16, 16, 16), \
+        RV(T, MODE, true, 512, 16, (sizeof(T) == 8 ? 8 : 16), 16, 16, 2),                                    \
+        RV(T, MODE, true, 1024, 16, (sizeof(T) == 8 ? 4 : 16), 16, 16, 4),                                   \
+        RV(T, MODE, true, 2048, 16, (sizeof(T) == 8 ? 4 : 8), 16, 16, 8),                                    \
+        RV(T, MODE, true, 4096, 16, (sizeof(T) == 8 ? 2 : 4), 16, 16, 16)
+
 static const RegVariant kRegVariants[] = {
     RV_CONTIG(float, REG_C2C),
     RV_CONTIG(double, REG_C2C),
@@ -220,6 +229,8 @@ static const RegVariant kRegVariants[] = {
     RV_CONTIG(double, REG_R2C_FULL),
     RV_CONTIG(float, REG_C2R_FULL),
     RV_CONTIG(double, REG_C2R_FULL),
+    RV_CONTIG(float, REG_C2C_PEER),
+    RV_CONTIG(double, REG_C2C_PEER),
     // strided (higher-axis) C2C lines: G neighbouring lines per CTA
     RV(float, REG_C2C, true, 16, 16, 32, 16), RV(float, REG_C2C, true, 32, 16, 32, 16, 2),
     RV(float, REG_C2C, true, 64, 16, 32, 16, 4), RV(float, REG_C2C, true, 128, 16, 32, 16, 8),
@@ -231,8 +242,11 @@ static const RegVariant kRegVariants[] = {
     RV(double, REG_C2C, true, 256, 16, 16, 16, 16), RV(double, REG_C2C, true, 512, 16, 8, 16, 16, 2),
     RV(double, REG_C2C, true, 1024, 16, 4, 16, 16, 4), RV(double, REG_C2C, true, 2048, 16, 4, 16, 16, 8),
     RV(double, REG_C2C, true, 4096, 16, 2, 16, 16, 16),
+    RV_STRIDED(float, REG_C2C_PEER),
+    RV_STRIDED(double, REG_C2C_PEER),
 };
 #undef RV_CONTIG
+#undef RV_STRIDED
 #undef RV
 
 int reg_variant_for(bool is_double, size_t n, int mode, bool strided) {
@@ -254,6 +268,13 @@ int reg_variant_radices(int v, int *out) {
 }
 
 int reg_variant_lines_per_cta(int v) { return kRegVariants[v].g; }
+
+// The REG_C2C_PEER twin of a REG_C2C variant (same precision, length and layout), or -1.
+int reg_variant_peer_twin(int v) {
+    const RegVariant &a = kRegVariants[v];
+    if (a.mode != REG_C2C) return -1;
+    return reg_variant_for(a.is_double != 0, (size_t)a.n, REG_C2C_PEER, a.strided != 0);
+}
 
 void set_reg_kernel_smem_limits() {
     static unsigned long long done_mask = 0;

@@ -11,6 +11,7 @@ enum RegMode : int32_t {
     REG_C2C = 0,      // complex in, complex out
     REG_R2C_FULL = 1, // real in (promoted on load), first N/2+1 bins out (RealFftAlgorithm::FullComplex)
     REG_C2R_FULL = 2, // N/2+1 Hermitian bins in (mirrored on load), real part out
+    REG_C2C_PEER = 3, // REG_C2C whose output is scattered into the ranks' exchange buffers (slab)
 };
 
 // Line l = o * ni + i; element p of the line is at o*os + i*is + p*es (units of the
@@ -29,7 +30,7 @@ struct RegParams {
     double scale;        // applied on store
     int32_t conj;        // inverse: conjugate on load and on store
     int32_t n;
-    PeerStore peer;      // REG_C2C: optional scatter of the output into the ranks' buffers
+    PeerStore peer;      // REG_C2C_PEER: the ranks' exchange buffers
 };
 
 }  // namespace b200fft

@@ -27,7 +27,9 @@ void mark_exchange_pass(Program &prog, size_t first, int out_buf) {
     if (pp.dst_buf != out_buf || pp.dst_off != 0) fail_runtime("slab exchange pass does not write the axis output");
     pp.peer_scatter = true;
     if (pp.kernel == KERNEL_REG) {
-        if (pp.reg_out_real) fail_runtime("slab exchange pass must be complex");
+        const int twin = reg_variant_peer_twin(pp.reg_variant);
+        if (twin < 0) fail_runtime("slab exchange pass has no peer-scatter register kernel");
+        pp.reg_variant = twin;
         pp.peer_es = pp.rp.dst.es;
         return;
     }
