@@ -150,6 +150,27 @@ def test_r2c_c2r(V, ctx, dims, batch, prec):
     assert e2 <= TOL[prec], (dims, ir.real_algorithm, e2)
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", ["F32", "F64"])
+@pytest.mark.parametrize("dims,batch", [([4096], 8), ([2048], 4), ([256], 16), ([64, 64], 2), ([32, 16, 128], 1)])
+def test_c2r_of_arbitrary_bins_matches_full_complex(V, ctx, dims, batch, prec):
+    """C2R of bins that are not the spectrum of a real signal (imaginary DC / Nyquist parts,
+    as a convolution product has): a FullComplex plan's result is the real part of the
+    Hermitian expansion (real_ir.rs:1037-1053), whatever kernel computes it."""
+    cdt, rdt = NP[prec]
+    rng = np.random.default_rng(sum(dims))
+    shape = (batch,) + tuple(dims[:-1]) + (dims[-1] // 2 + 1,)
+    bins = (rng.uniform(-1, 1, shape) + 1j * rng.uniform(-1, 1, shape)).astype(cdt)
+    inv = V.TransformIr.build(V.FftConfig(dims).with_batch_count(batch).with_precision(V.Precision[prec])
+                              .with_transform(V.TransformKind.C2R).with_inverse_normalization(True),
+                              V.Direction.INVERSE, ctx.device_profile())
+    if inv.real_algorithm != V.RealFftAlgorithm.FULL_COMPLEX:
+        pytest.skip("even-half plan: the reference's own even-half algebra defines the result")
+    out = ctx.execute_transform(inv, bins)
+    ref = oracle.c2r_nd(bins.astype(np.complex128), dims[-1], len(dims), normalize=True)
+    assert rel_l2(out, ref) <= TOL[prec]
+
+
 def _golden_inputs(kind, n, f32):
     x = np.arange(n, dtype=np.float32 if f32 else np.float64)
     if f32:

@@ -1026,6 +1026,40 @@ static bool even_half_usable(const Program &prog, const RealAxisJob &job) {
     return !(prog.is_double && job.alg->kind == AlgorithmKind::Bluestein);
 }
 
+// Power-of-two rows run the even-half algebra in the register kernel whatever the
+// plan's real algorithm (the planner's FullComplex / EvenHalfSize choice is kept and
+// reported): one read and one write of the tensor and half the butterflies of the
+// FullComplex transform.  R2C: both algorithms are the DFT of the real input.  C2R: the
+// FullComplex result is the real part of the Hermitian expansion, which ignores the
+// imaginary parts of X[0] and X[h]; for a FullComplex plan the kernel drops them, and the
+// even-half algebra then computes the same real inverse DFT.
+static bool lower_real_axis_register(Program &prog, const RealAxisJob &job, bool r2c) {
+    const size_t N = job.N, h = N / 2;
+    if (N % 2 || !is_pow2(h) || !reg_kernels_enabled() || job.in_off || job.out_off) return false;
+    const int rv = reg_variant_for(prog.is_double, h, r2c ? REG_R2C_HALF : REG_C2R_HALF, false);
+    if (rv < 0) return false;
+    PassPlan pp{};
+    pp.kernel = KERNEL_REG;
+    pp.reg_variant = rv;
+    pp.reg_table = table_reg_twiddles(prog, h, rv);
+    pp.reg_table2 = table_twiddle(prog, N);
+    pp.rp.nlines = job.lines;
+    pp.rp.ni = 1;
+    pp.rp.src = RegSide{(int64_t)(r2c ? h : h + 1), 0, 1};
+    pp.rp.dst = RegSide{(int64_t)(r2c ? h + 1 : h), 0, 1};
+    pp.rp.scale = (!r2c && job.normalize) ? 1.0 / (double)h : 1.0;
+    pp.rp.scale2 = (!r2c && job.normalize) ? 0.5 : 1.0;
+    pp.rp.conj = r2c ? 0 : 1;
+    pp.rp.n = (int32_t)h;
+    pp.rp.real_ends = (!r2c && job.full_complex) ? 1 : 0;
+    pp.src_buf = job.in_buf;
+    pp.dst_buf = job.out_buf;
+    pp.label = r2c ? "register r2c even-half" : "register c2r even-half";
+    for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
+    prog.passes.push_back(pp);
+    return true;
+}
+
 void lower_r2c_axis(Program &prog, const RealAxisJob &job) {
     const size_t N = job.N;
     const PlannerTuning *saved = g_tuning;
@@ -1034,6 +1068,7 @@ void lower_r2c_axis(Program &prog, const RealAxisJob &job) {
         const PlannerTuning *t;
         ~Restore() { g_tuning = t; }
     } restore{saved};
+    if (lower_real_axis_register(prog, job, true)) return;
     if (!job.full_complex && N % 2 == 0 && N >= 2 && even_half_usable(prog, job)) {
         const size_t h = N / 2;
         const int wn = table_twiddle(prog, N);
@@ -1109,6 +1144,7 @@ void lower_c2r_axis(Program &prog, const RealAxisJob &job) {
         const PlannerTuning *t;
         ~Restore() { g_tuning = t; }
     } restore{saved};
+    if (lower_real_axis_register(prog, job, false)) return;
     if (!job.full_complex && N % 2 == 0 && N >= 2 && even_half_usable(prog, job)) {
         const size_t h = N / 2;
         const int wn = table_twiddle(prog, N);

@@ -37,6 +37,7 @@ struct PassPlan {
     RegParams rp{};               // KERNEL_REG parameters (pointers patched at launch)
     int reg_variant = -1;
     int reg_table = -1;           // twiddle table id of a KERNEL_REG pass
+    int reg_table2 = -1;          // KERNEL_REG HALF modes: the W_2h table
     bool reg_in_real = false, reg_out_real = false;
     PassParams p{};               // device pointers are patched at upload / launch
     int op_tables[kMaxOps][3];    // table ids per op (lut, lut2, lut3) or -1

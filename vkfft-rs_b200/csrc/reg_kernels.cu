@@ -68,6 +68,10 @@ __device__ __forceinline__ void store_point(const RegParams &rp, const LineIO &i
         const int r = (int)((__umulhi((uint32_t)p, rp.peer.div.m) + (uint32_t)p) >> rp.peer.div.s);
         st_c<T>(rp.peer.ptr[r], io.out_base + (int64_t)p * rp.dst.es + rp.peer.off - (int64_t)r * rp.peer.sub,
                 cplx<T>{y.x * s, rp.conj ? -y.y * s : y.y * s});
+    } else if (MODE == REG_C2R_HALF) {
+        // (x[2p], x[2p+1]) as one complex pair, conjugated back from the inverse trick
+        const T s = T(rp.scale);
+        st_c<T>(rp.out, io.out_base + p, cplx<T>{y.x * s, -y.y * s});
     } else if (MODE == REG_R2C_FULL) {
         if (p <= N / 2) st_c<T>(rp.out, io.out_base + (int64_t)p * rp.dst.es, y);
     } else {
@@ -115,7 +119,12 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
             for (int q = 1; q < R; q++) x[q] = mul(x[q], w[q]);
         }
         dft<R, T>(x);
-        if (LAST) {
+        if (LAST && MODE == REG_R2C_HALF) {
+            // output q of butterfly k sits at position t + (k + q NB) TT: back into v for
+            // the post-processing epilogue
+#pragma unroll
+            for (int q = 0; q < R; q++) v[k + q * NB] = x[q];
+        } else if (LAST) {
             if (io.valid) {
 #pragma unroll
                 for (int q = 0; q < R; q++) store_point<T, N, MODE>(rp, io, b + q * (N / R), x[q]);
@@ -167,9 +176,21 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
 #pragma unroll
         for (int m = 0; m < E; m++) {
             const int p = t + m * TT;
-            if (MODE == REG_C2C || MODE == REG_C2C_PEER) {
+            if (MODE == REG_C2C || MODE == REG_C2C_PEER || MODE == REG_R2C_HALF) {
                 const cplx<T> w = ld_c<T>(rp.in, io.in_base + (int64_t)p * rp.src.es);
                 v[m] = {w.x, rp.conj ? -w.y : w.y};
+            } else if (MODE == REG_C2R_HALF) {
+                // Z[p] = s (X[p] + conj X[h-p] + i conj(W_2h^p) (X[p] - conj X[h-p])), then
+                // conjugated for the inverse-by-forward trick
+                cplx<T> x = ld_c<T>(rp.in, io.in_base + p);
+                cplx<T> mc = ld_c<T>(rp.in, io.in_base + (N - p));
+                if (p == 0 && rp.real_ends) x.y = mc.y = T(0);  // X[0], X[h]
+                const cplx<T> wv = tw_load(reinterpret_cast<const cplx<T> *>(rp.tw2), p);
+                const cplx<T> mm = {mc.x, -mc.y};
+                const cplx<T> d = {x.x - mm.x, x.y - mm.y};
+                const cplx<T> r = mul(cplx<T>{wv.x, -wv.y}, d);
+                const T sc = T(rp.scale2);
+                v[m] = {sc * (x.x + mm.x - r.y), -(sc * (x.y + mm.y + r.x))};
             } else if (MODE == REG_R2C_FULL) {
                 v[m] = {__ldcs(reinterpret_cast<const T *>(rp.in) + io.in_base + (int64_t)p * rp.src.es), T(0)};
             } else {
@@ -187,6 +208,29 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
     stages<T, N, E, MODE, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
     // peer stores are visible system-wide before the rank's exchange signal
     if (MODE == REG_C2C_PEER) __threadfence_system();
+    if (MODE == REG_R2C_HALF) {
+        // X[k] = 1/2 ((Z[k] + conj Z[h-k]) - i W_2h^k (Z[k] - conj Z[h-k])), k = 0..h:
+        // Z[h-k] belongs to another thread, so Z goes through shared memory once
+        __syncthreads();  // the last stage's shared-memory reads are done
+#pragma unroll
+        for (int m = 0; m < E; m++) sline[pad(t + m * TT)] = v[m];
+        __syncthreads();
+        if (io.valid) {
+            const cplx<T> *w2 = reinterpret_cast<const cplx<T> *>(rp.tw2);
+            auto post = [&](cplx<T> a, cplx<T> bc, int kk) {
+                const cplx<T> b = {bc.x, -bc.y};
+                const cplx<T> r = mul(tw_load(w2, kk), cplx<T>{a.x - b.x, a.y - b.y});
+                return cplx<T>{T(0.5) * (a.x + b.x + r.y), T(0.5) * (a.y + b.y - r.x)};
+            };
+#pragma unroll
+            for (int m = 0; m < E; m++) {
+                const int p = t + m * TT;
+                const cplx<T> zk2 = sline[pad((N - p) & (N - 1))];
+                st_c<T>(rp.out, io.out_base + p, post(v[m], zk2, p));
+                if (p == 0) st_c<T>(rp.out, io.out_base + N, post(v[m], v[m], N));
+            }
+        }
+    }
 }
 
 }  // namespace regk
@@ -231,6 +275,10 @@ static const RegVariant kRegVariants[] = {
     RV_CONTIG(double, REG_C2R_FULL),
     RV_CONTIG(float, REG_C2C_PEER),
     RV_CONTIG(double, REG_C2C_PEER),
+    RV_CONTIG(float, REG_R2C_HALF),
+    RV_CONTIG(double, REG_R2C_HALF),
+    RV_CONTIG(float, REG_C2R_HALF),
+    RV_CONTIG(double, REG_C2R_HALF),
     // strided (higher-axis) C2C lines: G neighbouring lines per CTA
     RV(float, REG_C2C, true, 16, 16, 32, 16), RV(float, REG_C2C, true, 32, 16, 32, 16, 2),
     RV(float, REG_C2C, true, 64, 16, 32, 16, 4), RV(float, REG_C2C, true, 128, 16, 32, 16, 8),

@@ -12,6 +12,10 @@ enum RegMode : int32_t {
     REG_R2C_FULL = 1, // real in (promoted on load), first N/2+1 bins out (RealFftAlgorithm::FullComplex)
     REG_C2R_FULL = 2, // N/2+1 Hermitian bins in (mirrored on load), real part out
     REG_C2C_PEER = 3, // REG_C2C whose output is scattered into the ranks' exchange buffers (slab)
+    REG_R2C_HALF = 4, // N = h: 2h reals read as h complex pairs, FFT_h, even-half post-processing
+                      // (real_ir.rs:1002-1013) -> h+1 bins
+    REG_C2R_HALF = 5, // N = h: h+1 bins, even-half pre-processing (real_ir.rs:1087-1100), inverse
+                      // FFT_h -> 2h reals stored as h complex pairs
 };
 
 // Line l = o * ni + i; element p of the line is at o*os + i*is + p*es (units of the
@@ -24,12 +28,17 @@ struct RegParams {
     const void *in;
     void *out;
     const void *tw;      // per-stage transposed twiddle tables (reg_kernels.cu)
+    const void *tw2;     // HALF modes: W_{2h}^k, k = 0..h
     int64_t nlines;      // transforms in this launch
     int64_t ni;          // inner line count (1 for contiguous lines)
     RegSide src, dst;
     double scale;        // applied on store
+    double scale2;       // REG_C2R_HALF: applied by the pre-processing (1/2 when normalised)
     int32_t conj;        // inverse: conjugate on load and on store
     int32_t n;
+    int32_t real_ends;   // REG_C2R_HALF: use only the real parts of X[0] and X[h] (the
+                         // FullComplex C2R result: its real output ignores those imaginary parts)
+    int32_t _pad;
     PeerStore peer;      // REG_C2C_PEER: the ranks' exchange buffers
 };
 

@@ -204,6 +204,7 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
             rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * (pp.reg_in_real ? esz / 2 : esz);
             rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * (pp.reg_out_real ? esz / 2 : esz);
             rp.tw = dt.ptrs[pp.reg_table];
+            rp.tw2 = pp.reg_table2 >= 0 ? dt.ptrs[pp.reg_table2] : nullptr;
             if (pp.peer_scatter) {
                 if (!peer) fail_runtime("slab exchange pass launched without the ranks' buffers");
                 rp.peer = *peer;

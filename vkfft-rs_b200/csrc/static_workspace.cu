@@ -111,6 +111,7 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
             rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * (pp.reg_in_real ? esz / 2 : esz);
             rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * (pp.reg_out_real ? esz / 2 : esz);
             rp.tw = tables[pp.reg_table];
+            rp.tw2 = pp.reg_table2 >= 0 ? tables[pp.reg_table2] : nullptr;
             check(launch_reg(pp.reg_variant, rp, stream), "kernel launch");
             continue;
         }
