@@ -1250,6 +1250,31 @@ void lower_convolution_axis0(Program &prog, size_t H, const AxisAlgorithm *alg, 
         ~Restore() { g_tuning = t; }
     } restore{saved};
     const int mflags = (conj_sequence ? F_CONJ_IN : 0) | (cross_power ? F_NORMALIZE : 0) | F_CONJ_OUT;
+    // power-of-two axis: forward FFT, multiply and inverse FFT in the register kernel
+    if (alg->kind == AlgorithmKind::Stockham && is_pow2(H) && reg_kernels_enabled()) {
+        const int rv = reg_variant_for(prog.is_double, H, REG_CONV, true);
+        if (rv >= 0) {
+            PassPlan pp{};
+            pp.kernel = KERNEL_REG;
+            pp.reg_variant = rv;
+            pp.reg_table = table_reg_twiddles(prog, H, rv);
+            pp.reg_table2 = spec_table;
+            pp.rp.nlines = systems * inner;
+            pp.rp.ni = inner;
+            pp.rp.src = pp.rp.dst = RegSide{(int64_t)H * inner, 1, inner};
+            pp.rp.scale = scale;
+            pp.rp.conj = 1;
+            pp.rp.n = (int32_t)H;
+            pp.rp.conv_flags = mflags;
+            pp.rp.conv_em = inner;
+            pp.rp.conv_om = spec_outer_stride;
+            pp.src_buf = pp.dst_buf = buf;
+            pp.label = "register convolution axis";
+            for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
+            prog.passes.push_back(pp);
+            return;
+        }
+    }
     const Side side = make_side((int64_t)H * inner, 0, 1, inner, false, (int64_t)H * inner, 1, (int)inner);
     if (alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.is_double, H, alg, true)) {
         PassBuilder b(prog, (int)H, line_stages(H, alg), true, systems * inner, kMaxOps);

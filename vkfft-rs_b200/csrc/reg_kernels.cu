@@ -36,7 +36,7 @@ __device__ __forceinline__ int pad(int e) { return e + (e >> 4); }
 template <typename T> __device__ __forceinline__ cplx<T> mul(cplx<T> a, cplx<T> b) {
     return {a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x};
 }
-template <typename T> __device__ __forceinline__ cplx<T> tw_load(const cplx<T> *tw, int idx) {
+template <typename T> __device__ __forceinline__ cplx<T> tw_load(const cplx<T> *tw, int64_t idx) {
     auto v = __ldg(reinterpret_cast<const typename vec2<T>::type *>(tw) + idx);
     return {v.x, v.y};
 }
@@ -119,7 +119,7 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
             for (int q = 1; q < R; q++) x[q] = mul(x[q], w[q]);
         }
         dft<R, T>(x);
-        if (LAST && MODE == REG_R2C_HALF) {
+        if (LAST && (MODE == REG_R2C_HALF || MODE == REG_CONV)) {
             // output q of butterfly k sits at position t + (k + q NB) TT: back into v for
             // the post-processing epilogue
 #pragma unroll
@@ -176,7 +176,9 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
 #pragma unroll
         for (int m = 0; m < E; m++) {
             const int p = t + m * TT;
-            if (MODE == REG_C2C || MODE == REG_C2C_PEER || MODE == REG_R2C_HALF) {
+            if (MODE == REG_CONV) {
+                v[m] = ld_c<T>(rp.in, io.in_base + (int64_t)p * rp.src.es);
+            } else if (MODE == REG_C2C || MODE == REG_C2C_PEER || MODE == REG_R2C_HALF) {
                 const cplx<T> w = ld_c<T>(rp.in, io.in_base + (int64_t)p * rp.src.es);
                 v[m] = {w.x, rp.conj ? -w.y : w.y};
             } else if (MODE == REG_C2R_HALF) {
@@ -204,6 +206,33 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
     } else {
 #pragma unroll
         for (int m = 0; m < E; m++) v[m] = {T(0), T(0)};
+    }
+    if constexpr (MODE == REG_CONV) {
+        // forward FFT (outputs back in v at positions t + m TT), spectrum multiply with the
+        // convolution policy, then the inverse FFT as conj(FFT(conj .)) whose store
+        // conjugates and scales (rp.conj = 1, rp.scale = 1/N)
+        stages<T, N, E, REG_CONV, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
+        const cplx<T> *spec = reinterpret_cast<const cplx<T> *>(rp.tw2);
+        const int64_t o = rp.ni == 1 ? line : line / rp.ni;
+        const int64_t i = line - o * rp.ni;
+        const int64_t base = i + o * rp.conv_om;
+#pragma unroll
+        for (int m = 0; m < E; m++) {
+            const int p = t + m * TT;
+            cplx<T> x = v[m];
+            if (rp.conv_flags & F_CONJ_IN) x.y = -x.y;
+            if (io.valid) x = mul(x, tw_load(spec, base + (int64_t)p * rp.conv_em));
+            if (rp.conv_flags & F_NORMALIZE) {
+                const T r = T(1) / sqrt(x.x * x.x + x.y * x.y);
+                x.x *= r;
+                x.y *= r;
+            }
+            if (rp.conv_flags & F_CONJ_OUT) x.y = -x.y;
+            v[m] = x;
+        }
+        __syncthreads();  // the forward FFT's last shared-memory reads are done
+        stages<T, N, E, REG_C2C, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
+        return;
     }
     stages<T, N, E, MODE, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
     // peer stores are visible system-wide before the rank's exchange signal
@@ -292,6 +321,8 @@ static const RegVariant kRegVariants[] = {
     RV(double, REG_C2C, true, 4096, 16, 2, 16, 16, 16),
     RV_STRIDED(float, REG_C2C_PEER),
     RV_STRIDED(double, REG_C2C_PEER),
+    RV_STRIDED(float, REG_CONV),
+    RV_STRIDED(double, REG_CONV),
 };
 #undef RV_CONTIG
 #undef RV_STRIDED

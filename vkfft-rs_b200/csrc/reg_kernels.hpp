@@ -16,6 +16,8 @@ enum RegMode : int32_t {
                       // (real_ir.rs:1002-1013) -> h+1 bins
     REG_C2R_HALF = 5, // N = h: h+1 bins, even-half pre-processing (real_ir.rs:1087-1100), inverse
                       // FFT_h -> 2h reals stored as h complex pairs
+    REG_CONV = 6,     // strided lines: FFT, pointwise multiply by a spectrum table (tw2), inverse
+                      // FFT (the fused outermost axis of the FFT convolution)
 };
 
 // Line l = o * ni + i; element p of the line is at o*os + i*is + p*es (units of the
@@ -38,7 +40,9 @@ struct RegParams {
     int32_t n;
     int32_t real_ends;   // REG_C2R_HALF: use only the real parts of X[0] and X[h] (the
                          // FullComplex C2R result: its real output ignores those imaginary parts)
-    int32_t _pad;
+    int32_t conv_flags;  // REG_CONV: F_CONJ_IN / F_NORMALIZE / F_CONJ_OUT of the multiply
+    int64_t conv_em;     // REG_CONV: spectrum index = i + p * conv_em + o * conv_om
+    int64_t conv_om;
     PeerStore peer;      // REG_C2C_PEER: the ranks' exchange buffers
 };
 
