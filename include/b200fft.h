@@ -258,6 +258,11 @@ int32_t b200fft_transform_input_is_real(const b200fft_transform *transform);
 int32_t b200fft_transform_output_is_real(const b200fft_transform *transform);
 /* Bytes of device scratch one execution needs (0 when every pass runs in place on chip). */
 uint64_t b200fft_transform_workspace_bytes(const b200fft_transform *transform);
+/* Compiles (NVRTC, no GPU needed, nothing loaded) the run-time specialised kernel of
+ * every generic pass of the transform: returns the number compiled, or -1 with the
+ * compiler log in `log`.  A build check for the specialisation; execution compiles and
+ * loads the same kernels on first use. */
+int32_t b200fft_transform_compile_check(const b200fft_transform *transform, char *log, size_t capacity);
 /* Number of kernel launches one execution issues. */
 uint32_t b200fft_transform_launch_count(const b200fft_transform *transform);
 

@@ -31,14 +31,13 @@ static void emu_launch(const PassParams &p, int64_t grid, int threads, size_t sm
     for (int64_t b = 0; b < grid; b++) {
         std::memset(buf.data(), 0xff, buf.size());
         blockIdx.x = (unsigned)b;
-        Op *s_ops = nullptr;
         LineMeta lm{};
         for (int t = 0; t < threads; t++) {
             threadIdx.x = t;
-            lm = pass_prologue<T>(p, sm_raw, &s_ops);
+            lm = pass_prologue<T>(p, sm_raw);
         }
         for (int k = 0; k < p.nops; k++) {
-            Op op = s_ops[k];
+            Op op = p.ops[k];
             for (int t = 0; t < threads; t++) {
                 threadIdx.x = t;
                 run_op<T>(p, op, reinterpret_cast<cplx<T> *>(sm_raw), lm);

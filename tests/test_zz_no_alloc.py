@@ -2,12 +2,21 @@
 
 Collected last (file name) so that it also runs after every other GPU test has used the
 context's own scratch and tables.  Each case compares two calls in a row of the static
-entry point with the ordinary resident entry point (b200fft_execute) on the same input:
-the same kernels run on the same tables, so the outputs must agree bit for bit."""
+entry point with the ordinary resident entry point (b200fft_execute) on the same input.
+The two calls agree bit for bit; against b200fft_execute they agree to the parity
+tolerance, because b200fft_execute runs generic passes as run-time specialised kernels
+(compiled and loaded on first use, which allocates) while the static entry point keeps
+the precompiled ones."""
 import numpy as np
 import pytest
 
 NP = {"F32": (np.complex64, np.float32), "F64": (np.complex128, np.float64)}
+TOL = {"F32": 2e-6, "F64": 1e-13}
+
+
+def close(a, b, prec):
+    import torch
+    return float(torch.linalg.norm((a - b).double()) / torch.linalg.norm(b.double())) <= TOL[prec]
 
 # transforms whose programs use scratch buffers (four-step, Bluestein, multi-axis real)
 CASES = [
@@ -55,8 +64,8 @@ def test_static_workspace_matches_resident_twice(V, ctx, case):
     ctx.execute_static_workspace(ir, x.data_ptr(), a.data_ptr(), stream=s)
     ctx.execute_static_workspace(ir, x.data_ptr(), b.data_ptr(), stream=s)
     torch.cuda.synchronize()
-    assert torch.equal(a, ref)
-    assert torch.equal(b, ref)
+    assert torch.equal(a, b)
+    assert close(a, ref, case["prec"])
 
 
 @pytest.mark.gpu
@@ -75,9 +84,9 @@ def test_static_workspace_switches_between_transforms(V, ctx):
     ir, x, ref, a, b = runs[0]
     ctx.execute_static_workspace(ir, x.data_ptr(), b.data_ptr(), stream=s)
     torch.cuda.synchronize()
-    for ir, x, ref, a, b in runs:
-        assert torch.equal(a, ref)
-    assert torch.equal(runs[0][4], runs[0][2])
+    for (ir, x, ref, a, b), case in zip(runs, (CASES[0], CASES[2])):
+        assert close(a, ref, case["prec"])
+    assert torch.equal(runs[0][4], runs[0][3])
 
 
 @pytest.mark.gpu

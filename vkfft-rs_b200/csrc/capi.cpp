@@ -464,3 +464,14 @@ b200fft_status b200fft_context_synchronize(b200fft_context *context, void *strea
         context_synchronize(context->ctx, static_cast<cudaStream_t>(stream));
     });
 }
+
+int32_t b200fft_transform_compile_check(const b200fft_transform *transform, char *log, size_t capacity) {
+    if (!transform) return -1;
+    std::string l;
+    const int n = jit_compile_check(transform->t->prog, l);
+    if (log && capacity) {
+        std::strncpy(log, l.c_str(), capacity - 1);
+        log[capacity - 1] = 0;
+    }
+    return n;
+}

@@ -333,7 +333,7 @@ static size_t rader_extra(size_t L, const std::vector<StageSpec> &stages, size_t
     return best;
 }
 
-struct PassShape {
+struct CtaShape {
     int G = 1, threads = 64, ls = 1;
     size_t extra = 0;  // Rader region elements
     size_t smem = 0, meta_off = 0;
@@ -344,7 +344,7 @@ static size_t budget_bytes() { return 200 * 1024; }
 // Choose lines per CTA, threads and shared-memory layout.  Returns false when one
 // line does not fit on chip.
 static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bool strided, int64_t nlines,
-                       int nops, PassShape &sh) {
+                       int nops, CtaShape &sh) {
     if (!stages_ok(stages)) return false;
     const size_t esz = dbl ? 16 : 8;
     sh.ls = line_stride_for(L);
@@ -378,13 +378,13 @@ static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bo
 // Shared-memory capacity only (for passes without an FFT network, e.g. real pre/post).
 static bool line_capacity_ok(bool dbl, size_t L) {
     if (L > (1u << 20)) return false;
-    PassShape sh;
+    CtaShape sh;
     return shape_pass(dbl, (int)L, {}, false, 1 << 20, 8, sh);
 }
 
 bool line_fits_on_chip(bool dbl, size_t L, const AxisAlgorithm *alg, bool strided) {
     if (L > (1u << 20)) return false;
-    PassShape sh;
+    CtaShape sh;
     return shape_pass(dbl, (int)L, line_stages(L, alg), strided, 1 << 20, kMaxOps, sh);
 }
 
@@ -661,7 +661,7 @@ class PassBuilder {
     Program &prog_;
     int L_;
     std::vector<StageSpec> stages_;
-    PassShape sh_;
+    CtaShape sh_;
     PassPlan plan_{};
     int nops_ = 0;
     int A_, B_, cur_, other_;

@@ -6,7 +6,14 @@
 // processing) and stored back.  Plain POD so it can be a __grid_constant__
 // kernel parameter.
 #pragma once
+#ifdef __CUDACC_RTC__
+typedef int int32_t;
+typedef unsigned int uint32_t;
+typedef long long int64_t;
+typedef unsigned long long uint64_t;
+#else
 #include <cstdint>
+#endif
 
 namespace b200fft {
 
@@ -105,7 +112,8 @@ struct PeerStore {
     FastDiv div;    // chunk
 };
 
-struct PassParams {
+// Everything a pass launch describes except its op list (the op functions read this).
+struct PassShape {
     int64_t nlines;   // total number of lines in this launch
     int64_t ni, nc;   // line decomposition
     int32_t G;        // lines per CTA
@@ -120,6 +128,9 @@ struct PassParams {
     void *dst;
     int *err;         // device error word (0 = ok), set instead of trapping
     PeerStore peer;   // STORE ops: optional scatter into the ranks' exchange buffers
+};
+
+struct PassParams : PassShape {
     Op ops[kMaxOps];
 };
 

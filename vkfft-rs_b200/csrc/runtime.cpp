@@ -170,6 +170,12 @@ static DeviceTables &ensure_tables(Context *ctx, uint64_t id, const Program &pro
     }
     for (size_t k = 0; k < prog.tables.size(); k++)
         dt.ptrs.push_back(static_cast<unsigned char *>(dt.base) + offs[k]);
+    try {
+        dt.jit = jit_kernels_for(prog, ctx->device);
+    } catch (...) {
+        cudaFree(dt.base);
+        throw;
+    }
     return ctx->tables.emplace(id, std::move(dt)).first->second;
 }
 
@@ -198,7 +204,8 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
     void *bufs[2 + kScratchBuffers] = {const_cast<void *>(in), out};
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scr ? scr + prog.scratch_offset(k) : nullptr;
     const int variant = kernel_variant_for(prog.is_double);
-    for (const PassPlan &pp : prog.passes) {
+    for (size_t pi = 0; pi < prog.passes.size(); pi++) {
+        const PassPlan &pp = prog.passes[pi];
         if (pp.kernel == KERNEL_REG) {
             RegParams rp = pp.rp;
             rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * (pp.reg_in_real ? esz / 2 : esz);
@@ -229,7 +236,13 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
             p.peer.sub = peer->chunk * pp.peer_es;
         }
         if (injected("launch", g_launch_count)) fail_runtime("kernel launch failed: injected launch fault");
-        check(launch_pass(variant, p, pp.grid, pp.threads, pp.smem, stream), "kernel launch");
+        if (pi < dt.jit.size() && dt.jit[pi]) {
+            void *args[] = {&p};
+            check(cudaLaunchKernel(dt.jit[pi], dim3((unsigned)pp.grid), dim3(pp.threads), args, pp.smem, stream),
+                  "kernel launch");
+        } else {
+            check(launch_pass(variant, p, pp.grid, pp.threads, pp.smem, stream), "kernel launch");
+        }
     }
 }
 

@@ -16,7 +16,12 @@ namespace b200fft {
 struct DeviceTables {
     void *base = nullptr;
     std::vector<const void *> ptrs;
+    std::vector<const void *> jit;  // per pass: specialised kernel (jit.cpp) or null
 };
+
+bool jit_enabled();
+std::vector<const void *> jit_kernels_for(const Program &prog, int device);
+int jit_compile_check(const Program &prog, std::string &log);
 
 struct Context {
     int device = 0;

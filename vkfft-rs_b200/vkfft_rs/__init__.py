@@ -242,6 +242,7 @@ def library():
         "b200fft_transform_output_is_real": ([vp], i32),
         "b200fft_transform_workspace_bytes": ([vp], u64),
         "b200fft_transform_launch_count": ([vp], u32),
+        "b200fft_transform_compile_check": ([vp, ctypes.c_char_p, ctypes.c_size_t], i32),
         "b200fft_probe": ([P(i32)], i32),
         "b200fft_context_create": ([i32, P(vp)], i32),
         "b200fft_context_destroy": ([vp], None),
@@ -625,6 +626,15 @@ class TransformIr:
         if h and _lib is not None:
             _lib.b200fft_transform_destroy(h)
             self._h = None
+
+    def compile_check(self):
+        """NVRTC-compiles the specialised kernel of every generic pass (no GPU needed);
+        returns how many, raises RuntimeError with the compiler log on failure."""
+        buf = ctypes.create_string_buffer(16384)
+        n = library().b200fft_transform_compile_check(self._h, buf, len(buf))
+        if n < 0:
+            raise RuntimeError(buf.value.decode(errors="replace"))
+        return n
 
     @property
     def family(self):
