@@ -226,6 +226,38 @@ def test_resident_execution_matches_host_execution(V, ctx):
     assert np.array_equal(xd.cpu().numpy().ravel(), host)
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("dims,batch,prec,kind", [([4096], 16384 + 100, "F32", "c2c"), ([4099], 20000, "F32", "c2c"),
+                                                  ([4096], 20000, "F64", "r2c"), ([1024], 100000, "F32", "c2r")])
+def test_pipelined_host_execution_matches_resident(V, ctx, dims, batch, prec, kind):
+    """Large batched host executions run as overlapped sub-batches (upload / transform /
+    download on three streams); the result equals one resident execution of the whole batch."""
+    torch = pytest.importorskip("torch")
+    cdt, rdt = NP[prec]
+    cfg = V.FftConfig(dims).with_batch_count(batch).with_precision(V.Precision[prec])
+    direction = V.Direction.FORWARD
+    if kind == "r2c":
+        cfg = cfg.with_transform(V.TransformKind.R2C)
+    elif kind == "c2r":
+        cfg = cfg.with_transform(V.TransformKind.C2R).with_inverse_normalization(True)
+        direction = V.Direction.INVERSE
+    ir = V.TransformIr.build(cfg, direction, ctx.device_profile())
+    rng = np.random.default_rng(batch)
+    n_in = ir.input_elements * (1 if kind == "r2c" else 2)
+    x = rng.uniform(-1, 1, n_in).astype(rdt)
+    host_in = torch.from_numpy(x).pin_memory()
+    host_out = torch.empty(ir.output_elements * (1 if kind == "c2r" else 2), dtype=host_in.dtype).pin_memory()
+    xin = host_in.numpy().view(np.float32 if prec == "F32" else np.float64)
+    out = ctx.execute_transform(ir, xin.view(rdt if kind == "r2c" else cdt),
+                                out=host_out.numpy().view(rdt if kind == "c2r" else cdt))
+    xd = host_in.cuda()
+    yd = torch.empty(host_out.numel(), dtype=host_in.dtype, device="cuda")
+    ctx.execute_resident(ir, xd.data_ptr(), yd.data_ptr(), stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ref = yd.cpu().numpy().view(rdt if kind == "c2r" else cdt)
+    assert rel_l2(out, ref) <= TOL[prec]
+
+
 def test_input_length_mismatch_is_reported(V, ctx):
     ir = V.TransformIr.build(V.FftConfig([64]).with_batch_count(2), V.Direction.FORWARD, ctx.device_profile())
     import ctypes

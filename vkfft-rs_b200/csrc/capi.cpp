@@ -228,6 +228,8 @@ b200fft_status b200fft_transform_build(const b200fft_config *config, int32_t dir
 void b200fft_transform_destroy(b200fft_transform *transform) {
     if (!transform) return;
     forget_program(transform->t->id);
+    for (auto &kv : transform->t->chunks)
+        if (kv.second) forget_program(kv.second->id);
     delete transform;
 }
 
@@ -335,8 +337,7 @@ b200fft_status b200fft_execute_host(b200fft_context *context, b200fft_transform 
         need(transform, "transform");
         need(input, "input");
         need(output, "output");
-        execute_program_host(context->ctx, transform->t->id, transform->t->prog, input, input_bytes, output,
-                             output_bytes);
+        execute_transform_host(context->ctx, *transform->t, input, input_bytes, output, output_bytes);
     });
 }
 

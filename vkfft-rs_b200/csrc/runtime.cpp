@@ -69,6 +69,9 @@ Context *context_create(int device) {
         check(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking), "cudaStreamCreate");
         ctx->d_err = static_cast<int *>(device_alloc(sizeof(int), "error word allocation"));
         check(cudaMemset(ctx->d_err, 0, sizeof(int)), "cudaMemset");
+        // the memset runs on the legacy stream, which the context's non-blocking streams
+        // do not wait for
+        check(cudaStreamSynchronize(cudaStreamLegacy), "stream synchronize");
         cudaDeviceProp prop;
         check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
         ctx->name = prop.name;
@@ -114,6 +117,12 @@ void context_destroy(Context *ctx) {
     cudaFree(ctx->scratch);
     cudaFree(ctx->stage_in);
     cudaFree(ctx->stage_out);
+    for (cudaStream_t s : ctx->pipe)
+        if (s) {
+            cudaStreamSynchronize(s);
+            cudaStreamDestroy(s);
+        }
+    cudaFree(ctx->pipe_buf);
     cudaFree(ctx->d_err);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -163,7 +172,11 @@ static DeviceTables &ensure_tables(Context *ctx, uint64_t id, const Program &pro
         }
     }
     dt.base = device_alloc(host.size(), "table upload allocation");
+    // A copy from pageable memory may return before its DMA has reached device memory, and
+    // the kernels that read the tables run on non-blocking streams: wait for the legacy
+    // stream that carries the copy.
     cudaError_t e = cudaMemcpy(dt.base, host.data(), host.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
     if (e != cudaSuccess) {
         cudaFree(dt.base);
         check(e, "table upload");
@@ -288,6 +301,101 @@ void context_synchronize(Context *ctx, cudaStream_t stream) {
     check(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost), "error word read");
     if (err) {
         check(cudaMemset(ctx->d_err, 0, sizeof(int)), "error word reset");
+        check(cudaStreamSynchronize(cudaStreamLegacy), "stream synchronize");
+        fail_runtime(describe_error_word(err));
+    }
+}
+
+// ---- pipelined host execution ------------------------------------------------------
+
+// The executed algorithm of two programs is the same when every pass runs the same
+// kernel on the same op sequence (only line counts, grids and scratch sizes differ).
+static bool same_algorithm(const Program &a, const Program &b) {
+    if (a.passes.size() != b.passes.size() || a.tables.size() != b.tables.size()) return false;
+    for (size_t i = 0; i < a.passes.size(); i++) {
+        const PassPlan &x = a.passes[i], &y = b.passes[i];
+        if (x.kernel != y.kernel || x.reg_variant != y.reg_variant || x.p.nops != y.p.nops) return false;
+        for (int k = 0; k < x.p.nops; k++) {
+            const Op &u = x.p.ops[k], &v = y.p.ops[k];
+            if (u.type != v.type || u.radix != v.radix || u.len != v.len || u.flags != v.flags || u.mul != v.mul)
+                return false;
+        }
+    }
+    for (size_t i = 0; i < a.tables.size(); i++)
+        if (a.tables[i].bytes(a.is_double) != b.tables[i].bytes(b.is_double)) return false;
+    return true;
+}
+
+static Transform *chunk_transform(Transform &t, size_t batch) {
+    std::lock_guard<std::mutex> g(t.chunk_mu);
+    auto it = t.chunks.find(batch);
+    if (it != t.chunks.end()) return it->second.get();
+    std::unique_ptr<Transform> c;
+    try {
+        FftConfig cfg = t.config;
+        cfg.batch_count = batch;
+        c = build_transform(cfg, t.direction, t.device);
+        if (!same_algorithm(t.prog, c->prog)) c.reset();
+    } catch (const FftError &) {
+        c.reset();
+    }
+    return t.chunks.emplace(batch, std::move(c)).first->second.get();
+}
+
+void execute_transform_host(Context *ctx, Transform &t, const void *in, size_t in_bytes, void *out,
+                            size_t out_bytes) {
+    const Program &prog = t.prog;
+    const size_t esz = prog.is_double ? 16 : 8;
+    const size_t in_need = prog.input_elems * (prog.input_real ? esz / 2 : esz);
+    const size_t out_need = prog.output_elems * (prog.output_real ? esz / 2 : esz);
+    const size_t batch = t.plan.config.kernel_preparation_system_count();
+    constexpr size_t kChunkBytes = size_t(128) << 20;  // input bytes per sub-batch
+    const size_t in_per = batch ? in_need / batch : 0, out_per = batch ? out_need / batch : 0;
+    const size_t chunk = in_per ? std::max<size_t>(1, kChunkBytes / in_per) : 0;
+    Transform *ct = nullptr, *rt = nullptr;
+    const size_t nfull = chunk ? batch / chunk : 0, rem = chunk ? batch % chunk : 0;
+    if (in_bytes == in_need && out_bytes == out_need && in_per * batch == in_need && out_per * batch == out_need &&
+        nfull >= 3) {
+        ct = chunk_transform(t, chunk);
+        if (ct && rem) rt = chunk_transform(t, rem);
+    }
+    if (!ct || (rem && !rt)) {
+        execute_program_host(ctx, t.id, prog, in, in_bytes, out, out_bytes);
+        return;
+    }
+    check(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const size_t scr = std::max(ct->prog.scratch_bytes(), rt ? rt->prog.scratch_bytes() : 0);
+    const size_t cin = (chunk * in_per + 255) & ~size_t(255), cout = (chunk * out_per + 255) & ~size_t(255);
+    const size_t slot_bytes = cin + cout + ((scr + 255) & ~size_t(255));
+    unsigned char *base;
+    {
+        std::lock_guard<std::mutex> l(ctx->mu);
+        for (cudaStream_t &s : ctx->pipe)
+            if (!s) check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+        base = static_cast<unsigned char *>(
+            ensure_buffer(ctx->pipe_buf, ctx->pipe_bytes, Context::kPipeSlots * slot_bytes, "pipeline staging allocation"));
+    }
+    const size_t nchunks = nfull + (rem ? 1 : 0);
+    for (size_t i = 0; i < nchunks; i++) {
+        const int slot = (int)(i % Context::kPipeSlots);
+        cudaStream_t s = ctx->pipe[slot];
+        Transform *tt = i < nfull ? ct : rt;
+        const size_t nb = i < nfull ? chunk : rem;
+        unsigned char *din = base + slot * slot_bytes, *dout = din + cin, *dscr = dout + cout;
+        check(cudaMemcpyAsync(din, static_cast<const unsigned char *>(in) + i * chunk * in_per, nb * in_per,
+                              cudaMemcpyHostToDevice, s),
+              "input upload");
+        execute_program(ctx, tt->id, tt->prog, din, dout, scr ? dscr : nullptr, s);
+        check(cudaMemcpyAsync(static_cast<unsigned char *>(out) + i * chunk * out_per, dout, nb * out_per,
+                              cudaMemcpyDeviceToHost, s),
+              "output download");
+    }
+    for (cudaStream_t s : ctx->pipe) check(cudaStreamSynchronize(s), "stream synchronize");
+    int err = 0;
+    check(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost), "error word read");
+    if (err) {
+        check(cudaMemset(ctx->d_err, 0, sizeof(int)), "error word reset");
+        check(cudaStreamSynchronize(cudaStreamLegacy), "stream synchronize");
         fail_runtime(describe_error_word(err));
     }
 }

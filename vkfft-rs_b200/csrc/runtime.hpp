@@ -36,6 +36,11 @@ struct Context {
     size_t scratch_bytes = 0;
     void *stage_in = nullptr, *stage_out = nullptr;
     size_t stage_in_bytes = 0, stage_out_bytes = 0;
+    // pipelined host execution: streams and per-slot staging (input, output, scratch)
+    static constexpr int kPipeSlots = 3;
+    cudaStream_t pipe[kPipeSlots] = {};
+    void *pipe_buf = nullptr;
+    size_t pipe_bytes = 0;
 };
 
 int probe_devices();
@@ -53,6 +58,10 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
 // Waits for the stream (null: the context's) and turns a recorded kernel error into
 // a NativeRuntime error (clearing it).
 void context_synchronize(Context *ctx, cudaStream_t stream);
+// Host-buffer execution of a transform with copy semantics: large batched transforms are
+// split into sub-batches whose upload, transform and download overlap on three streams.
+void execute_transform_host(Context *ctx, Transform &t, const void *in, size_t in_bytes, void *out,
+                            size_t out_bytes);
 // Synchronous host-buffer execution with copy semantics.
 void execute_program_host(Context *ctx, uint64_t id, const Program &prog, const void *in, size_t in_bytes, void *out,
                           size_t out_bytes);

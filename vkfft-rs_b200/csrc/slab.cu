@@ -96,6 +96,7 @@ void slab_attach(Context *ctx, Slab *s, unsigned char *handle_out) {
         void *p = nullptr;
         check(cudaMalloc(&p, kFlagBytes + 2 * s->buffer_bytes()), "slab exchange allocation");
         cudaError_t e = cudaMemset(p, 0, kFlagBytes);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);  // before any peer or barrier
         if (e != cudaSuccess) {
             cudaFree(p);
             check(e, "cudaMemset");

@@ -1,7 +1,9 @@
 // TransformIr analogue: device-scored plan + executed child plans + B200 program.
 #pragma once
 
+#include <map>
 #include <memory>
+#include <mutex>
 #include <optional>
 
 #include "lower.hpp"
@@ -20,6 +22,10 @@ struct Transform {
     // executed 1D child plan per tensor axis (empty for omitted axes)
     std::vector<std::optional<FftPlan>> children;
     Program prog;
+    // same transform over a sub-batch, for pipelined host execution (runtime.cpp);
+    // null when planning the sub-batch changes the executed algorithm
+    std::mutex chunk_mu;
+    std::map<size_t, std::unique_ptr<Transform>> chunks;
 };
 
 std::unique_ptr<Transform> build_transform(const FftConfig &config, int direction, const DeviceProfile &device);
