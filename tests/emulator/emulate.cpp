@@ -216,4 +216,5 @@ int reg_variant_for(bool, size_t, int, bool) { return -1; }
 namespace b200fft {
 int reg_variant_radices(int, int *) { return 0; }
 int reg_variant_peer_twin(int) { return -1; }
+int reg_variant_persistent_twin(int) { return -1; }
 }  // namespace b200fft

@@ -808,6 +808,16 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
             pp.dst_buf = job.out_buf;
             pp.dst_off = job.out_off;
             pp.label = "register stockham";
+            // dense contiguous lines: the persistent variant prefetches each CTA's next
+            // line group with a bulk copy while the current one is transformed
+            if (mode == REG_C2C && !strided && job.in_os == (int64_t)N && job.in_off == 0) {
+                const int pv = reg_variant_persistent_twin(rv);
+                if (pv >= 0) {
+                    pp.reg_variant_plain = rv;
+                    pp.reg_variant = pv;
+                    pp.label = "register stockham (bulk prefetch)";
+                }
+            }
             for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
             prog.passes.push_back(pp);
             return;

@@ -18,6 +18,7 @@
 // Inverse transforms conjugate on load and store (tables stay forward).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "dft_codelets.cuh"
@@ -262,6 +263,98 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
     }
 }
 
+// ---- persistent variant: bulk-copy prefetch of the next line group -------------------
+// Dense contiguous C2C lines (line stride N, element stride 1): each CTA loops over
+// groups of G lines.  One thread fetches the group with cp.async.bulk into a shared
+// buffer, tracked by an mbarrier; as soon as every thread has taken its points from the
+// buffer it fetches the CTA's next group, so the next load overlaps the radix stages and
+// the stores of the current one.  Waits are bounded: on expiry the kernel records error
+// bit 64 and stops.
+
+__device__ __forceinline__ unsigned smem_addr(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void bulk_fetch(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool bar_wait(uint64_t *bar, unsigned parity) {
+    for (int i = 0; i < (1 << 22); i++) {
+        unsigned done;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(done)
+            : "r"(smem_addr(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+template <typename T, int N, int E, int G, int MINB, int... Rs>
+__global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __grid_constant__ RegParams rp) {
+    constexpr int TT = N / E;
+    constexpr int LS = N + N / 16 + 1;
+    constexpr unsigned GROUP_BYTES = (unsigned)(G * N * sizeof(cplx<T>));
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem_raw);
+    cplx<T> *buf = reinterpret_cast<cplx<T> *>(smem_raw + 128);
+    cplx<T> *xch = buf + G * N;
+    const int g = threadIdx.x / TT, t = threadIdx.x - g * TT;
+    cplx<T> *sline = xch + g * LS;
+    const cplx<T> *tw = reinterpret_cast<const cplx<T> *>(rp.tw);
+    const int64_t ngroups = (rp.nlines + G - 1) / G;
+    auto group_bytes = [&](int64_t grp) {
+        const int64_t lines = rp.nlines - grp * G;
+        return lines >= G ? GROUP_BYTES : (unsigned)(lines * N * sizeof(cplx<T>));
+    };
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    int64_t grp = blockIdx.x;
+    bool in_flight = false;
+    if (threadIdx.x == 0 && grp < ngroups) {
+        bulk_fetch(buf, reinterpret_cast<const cplx<T> *>(rp.in) + grp * G * N, group_bytes(grp), bar);
+        in_flight = true;
+    }
+    unsigned parity = 0;
+    for (; grp < ngroups; grp += gridDim.x) {
+        if (!bar_wait(bar, parity)) {
+            if (threadIdx.x == 0) atomicOr(rp.err, 64);
+            break;
+        }
+        parity ^= 1u;
+        in_flight = false;
+        const int64_t line = grp * G + g;
+        LineIO io;
+        io.valid = line < rp.nlines;
+        io.in_base = line * rp.src.os;
+        io.out_base = line * rp.dst.os;
+        cplx<T> v[E];
+#pragma unroll
+        for (int m = 0; m < E; m++) {
+            const cplx<T> w = buf[g * N + t + m * TT];
+            v[m] = {w.x, rp.conj ? -w.y : w.y};
+        }
+        __syncthreads();  // the group buffer is consumed
+        const int64_t nxt = grp + gridDim.x;
+        if (threadIdx.x == 0 && nxt < ngroups) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            bulk_fetch(buf, reinterpret_cast<const cplx<T> *>(rp.in) + nxt * G * N, group_bytes(nxt), bar);
+            in_flight = true;
+        }
+        stages<T, N, E, REG_C2C, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
+    }
+    // never leave with a bulk copy still writing this CTA's shared memory
+    if (threadIdx.x == 0 && in_flight && !bar_wait(bar, parity)) atomicOr(rp.err, 64);
+}
+
 }  // namespace regk
 
 // ---- variant table ----------------------------------------------------------------
@@ -271,11 +364,17 @@ struct RegVariant {
     size_t smem;
     const void *fn;
     int radices[8];
+    int persistent;  // reg_fft_persistent (grid sized to the resident CTAs)
 };
 
 #define RV(T, MODE, STR, N, E, G, ...)                                                                      \
     {sizeof(T) == 8, N, MODE, STR, G *(N / E), G, (size_t)G *(N + N / 16 + 1) * sizeof(T) * 2,             \
-     (const void *)regk::reg_fft_kernel<T, N, E, G, MODE, STR, __VA_ARGS__>, {__VA_ARGS__}}
+     (const void *)regk::reg_fft_kernel<T, N, E, G, MODE, STR, __VA_ARGS__>, {__VA_ARGS__}, 0}
+// persistent contiguous C2C: barrier slot + one group buffer + the exchange buffer
+#define RVP(T, N, E, G, MINB, ...)                                                                          \
+    {sizeof(T) == 8, N, REG_C2C, 0, G *(N / E), G,                                                          \
+     128 + (size_t)G * N * sizeof(T) * 2 + (size_t)G *(N + N / 16 + 1) * sizeof(T) * 2,                     \
+     (const void *)regk::reg_fft_persistent<T, N, E, G, MINB, __VA_ARGS__>, {__VA_ARGS__}, 1}
 
 // contiguous lines, all modes
 #define RV_CONTIG(T, MODE)                                                                                  \
@@ -323,15 +422,36 @@ static const RegVariant kRegVariants[] = {
     RV_STRIDED(double, REG_C2C_PEER),
     RV_STRIDED(float, REG_CONV),
     RV_STRIDED(double, REG_CONV),
+    // persistent twins of the contiguous C2C variants (bulk-copy prefetch)
+    // (blocks per SM asked of the register allocator: the shared-memory limit)
+    RVP(float, 256, 16, 16, 3, 16, 16), RVP(float, 512, 16, 8, 3, 16, 16, 2), RVP(float, 1024, 16, 4, 3, 16, 16, 4),
+    RVP(float, 2048, 16, 2, 3, 16, 16, 8), RVP(float, 4096, 16, 1, 3, 16, 16, 16),
+    // (f64 groups need twice the buffer and registers: one CTA per SM, slower than the
+    // ordinary kernel's two, so f64 keeps the ordinary variants)
 };
 #undef RV_CONTIG
 #undef RV_STRIDED
+#undef RVP
 #undef RV
 
 int reg_variant_for(bool is_double, size_t n, int mode, bool strided) {
     for (int i = 0; i < (int)(sizeof(kRegVariants) / sizeof(kRegVariants[0])); i++) {
         const RegVariant &v = kRegVariants[i];
-        if (v.is_double == (int)is_double && (size_t)v.n == n && v.mode == mode && v.strided == (int)strided) return i;
+        if (v.is_double == (int)is_double && (size_t)v.n == n && v.mode == mode && v.strided == (int)strided &&
+            !v.persistent)
+            return i;
+    }
+    return -1;
+}
+
+// The persistent twin of a contiguous C2C variant (same precision, length, radices and
+// lines per CTA), or -1.
+int reg_variant_persistent_twin(int v) {
+    const RegVariant &a = kRegVariants[v];
+    if (a.mode != REG_C2C || a.strided || a.persistent) return -1;
+    for (int i = 0; i < (int)(sizeof(kRegVariants) / sizeof(kRegVariants[0])); i++) {
+        const RegVariant &b = kRegVariants[i];
+        if (b.persistent && b.is_double == a.is_double && b.n == a.n && b.g == a.g && b.smem <= 232448) return i;
     }
     return -1;
 }
@@ -365,9 +485,26 @@ void set_reg_kernel_smem_limits() {
     done_mask |= 1ull << dev;
 }
 
+// Resident CTAs of a persistent variant on the current device (cached per device).
+static int64_t persistent_grid(int variant) {
+    static int cache[64][sizeof(kRegVariants) / sizeof(kRegVariants[0])] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    int &c = cache[dev][variant];
+    if (!c) {
+        const RegVariant &v = kRegVariants[variant];
+        int sms = 0, per = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, v.fn, v.threads, v.smem);
+        c = std::max(1, sms) * std::max(1, per);
+    }
+    return c;
+}
+
 cudaError_t launch_reg(int variant, const RegParams &rp, cudaStream_t stream) {
     const RegVariant &v = kRegVariants[variant];
-    const int64_t grid = (rp.nlines + v.g - 1) / v.g;
+    int64_t grid = (rp.nlines + v.g - 1) / v.g;
+    if (v.persistent) grid = std::min<int64_t>(grid, persistent_grid(variant));
     void *args[] = {const_cast<RegParams *>(&rp)};
     return cudaLaunchKernel(v.fn, dim3((unsigned)grid), dim3(v.threads), args, v.smem, stream);
 }

@@ -43,6 +43,7 @@ struct RegParams {
     int32_t conv_flags;  // REG_CONV: F_CONJ_IN / F_NORMALIZE / F_CONJ_OUT of the multiply
     int64_t conv_em;     // REG_CONV: spectrum index = i + p * conv_em + o * conv_om
     int64_t conv_om;
+    int *err;            // persistent variants: error word (a bulk copy that never completed)
     PeerStore peer;      // REG_C2C_PEER: the ranks' exchange buffers
 };
 

@@ -225,13 +225,16 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
             rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * (pp.reg_out_real ? esz / 2 : esz);
             rp.tw = dt.ptrs[pp.reg_table];
             rp.tw2 = pp.reg_table2 >= 0 ? dt.ptrs[pp.reg_table2] : nullptr;
+            rp.err = ctx->d_err;
+            int rv = pp.reg_variant;
+            if (pp.reg_variant_plain >= 0 && (reinterpret_cast<uintptr_t>(rp.in) & 15)) rv = pp.reg_variant_plain;
             if (pp.peer_scatter) {
                 if (!peer) fail_runtime("slab exchange pass launched without the ranks' buffers");
                 rp.peer = *peer;
                 rp.peer.sub = peer->chunk * pp.peer_es;
             }
             if (injected("launch", g_launch_count)) fail_runtime("kernel launch failed: injected launch fault");
-            check(launch_reg(pp.reg_variant, rp, stream), "kernel launch");
+            check(launch_reg(rv, rp, stream), "kernel launch");
             continue;
         }
         PassParams p = pp.p;

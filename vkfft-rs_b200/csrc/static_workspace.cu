@@ -112,7 +112,10 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
             rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * (pp.reg_out_real ? esz / 2 : esz);
             rp.tw = tables[pp.reg_table];
             rp.tw2 = pp.reg_table2 >= 0 ? tables[pp.reg_table2] : nullptr;
-            check(launch_reg(pp.reg_variant, rp, stream), "kernel launch");
+            rp.err = ctx->d_err;
+            int rv = pp.reg_variant;
+            if (pp.reg_variant_plain >= 0 && (reinterpret_cast<uintptr_t>(rp.in) & 15)) rv = pp.reg_variant_plain;
+            check(launch_reg(rv, rp, stream), "kernel launch");
             continue;
         }
         PassParams p = pp.p;
