@@ -282,7 +282,7 @@ def run_ours(args):
                    "l2": "inputs (2 GiB per rank) larger than L2; no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": peak_kind, "this_gpu_copy_gbs": box_copy,
-                     "kernel": "reg_fft_kernel<float,4096> (register-resident Stockham, one launch per transform direction)"},
+                     "kernel": "reg_fft_persistent<float,4096> (register-resident Stockham with bulk-copy prefetch, one launch per transform direction)"},
         "e2e": None if e2e_value is None else {"value": e2e_value, "unit": "GFLOP/s", "h2d_bytes_per_step": 2 * bytes_one,
                 "d2h_bytes_per_step": 2 * bytes_one, "path": "execute_transform (host arrays, pinned)"},
         "gpu_launches": args.steps * (fwd.launch_count + inv.launch_count),
