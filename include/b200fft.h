@@ -251,9 +251,16 @@ const b200fft_plan *b200fft_transform_plan(const b200fft_transform *transform);
  * real_ir.rs:326-345 internal plan for the real axis) */
 b200fft_status b200fft_transform_axis_child_info(const b200fft_transform *transform, uint32_t axis,
                                                  b200fft_axis_info *info);
-/* Element counts of one input / output tensor (complex or real elements) */
+/* Element counts (complex or real) of the logical input / output tensors: the sizes of
+ * the host arrays of b200fft_execute_host, which are always dense (the reference packs
+ * formatted layouts internally, nd_real_ir.rs:715-750). */
 uint64_t b200fft_transform_input_elements(const b200fft_transform *transform);
 uint64_t b200fft_transform_output_elements(const b200fft_transform *transform);
+/* Element counts of the device buffers of b200fft_execute: with formatted buffer strides
+ * (config.rs:893-1002) batch_stride x batch stored elements, otherwise the logical
+ * counts.  Elements of a formatted output buffer outside the tensor are not written. */
+uint64_t b200fft_transform_input_buffer_elements(const b200fft_transform *transform);
+uint64_t b200fft_transform_output_buffer_elements(const b200fft_transform *transform);
 int32_t b200fft_transform_input_is_real(const b200fft_transform *transform);
 int32_t b200fft_transform_output_is_real(const b200fft_transform *transform);
 /* Bytes of device scratch one execution needs (0 when every pass runs in place on chip). */

@@ -72,6 +72,13 @@ static void run_program(const Program &prog, const void *in, void *out, const Pe
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scratch[k].empty() ? nullptr : scratch[k].data();
     int err = 0;
     for (const PassPlan &pp : prog.passes) {
+        if (pp.kernel == KERNEL_COPY) {
+            BoundaryCopy bc = pp.bc;
+            bc.src = bufs[pp.src_buf];
+            bc.dst = bufs[pp.dst_buf];
+            for (int64_t L = 0; L < bc.total; L++) boundary_copy_one(bc, L);
+            continue;
+        }
         PassParams p = pp.p;
         for (int k = 0; k < p.nops; k++) {
             const void **slots[3] = {&p.ops[k].lut, &p.ops[k].lut2, &p.ops[k].lut3};

@@ -58,6 +58,8 @@ def run(case, V, lib):
         return run_conv(case, V, lib, dev, cfg, rng, cdt, rdt)
     elif kind == "slab":
         return run_slab(case, V, lib, dev, cfg, rng, cdt, rdt)
+    elif kind == "bnd":
+        return run_boundary(case, V, lib, dev, cfg, rng, cdt, rdt)
     else:
         x = rng.uniform(-1, 1, shape)
         spec = oracle.r2c_nd(x, len(dims), threads=4).astype(cdt)
@@ -147,6 +149,94 @@ def run_slab(case, V, lib, dev, cfg, rng, cdt, rdt):
     if st != 0:
         raise V.VkFftError(st, err.value.decode())
     return {"err": rel_l2(out, ref), "launches": launches.value}
+
+
+def _pad_mask(dims, pads):
+    """True where any padded axis coordinate lies in its [left, right) interval."""
+    mask = np.zeros(dims, dtype=bool)
+    for axis, (lo, hi) in pads.items():
+        idx = [slice(None)] * len(dims)
+        idx[int(axis)] = slice(lo, hi)
+        mask[tuple(idx)] = True
+    return mask
+
+
+def _resolve(dims, strides, batch_stride):
+    """config.rs:1463-1522: per-axis strides (None = dense minimum) and batch stride."""
+    st = [1] * len(dims)
+    for a in range(len(dims) - 2, -1, -1):
+        minimum = st[a + 1] * dims[a + 1]
+        st[a] = (strides or {}).get(str(a), minimum)
+    return st, (batch_stride or st[0] * dims[0])
+
+
+def _pack(x, dims, strides, batch_stride, fill):
+    st, bs = _resolve(dims, strides, batch_stride)
+    batch = x.shape[0]
+    phys = np.full(bs * batch, fill, dtype=x.dtype)
+    idx = np.indices(dims).reshape(len(dims), -1)
+    off = sum(idx[a] * st[a] for a in range(len(dims)))
+    for b in range(batch):
+        phys[b * bs + off] = x[b].reshape(-1)
+    return phys
+
+
+def _unpack(phys, dims, strides, batch_stride, batch):
+    st, bs = _resolve(dims, strides, batch_stride)
+    idx = np.indices(dims).reshape(len(dims), -1)
+    off = sum(idx[a] * st[a] for a in range(len(dims)))
+    return np.stack([phys[b * bs + off].reshape(dims) for b in range(batch)])
+
+
+def run_boundary(case, V, lib, dev, cfg, rng, cdt, rdt):
+    """Zero padding / formatted strides (kind "bnd"): mode c2c | c2c_inv | r2c | c2r."""
+    dims, batch, mode = case["dims"], case["batch"], case["mode"]
+    pads = case.get("pad", {})
+    freq = case.get("domain") == "frequency"
+    for axis, (lo, hi) in pads.items():
+        cfg = cfg.with_zero_padding(int(axis), lo, hi)
+    if freq:
+        cfg = cfg.with_zero_padding_domain(V.ZeroPaddingDomain.FREQUENCY)
+    for axis, st in (case.get("in_strides") or {}).items():
+        cfg = cfg.with_input_buffer_axis_stride(int(axis), st)
+    for axis, st in (case.get("out_strides") or {}).items():
+        cfg = cfg.with_output_buffer_axis_stride(int(axis), st)
+    if case.get("in_batch_stride"):
+        cfg = cfg.with_input_buffer_batch_stride(case["in_batch_stride"])
+    if case.get("out_batch_stride"):
+        cfg = cfg.with_output_buffer_batch_stride(case["out_batch_stride"])
+    half = list(dims[:-1]) + [dims[-1] // 2 + 1]
+    nd = len(dims)
+    shape = (batch,) + tuple(dims)
+    mask = _pad_mask(dims, pads) if pads else np.zeros(dims, dtype=bool)
+    direction = V.Direction.FORWARD
+    if mode in ("c2c", "c2c_inv"):
+        x = rng.uniform(-1, 1, shape) + 1j * rng.uniform(-1, 1, shape)
+        inv = mode == "c2c_inv"
+        direction = V.Direction.INVERSE if inv else V.Direction.FORWARD
+        pad_in = bool(pads) and (freq == inv)
+        xi = np.where(mask, 0, x) if pad_in else x
+        ref = oracle.fft_nd(xi, nd, inverse=inv, normalize=case.get("normalize", False), threads=4)
+        if pads and not pad_in:
+            ref = np.where(mask, 0, ref)
+        in_dims, out_dims, in_dt, out_dt = dims, dims, cdt, cdt
+    elif mode == "r2c":
+        cfg = cfg.with_transform(V.TransformKind.R2C)
+        x = rng.uniform(-1, 1, shape)
+        ref = oracle.r2c_nd(np.where(mask, 0, x), nd, threads=4)
+        in_dims, out_dims, in_dt, out_dt = dims, half, rdt, cdt
+    else:
+        cfg = cfg.with_transform(V.TransformKind.C2R).with_inverse_normalization(True)
+        direction = V.Direction.INVERSE
+        x = oracle.r2c_nd(rng.uniform(-1, 1, shape), nd, threads=4)
+        ref = np.where(mask, 0, oracle.c2r_nd(x, dims[-1], nd, normalize=True, threads=4))
+        in_dims, out_dims, in_dt, out_dt = half, dims, cdt, rdt
+    phys_in = _pack(np.asarray(x).astype(in_dt), in_dims, case.get("in_strides"), case.get("in_batch_stride"),
+                    in_dt(7.0))
+    st, bs = _resolve(out_dims, case.get("out_strides"), case.get("out_batch_stride"))
+    y, n = emulate(V, lib, cfg, direction, dev, phys_in, bs * batch, out_dt)
+    got = _unpack(y, out_dims, case.get("out_strides"), case.get("out_batch_stride"), batch)
+    return {"err": rel_l2(got, ref), "launches": n}
 
 
 def main():

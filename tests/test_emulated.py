@@ -72,6 +72,22 @@ CASES = [
     dict(kind="slab", mode="c2c", dims=[8, 8, 8], batch=1, prec="F64", nranks=1),
     dict(kind="slab", mode="c2c", dims=[4099 * 2, 4, 3], batch=1, prec="F32", nranks=2),
     dict(kind="slab", mode="c2c_inv", dims=[4099 * 2, 4, 3], batch=1, prec="F32", nranks=2, normalize=True),
+    # zero padding (spatial / frequency, every boundary) and formatted buffer strides
+    dict(kind="bnd", mode="c2c", dims=[64], batch=3, prec="F64", pad={"0": [40, 64]}),
+    dict(kind="bnd", mode="c2c_inv", dims=[64], batch=3, prec="F64", pad={"0": [10, 20]}, normalize=True),
+    dict(kind="bnd", mode="c2c", dims=[16, 12, 10], batch=2, prec="F64", pad={"0": [8, 16], "1": [6, 12], "2": [5, 10]}),
+    dict(kind="bnd", mode="c2c", dims=[16, 12], batch=2, prec="F64", pad={"1": [6, 12]}, domain="frequency"),
+    dict(kind="bnd", mode="c2c_inv", dims=[16, 12], batch=2, prec="F64", pad={"0": [3, 5]}, domain="frequency"),
+    dict(kind="bnd", mode="r2c", dims=[34], batch=2, prec="F64", pad={"0": [7, 13]}),
+    dict(kind="bnd", mode="c2r", dims=[34], batch=2, prec="F64", pad={"0": [7, 13]}),
+    dict(kind="bnd", mode="r2c", dims=[6, 8], batch=2, prec="F64", pad={"0": [1, 2], "1": [2, 4]}),
+    dict(kind="bnd", mode="c2c", dims=[8, 10], batch=3, prec="F64", in_strides={"0": 13}, in_batch_stride=120,
+         out_strides={"0": 11}, out_batch_stride=100),
+    dict(kind="bnd", mode="r2c", dims=[6, 8], batch=2, prec="F32", in_strides={"0": 9}, out_strides={"0": 7},
+         out_batch_stride=50, pad={"0": [1, 2]}),
+    dict(kind="bnd", mode="c2r", dims=[6, 8], batch=2, prec="F64", in_strides={"0": 6}, in_batch_stride=40,
+         out_strides={"0": 10}),
+    dict(kind="bnd", mode="c2c", dims=[4099], batch=2, prec="F32", pad={"0": [2000, 4099]}),
 ]
 
 
@@ -82,7 +98,8 @@ def results():
 
 
 @pytest.mark.parametrize("i", range(len(CASES)), ids=[f"{c['kind']}{'-' + c['mode'] if 'mode' in c else ''}-{c['dims']}-{c['prec']}"
-                              + (f"-P{c['nranks']}" if "nranks" in c else "") for c in CASES])
+                              + (f"-P{c['nranks']}" if "nranks" in c else "") + (f"-pad{c['pad']}" if "pad" in c else "")
+                              + ("-strided" if "in_strides" in c or "out_strides" in c else "") for c in CASES])
 def test_emulated_program_matches_oracle(results, i):
     r = results[i]
     assert "error" not in r, r

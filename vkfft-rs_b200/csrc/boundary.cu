@@ -1,0 +1,24 @@
+// Boundary copy kernel: gathers a caller's (formatted, zero-padded) input into a dense
+// scratch tensor, or scatters a dense result into the caller's formatted output with the
+// zero-padding interval applied.  One thread per logical element, grid-stride.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "pass_device.cuh"
+
+namespace b200fft {
+
+__global__ void __launch_bounds__(256) boundary_copy_kernel(const __grid_constant__ BoundaryCopy b) {
+    for (int64_t L = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; L < b.total; L += (int64_t)gridDim.x * blockDim.x)
+        boundary_copy_one(b, L);
+}
+
+cudaError_t launch_boundary_copy(const BoundaryCopy &b, cudaStream_t stream) {
+    if (b.total <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((b.total + 255) / 256, 148 * 32);
+    boundary_copy_kernel<<<(unsigned)blocks, 256, 0, stream>>>(b);
+    return cudaGetLastError();
+}
+
+}  // namespace b200fft

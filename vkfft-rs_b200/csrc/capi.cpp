@@ -225,11 +225,17 @@ b200fft_status b200fft_transform_build(const b200fft_config *config, int32_t dir
     });
 }
 
+// Drops the uploaded tables of a transform and of its sub-batch and dense twins.
+static void forget_transform(const Transform &t) {
+    forget_program(t.id);
+    for (auto &kv : t.chunks)
+        if (kv.second) forget_transform(*kv.second);
+    if (t.dense_twin) forget_transform(*t.dense_twin);
+}
+
 void b200fft_transform_destroy(b200fft_transform *transform) {
     if (!transform) return;
-    forget_program(transform->t->id);
-    for (auto &kv : transform->t->chunks)
-        if (kv.second) forget_program(kv.second->id);
+    forget_transform(*transform->t);
     delete transform;
 }
 
@@ -259,8 +265,12 @@ b200fft_status b200fft_transform_axis_child_info(const b200fft_transform *t, uin
     });
 }
 
-uint64_t b200fft_transform_input_elements(const b200fft_transform *t) { return t ? t->t->prog.input_elems : 0; }
-uint64_t b200fft_transform_output_elements(const b200fft_transform *t) { return t ? t->t->prog.output_elems : 0; }
+uint64_t b200fft_transform_input_elements(const b200fft_transform *t) { return t ? t->t->logical_in_elems : 0; }
+uint64_t b200fft_transform_output_elements(const b200fft_transform *t) { return t ? t->t->logical_out_elems : 0; }
+uint64_t b200fft_transform_input_buffer_elements(const b200fft_transform *t) { return t ? t->t->prog.input_elems : 0; }
+uint64_t b200fft_transform_output_buffer_elements(const b200fft_transform *t) {
+    return t ? t->t->prog.output_elems : 0;
+}
 int32_t b200fft_transform_input_is_real(const b200fft_transform *t) { return t ? t->t->prog.input_real : 0; }
 int32_t b200fft_transform_output_is_real(const b200fft_transform *t) { return t ? t->t->prog.output_real : 0; }
 uint64_t b200fft_transform_workspace_bytes(const b200fft_transform *t) { return t ? t->t->prog.scratch_bytes() : 0; }

@@ -134,4 +134,22 @@ struct PassParams : PassShape {
     Op ops[kMaxOps];
 };
 
+// Boundary copy between a caller's buffer and a dense scratch tensor, with the
+// zero-padding interval applied (zero_pad_ir.rs: elements whose coordinate on any padded
+// axis lies in [pad_lo, pad_hi) become zero) and formatted buffer strides
+// (config.rs:893-1002: per-axis stored-element strides and a batch stride).  Element L of
+// the batch-major logical tensor has coordinates (batch, c_0 .. c_{rank-1}), fastest last.
+constexpr int kMaxCopyRank = 8;
+struct BoundaryCopy {
+    const void *src;
+    void *dst;
+    int64_t total;       // logical elements over all batches
+    int32_t rank;
+    int32_t elem_bytes;  // 4, 8 or 16
+    int64_t dims[kMaxCopyRank];
+    int64_t src_stride[kMaxCopyRank], dst_stride[kMaxCopyRank];
+    int64_t src_batch, dst_batch;
+    int64_t pad_lo[kMaxCopyRank], pad_hi[kMaxCopyRank];
+};
+
 }  // namespace b200fft

@@ -530,4 +530,29 @@ __device__ __forceinline__ void run_op(const PassShape &p, const Op &op, cplx<T>
     }
 }
 
+// One element of a boundary copy (pass_desc.hpp BoundaryCopy).
+B200FFT_HD void boundary_copy_one(const BoundaryCopy &b, int64_t L) {
+    int64_t so = 0, dof = 0;
+    bool zero = false;
+    for (int a = b.rank - 1; a >= 0; a--) {
+        const int64_t c = L % b.dims[a];
+        L /= b.dims[a];
+        so += c * b.src_stride[a];
+        dof += c * b.dst_stride[a];
+        zero |= c >= b.pad_lo[a] && c < b.pad_hi[a];
+    }
+    so += L * b.src_batch;
+    dof += L * b.dst_batch;
+    if (b.elem_bytes == 16) {
+        double2 v = zero ? double2{0.0, 0.0} : reinterpret_cast<const double2 *>(b.src)[so];
+        reinterpret_cast<double2 *>(b.dst)[dof] = v;
+    } else if (b.elem_bytes == 8) {
+        unsigned long long v = zero ? 0ull : reinterpret_cast<const unsigned long long *>(b.src)[so];
+        reinterpret_cast<unsigned long long *>(b.dst)[dof] = v;
+    } else {
+        unsigned v = zero ? 0u : reinterpret_cast<const unsigned *>(b.src)[so];
+        reinterpret_cast<unsigned *>(b.dst)[dof] = v;
+    }
+}
+
 }  // namespace b200fft

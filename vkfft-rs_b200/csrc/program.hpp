@@ -15,8 +15,17 @@
 
 namespace b200fft {
 
-enum BufId : int { BUF_IN = 0, BUF_OUT = 1, BUF_SCRATCH0 = 2, BUF_SCRATCH1 = 3, BUF_SCRATCH2 = 4, BUF_SCRATCH3 = 5 };
-constexpr int kScratchBuffers = 4;
+enum BufId : int {
+    BUF_IN = 0,
+    BUF_OUT = 1,
+    BUF_SCRATCH0 = 2,  // four-step / Bluestein intermediate
+    BUF_SCRATCH1 = 3,  // ND C2R / convolution working copy
+    BUF_SCRATCH2 = 4,  // real even-half child output
+    BUF_SCRATCH3 = 5,  // pass-level Rader lines
+    BUF_SCRATCH4 = 6,  // dense input behind a boundary copy (zero padding / formatted strides)
+    BUF_SCRATCH5 = 7,  // dense output in front of a boundary copy
+};
+constexpr int kScratchBuffers = 6;
 
 struct HostTable {
     bool is_int = false;
@@ -30,7 +39,7 @@ struct HostTable {
     }
 };
 
-enum KernelKind : int { KERNEL_PASS = 0, KERNEL_REG = 1 };
+enum KernelKind : int { KERNEL_PASS = 0, KERNEL_REG = 1, KERNEL_COPY = 2 };
 
 struct PassPlan {
     int kernel = KERNEL_PASS;     // KERNEL_REG: register-resident Stockham (reg_kernels.cu)
@@ -42,6 +51,7 @@ struct PassPlan {
                                   // input is not 16-byte aligned for the bulk copies
     bool reg_in_real = false, reg_out_real = false;
     PassParams p{};               // device pointers are patched at upload / launch
+    BoundaryCopy bc{};            // KERNEL_COPY parameters (pointers patched at launch)
     int op_tables[kMaxOps][3];    // table ids per op (lut, lut2, lut3) or -1
     int src_buf = BUF_IN, dst_buf = BUF_OUT;
     int64_t src_off = 0, dst_off = 0;  // element offsets (units of the side's element type)
@@ -58,7 +68,7 @@ struct Program {
     std::vector<PassPlan> passes;
     std::vector<HostTable> tables;
     std::map<std::string, int> table_cache;
-    size_t scratch_elems[kScratchBuffers] = {0, 0, 0, 0};  // complex elements of the compute precision
+    size_t scratch_elems[kScratchBuffers] = {};  // complex elements of the compute precision
     size_t input_elems = 0, output_elems = 0;
     bool input_real = false, output_real = false;
     double algorithmic_flops = 0;  // 5 N log2 N per complex transform (for reports)

@@ -14,6 +14,7 @@ cudaError_t launch_pass(int variant, const PassParams &p, int64_t grid, int thre
 void set_kernel_smem_limits();
 void set_reg_kernel_smem_limits();
 cudaError_t launch_reg(int variant, const RegParams &rp, cudaStream_t stream);
+cudaError_t launch_boundary_copy(const BoundaryCopy &b, cudaStream_t stream);
 
 // ---- host-side fault injection (no GPU fault is ever provoked) ------------------
 // B200FFT_FAULT=alloc:<n> or launch:<n> makes the n-th device allocation or kernel
@@ -219,6 +220,13 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
     const int variant = kernel_variant_for(prog.is_double);
     for (size_t pi = 0; pi < prog.passes.size(); pi++) {
         const PassPlan &pp = prog.passes[pi];
+        if (pp.kernel == KERNEL_COPY) {
+            BoundaryCopy bc = pp.bc;
+            bc.src = bufs[pp.src_buf];
+            bc.dst = bufs[pp.dst_buf];
+            check(launch_boundary_copy(bc, stream), "kernel launch");
+            continue;
+        }
         if (pp.kernel == KERNEL_REG) {
             RegParams rp = pp.rp;
             rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * (pp.reg_in_real ? esz / 2 : esz);
@@ -345,8 +353,25 @@ static Transform *chunk_transform(Transform &t, size_t batch) {
     return t.chunks.emplace(batch, std::move(c)).first->second.get();
 }
 
-void execute_transform_host(Context *ctx, Transform &t, const void *in, size_t in_bytes, void *out,
+// Host arrays are logical tensors (the reference packs formatted layouts internally,
+// nd_real_ir.rs:715-750): a transform with formatted buffer strides runs its dense twin.
+static Transform &host_view(Transform &t) {
+    if (!t.formatted) return t;
+    std::lock_guard<std::mutex> g(t.chunk_mu);
+    if (!t.dense_twin) {
+        FftConfig cfg = t.config;
+        for (auto &v : cfg.input_buffer_axis_strides) v.reset();
+        for (auto &v : cfg.output_buffer_axis_strides) v.reset();
+        cfg.input_buffer_batch_stride.reset();
+        cfg.output_buffer_batch_stride.reset();
+        t.dense_twin = build_transform(cfg, t.direction, t.device);
+    }
+    return *t.dense_twin;
+}
+
+void execute_transform_host(Context *ctx, Transform &t_in, const void *in, size_t in_bytes, void *out,
                             size_t out_bytes) {
+    Transform &t = host_view(t_in);
     const Program &prog = t.prog;
     const size_t esz = prog.is_double ? 16 : 8;
     const size_t in_need = prog.input_elems * (prog.input_real ? esz / 2 : esz);

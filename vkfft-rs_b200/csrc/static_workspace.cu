@@ -18,6 +18,7 @@ namespace b200fft {
 int kernel_variant_for(bool is_double);
 cudaError_t launch_pass(int variant, const PassParams &p, int64_t grid, int threads, size_t smem, cudaStream_t stream);
 cudaError_t launch_reg(int variant, const RegParams &rp, cudaStream_t stream);
+cudaError_t launch_boundary_copy(const BoundaryCopy &b, cudaStream_t stream);
 
 constexpr size_t kStaticWorkspaceBytes = size_t(16) << 20;  // B200FFT_STATIC_WORKSPACE_BYTES
 constexpr int kMaxStaticDevices = 64;
@@ -106,6 +107,13 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scr + prog.scratch_offset(k);
     const int variant = kernel_variant_for(prog.is_double);
     for (const PassPlan &pp : prog.passes) {
+        if (pp.kernel == KERNEL_COPY) {
+            BoundaryCopy bc = pp.bc;
+            bc.src = bufs[pp.src_buf];
+            bc.dst = bufs[pp.dst_buf];
+            check(launch_boundary_copy(bc, stream), "kernel launch");
+            continue;
+        }
         if (pp.kernel == KERNEL_REG) {
             RegParams rp = pp.rp;
             rp.in = static_cast<const unsigned char *>(bufs[pp.src_buf]) + pp.src_off * (pp.reg_in_real ? esz / 2 : esz);

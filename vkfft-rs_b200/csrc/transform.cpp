@@ -34,13 +34,114 @@ static void check_executable(const FftConfig &c) {
         fail_precision("B200 engine", precision_name(c.precision));
     if (!(c.transform == TransformKind::C2C || c.transform == TransformKind::R2C || c.transform == TransformKind::C2R))
         fail_unsupported("B200 engine executes C2C, R2C and C2R transforms (R2R is outside the FFT hot path)");
-    for (auto &z : c.zero_padding)
-        if (z) fail_unsupported("B200 engine: zero padding is not implemented yet");
-    if (c.has_formatted_strides()) fail_unsupported("B200 engine: formatted buffer strides are not implemented yet");
     if (c.kernel_convolution) fail_unsupported("B200 engine: kernelConvolution preparation is not implemented yet");
 }
 
+static std::vector<int64_t> dense_strides(const std::vector<size_t> &dims) {
+    std::vector<int64_t> st(dims.size(), 1);
+    for (size_t a = dims.size() - 1; a-- > 0;) st[a] = st[a + 1] * (int64_t)dims[a + 1];
+    return st;
+}
+
+// Zero padding (zero_pad_ir.rs) and formatted buffer strides (config.rs:893-1002,
+// nd_ir.rs:1190-1260) at the transform's boundary: the lowered program reads a dense
+// scratch copy of the input gathered from the caller's buffer (padding of the input
+// boundary applied) and/or writes a dense scratch result scattered to the caller's
+// buffer (padding of the output boundary applied).  Spatial padding owns the forward
+// input / inverse output, frequency padding the forward output / inverse input; real
+// transforms pad their real side.
+static void add_boundaries(Transform &t) {
+    const FftConfig &c = t.plan.config;
+    Program &prog = t.prog;
+    const bool r2c = c.transform == TransformKind::R2C, c2r = c.transform == TransformKind::C2R;
+    const bool inverse = t.direction == B200FFT_INVERSE;
+    std::vector<size_t> compact = c.dimensions;
+    compact.back() = compact.back() / 2 + 1;
+    const std::vector<size_t> &in_dims = c2r ? compact : c.dimensions;
+    const std::vector<size_t> &out_dims = r2c ? compact : c.dimensions;
+    bool any_pad = false;
+    for (auto &z : c.zero_padding) any_pad |= z.has_value();
+    bool pad_in = false, pad_out = false;
+    if (any_pad) {
+        if (r2c || c2r)
+            (r2c ? pad_in : pad_out) = true;
+        else
+            ((c.zero_padding_domain == ZeroPaddingDomain::Spatial) != inverse ? pad_in : pad_out) = true;
+    }
+    bool fmt_in = c.input_buffer_batch_stride.has_value(), fmt_out = c.output_buffer_batch_stride.has_value();
+    for (auto &v : c.input_buffer_axis_strides) fmt_in |= v.has_value();
+    for (auto &v : c.output_buffer_axis_strides) fmt_out |= v.has_value();
+    t.logical_in_elems = prog.input_elems;
+    t.logical_out_elems = prog.output_elems;
+    t.formatted = fmt_in || fmt_out;
+    if (!pad_in && !pad_out && !fmt_in && !fmt_out) return;
+    if (c.dimensions.size() > (size_t)kMaxCopyRank) fail_unsupported("boundary copies support rank <= 8");
+    const size_t batch = c.kernel_preparation_system_count();
+    const size_t esz = prog.is_double ? 16 : 8;
+    auto copy = [&](const std::vector<size_t> &dims, bool input, bool pad, size_t elem_bytes, int src, int dst) {
+        PassPlan pp{};
+        pp.kernel = KERNEL_COPY;
+        BoundaryCopy &b = pp.bc;
+        const std::vector<size_t> fst = c.resolved_axis_strides(dims, input);
+        const size_t fbatch = c.resolved_batch_stride(dims, input);
+        const std::vector<int64_t> dst_dense = dense_strides(dims);
+        size_t tensor = 1;
+        for (size_t d : dims) tensor *= d;
+        b.total = (int64_t)(tensor * batch);
+        b.rank = (int32_t)dims.size();
+        b.elem_bytes = (int32_t)elem_bytes;
+        for (size_t a = 0; a < dims.size(); a++) {
+            b.dims[a] = (int64_t)dims[a];
+            const int64_t formatted = (int64_t)fst[a], dense = dst_dense[a];
+            b.src_stride[a] = input ? formatted : dense;
+            b.dst_stride[a] = input ? dense : formatted;
+            b.pad_lo[a] = b.pad_hi[a] = 0;
+            if (pad && c.zero_padding[a]) {
+                b.pad_lo[a] = (int64_t)c.zero_padding[a]->left;
+                b.pad_hi[a] = (int64_t)c.zero_padding[a]->right;
+            }
+        }
+        b.src_batch = input ? (int64_t)fbatch : (int64_t)tensor;
+        b.dst_batch = input ? (int64_t)tensor : (int64_t)fbatch;
+        pp.src_buf = src;
+        pp.dst_buf = dst;
+        pp.label = input ? "boundary gather" : "boundary scatter";
+        for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
+        return std::make_pair(pp, fbatch * batch);
+    };
+    if (pad_in || fmt_in) {
+        const size_t eb = r2c ? esz / 2 : esz;
+        for (PassPlan &pp : prog.passes)
+            if (pp.src_buf == BUF_IN) pp.src_buf = BUF_SCRATCH4;
+        auto [pp, physical] = copy(in_dims, true, pad_in, eb, BUF_IN, BUF_SCRATCH4);
+        prog.scratch_elems[4] = (prog.input_elems * eb + esz - 1) / esz;
+        prog.passes.insert(prog.passes.begin(), pp);
+        prog.input_elems = physical;
+    }
+    if (pad_out || fmt_out) {
+        const size_t eb = c2r ? esz / 2 : esz;
+        for (PassPlan &pp : prog.passes) {
+            if (pp.src_buf == BUF_OUT) pp.src_buf = BUF_SCRATCH5;
+            if (pp.dst_buf == BUF_OUT) pp.dst_buf = BUF_SCRATCH5;
+        }
+        auto [pp, physical] = copy(out_dims, false, pad_out, eb, BUF_SCRATCH5, BUF_OUT);
+        prog.scratch_elems[5] = (prog.output_elems * eb + esz - 1) / esz;
+        prog.passes.push_back(pp);
+        prog.output_elems = physical;
+    }
+}
+
+static std::unique_ptr<Transform> build_transform_core(const FftConfig &config_in, int direction,
+                                                       const DeviceProfile &device);
+
 std::unique_ptr<Transform> build_transform(const FftConfig &config_in, int direction, const DeviceProfile &device) {
+    auto t = build_transform_core(config_in, direction, device);
+    add_boundaries(*t);
+    return t;
+}
+
+static std::unique_ptr<Transform> build_transform_core(const FftConfig &config_in, int direction,
+                                                       const DeviceProfile &device) {
     if (config_in.transform == TransformKind::R2C && direction != B200FFT_FORWARD)
         fail_unsupported("RealToComplex is a forward transform; use Direction::Forward");
     if (config_in.transform == TransformKind::C2R && direction != B200FFT_INVERSE)

@@ -26,6 +26,11 @@ struct Transform {
     // null when planning the sub-batch changes the executed algorithm
     std::mutex chunk_mu;
     std::map<size_t, std::unique_ptr<Transform>> chunks;
+    // logical (host-API) element counts; prog.input_elems / output_elems are the device
+    // buffers', which differ with formatted strides
+    size_t logical_in_elems = 0, logical_out_elems = 0;
+    bool formatted = false;
+    std::unique_ptr<Transform> dense_twin;  // same transform on dense buffers (host API)
 };
 
 std::unique_ptr<Transform> build_transform(const FftConfig &config, int direction, const DeviceProfile &device);

@@ -121,6 +121,12 @@ class RaderMode(enum.IntEnum):
     DIRECT_MULTIPLICATION = 1
 
 
+class ZeroPaddingDomain(enum.IntEnum):
+    """config.rs:548-555: which transform boundary owns the zero-padding interval."""
+    SPATIAL = 0
+    FREQUENCY = 1
+
+
 class RealFftAlgorithm(enum.IntEnum):
     FULL_COMPLEX = 0
     EVEN_HALF_SIZE = 1
@@ -238,6 +244,8 @@ def library():
         "b200fft_transform_axis_child_info": ([vp, u32, P(_AxisInfo)], i32),
         "b200fft_transform_input_elements": ([vp], u64),
         "b200fft_transform_output_elements": ([vp], u64),
+        "b200fft_transform_input_buffer_elements": ([vp], u64),
+        "b200fft_transform_output_buffer_elements": ([vp], u64),
         "b200fft_transform_input_is_real": ([vp], i32),
         "b200fft_transform_output_is_real": ([vp], i32),
         "b200fft_transform_workspace_bytes": ([vp], u64),
@@ -471,6 +479,9 @@ class FftConfig:
         c._s.zero_padding_right[axis] = right
         return c
 
+    def with_zero_padding_domain(self, domain):
+        return self._set(zero_padding_domain=int(domain))
+
     def with_omit_dimension(self, axis, omit):
         self._axis_check(axis, "omitDimension axis")
         c = self._copy()
@@ -669,6 +680,15 @@ class TransformIr:
     @property
     def output_elements(self):
         return int(library().b200fft_transform_output_elements(self._h))
+
+    @property
+    def input_buffer_elements(self):
+        """Device input buffer size (formatted strides: batch_stride x batch)."""
+        return int(library().b200fft_transform_input_buffer_elements(self._h))
+
+    @property
+    def output_buffer_elements(self):
+        return int(library().b200fft_transform_output_buffer_elements(self._h))
 
     @property
     def input_is_real(self):
