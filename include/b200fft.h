@@ -388,6 +388,21 @@ b200fft_status b200fft_slab_connect(b200fft_context *context, b200fft_slab *slab
 b200fft_status b200fft_execute_slab(b200fft_context *context, b200fft_slab *slab, const void *input,
                                     void *output, void *workspace, void *stream);
 
+/* ---- asynchronous submission (NativeAsyncRuntime, native_runtime.rs:362-451) -------
+ * submit_transform_f32_async / _f64_async: queues a host execution with the semantics of
+ * b200fft_execute_host and returns a ticket at once.  The input array must stay alive and
+ * unchanged, and the output array unread, until the ticket is waited for.  Submissions on
+ * one context run in submission order on a worker thread; the transform must outlive its
+ * tickets.  b200fft_ticket_wait returns the execution's status (the error text through
+ * b200fft_last_error_string on the waiting thread) and frees the ticket; _destroy waits
+ * and frees without reporting. */
+typedef struct b200fft_ticket b200fft_ticket;
+b200fft_status b200fft_submit_host(b200fft_context *context, b200fft_transform *transform,
+                                   const void *input, size_t input_bytes, void *output,
+                                   size_t output_bytes, b200fft_ticket **ticket);
+b200fft_status b200fft_ticket_wait(b200fft_ticket *ticket);
+void b200fft_ticket_destroy(b200fft_ticket *ticket);
+
 /* Waits for the stream (NULL: the context's) and reports any error the context's kernels
  * recorded since the last check (bounded waits that expired, invalid programs) as
  * NativeRuntime, clearing it. */

@@ -266,3 +266,20 @@ def test_input_length_mismatch_is_reported(V, ctx):
     lib = V.library()
     st = lib.b200fft_execute_host(ctx._h, ir._h, x.ctypes.data, x.nbytes, out.ctypes.data, out.nbytes)
     assert st == V.Status.InputLengthMismatch
+
+
+@pytest.mark.gpu
+def test_async_submissions_match_synchronous_execution(V, ctx):
+    """NativeAsyncRuntime tickets: several submissions in flight, waited for in any order,
+    each equal to the synchronous execution of its own input; errors surface at wait()."""
+    dev = ctx.device_profile()
+    irs = [V.TransformIr.build(V.FftConfig([n]).with_batch_count(b), V.Direction.FORWARD, dev)
+           for n, b in ((4096, 256), (4099, 16), (1000, 40))]
+    rng = np.random.default_rng(5)
+    xs = [uniform_complex(rng, (ir.input_elements,), np.complex64) for ir in irs]
+    tickets = [ctx.submit_transform(ir, x) for ir, x in zip(irs, xs)]
+    for ir, x, t in reversed(list(zip(irs, xs, tickets))):
+        assert np.array_equal(t.wait(), ctx.execute_transform(ir, x))
+    bad = ctx.submit_transform(irs[0], xs[0], out=np.empty(irs[0].output_elements - 1, dtype=np.complex64))
+    with pytest.raises(V.VkFftError):
+        bad.wait()

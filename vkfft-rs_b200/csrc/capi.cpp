@@ -24,6 +24,9 @@ struct b200fft_convolution {
 struct b200fft_slab {
     std::unique_ptr<Slab> s;
 };
+struct b200fft_ticket {
+    std::shared_ptr<Ticket> t;
+};
 
 static thread_local std::string g_last_error;
 
@@ -485,4 +488,35 @@ int32_t b200fft_transform_compile_check(const b200fft_transform *transform, char
         log[capacity - 1] = 0;
     }
     return n;
+}
+
+b200fft_status b200fft_submit_host(b200fft_context *context, b200fft_transform *transform, const void *input,
+                                   size_t input_bytes, void *output, size_t output_bytes, b200fft_ticket **ticket) {
+    return guarded([&] {
+        need(context, "context");
+        need(transform, "transform");
+        need(input, "input");
+        need(output, "output");
+        need(ticket, "ticket");
+        *ticket = new b200fft_ticket{
+            submit_transform_host(context->ctx, *transform->t, input, input_bytes, output, output_bytes)};
+    });
+}
+
+b200fft_status b200fft_ticket_wait(b200fft_ticket *ticket) {
+    if (!ticket) {
+        g_last_error = "ticket must not be null";
+        return B200FFT_VALUE_OUT_OF_RANGE;
+    }
+    wait_ticket(*ticket->t);
+    const b200fft_status st = static_cast<b200fft_status>(ticket->t->status);
+    if (st != B200FFT_OK) g_last_error = ticket->t->message;
+    delete ticket;
+    return st;
+}
+
+void b200fft_ticket_destroy(b200fft_ticket *ticket) {
+    if (!ticket) return;
+    wait_ticket(*ticket->t);
+    delete ticket;
 }

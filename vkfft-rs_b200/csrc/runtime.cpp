@@ -112,6 +112,14 @@ void context_destroy(Context *ctx) {
         std::lock_guard<std::mutex> g(g_ctx_mu);
         g_contexts.erase(ctx);
     }
+    if (ctx->worker.joinable()) {  // finish every submitted job first
+        {
+            std::lock_guard<std::mutex> l(ctx->job_mu);
+            ctx->stopping = true;
+        }
+        ctx->job_cv.notify_all();
+        ctx->worker.join();
+    }
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     for (auto &kv : ctx->tables) cudaFree(kv.second.base);
@@ -371,6 +379,7 @@ static Transform &host_view(Transform &t) {
 
 void execute_transform_host(Context *ctx, Transform &t_in, const void *in, size_t in_bytes, void *out,
                             size_t out_bytes) {
+    std::lock_guard<std::mutex> host_lock(ctx->host_mu);  // the worker thread may run one too
     Transform &t = host_view(t_in);
     const Program &prog = t.prog;
     const size_t esz = prog.is_double ? 16 : 8;
@@ -426,6 +435,57 @@ void execute_transform_host(Context *ctx, Transform &t_in, const void *in, size_
         check(cudaStreamSynchronize(cudaStreamLegacy), "stream synchronize");
         fail_runtime(describe_error_word(err));
     }
+}
+
+// ---- asynchronous submissions ----------------------------------------------------------
+
+static void worker_loop(Context *ctx) {
+    for (;;) {
+        std::function<void()> job;
+        {
+            std::unique_lock<std::mutex> l(ctx->job_mu);
+            ctx->job_cv.wait(l, [&] { return ctx->stopping || !ctx->jobs.empty(); });
+            if (ctx->jobs.empty()) return;  // stopping and drained
+            job = std::move(ctx->jobs.front());
+            ctx->jobs.pop_front();
+        }
+        job();
+    }
+}
+
+std::shared_ptr<Ticket> submit_transform_host(Context *ctx, Transform &t, const void *in, size_t in_bytes, void *out,
+                                              size_t out_bytes) {
+    auto ticket = std::make_shared<Ticket>();
+    auto job = [ctx, &t, in, in_bytes, out, out_bytes, ticket] {
+        int status = 0;
+        std::string message;
+        try {
+            execute_transform_host(ctx, t, in, in_bytes, out, out_bytes);
+        } catch (const FftError &e) {
+            status = e.code;
+            message = e.message;
+        } catch (const std::exception &e) {
+            status = B200FFT_NATIVE_RUNTIME;
+            message = std::string("CUDA runtime error: ") + e.what();
+        }
+        std::lock_guard<std::mutex> l(ticket->mu);
+        ticket->status = status;
+        ticket->message = std::move(message);
+        ticket->done = true;
+        ticket->cv.notify_all();
+    };
+    {
+        std::lock_guard<std::mutex> l(ctx->job_mu);
+        if (!ctx->worker.joinable()) ctx->worker = std::thread(worker_loop, ctx);
+        ctx->jobs.push_back(std::move(job));
+    }
+    ctx->job_cv.notify_one();
+    return ticket;
+}
+
+void wait_ticket(Ticket &t) {
+    std::unique_lock<std::mutex> l(t.mu);
+    t.cv.wait(l, [&] { return t.done; });
 }
 
 }  // namespace b200fft

@@ -5,8 +5,13 @@
 
 #include <cuda_runtime.h>
 
+#include <condition_variable>
+#include <deque>
+#include <functional>
+#include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <unordered_map>
 
 #include "transform.hpp"
@@ -36,6 +41,13 @@ struct Context {
     size_t scratch_bytes = 0;
     void *stage_in = nullptr, *stage_out = nullptr;
     size_t stage_in_bytes = 0, stage_out_bytes = 0;
+    std::mutex host_mu;  // host executions (staging buffers, pipeline streams) one at a time
+    // asynchronous submissions: one worker thread runs them in submission order
+    std::mutex job_mu;
+    std::condition_variable job_cv;
+    std::deque<std::function<void()>> jobs;
+    std::thread worker;
+    bool stopping = false;
     // pipelined host execution: streams and per-slot staging (input, output, scratch)
     static constexpr int kPipeSlots = 3;
     cudaStream_t pipe[kPipeSlots] = {};
@@ -55,6 +67,20 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
 // Stream-ordered execution out of the library's static device region (allocates nothing).
 void execute_program_static(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out,
                             cudaStream_t stream);
+// Result of an asynchronous submission (NativeAsyncRuntime tickets, native_runtime.rs:362-451).
+struct Ticket {
+    std::mutex mu;
+    std::condition_variable cv;
+    bool done = false;
+    int status = 0;
+    std::string message;
+};
+// Queues a host execution (copy semantics) on the context's worker; the arrays must
+// stay valid until the ticket is waited for.
+std::shared_ptr<Ticket> submit_transform_host(Context *ctx, Transform &t, const void *in, size_t in_bytes, void *out,
+                                              size_t out_bytes);
+void wait_ticket(Ticket &t);
+
 // Waits for the stream (null: the context's) and turns a recorded kernel error into
 // a NativeRuntime error (clearing it).
 void context_synchronize(Context *ctx, cudaStream_t stream);

@@ -272,6 +272,9 @@ def library():
         "b200fft_slab_connect": ([vp, vp, vp], i32),
         "b200fft_execute_slab": ([vp, vp, vp, vp, vp, vp], i32),
         "b200fft_context_synchronize": ([vp, vp], i32),
+        "b200fft_submit_host": ([vp, vp, vp, ctypes.c_size_t, vp, ctypes.c_size_t, P(vp)], i32),
+        "b200fft_ticket_wait": ([vp], i32),
+        "b200fft_ticket_destroy": ([vp], None),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -844,6 +847,30 @@ class SlabTransform:
         return (real if self.input_is_real else cplx), (real if self.output_is_real else cplx)
 
 
+class AsyncTransformTicket:
+    """NativeAsyncTransformTicket32/64 (native_runtime.rs:372-401): wait() returns the
+    output array once the submitted execution has finished."""
+
+    def __init__(self, handle, keep, out):
+        self._h = handle
+        self._keep = keep  # the arrays stay alive while the execution may use them
+        self._out = out
+
+    def wait(self):
+        h, self._h = self._h, None
+        if h is None:
+            raise VkFftError(Status.ValueOutOfRange, "ticket was already waited for")
+        _check(library().b200fft_ticket_wait(h))
+        self._keep = None
+        return self._out
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h and _lib is not None:
+            _lib.b200fft_ticket_destroy(h)
+            self._h = None
+
+
 class CudaExecutionContext:
     """backend/cuda/runtime.rs:959-2840"""
 
@@ -895,6 +922,17 @@ class CudaExecutionContext:
         _check(library().b200fft_execute_host(self._h, ir._h, x.ctypes.data, x.nbytes,
                                               out.ctypes.data, out.nbytes))
         return out
+
+    def submit_transform(self, ir, data, out=None):
+        """submit_transform_f32_async / _f64_async (native_runtime.rs:424-451): starts the
+        host execution and returns an AsyncTransformTicket at once."""
+        x = np.ascontiguousarray(data, dtype=ir.input_dtype())
+        if out is None:
+            out = np.empty(ir.output_elements, dtype=ir.output_dtype())
+        h = ctypes.c_void_p()
+        _check(library().b200fft_submit_host(self._h, ir._h, x.ctypes.data, x.nbytes, out.ctypes.data, out.nbytes,
+                                             ctypes.byref(h)))
+        return AsyncTransformTicket(h, (x, ir), out)
 
     # typed aliases matching the reference's two entry points
     def execute_transform_f32(self, ir, data):
