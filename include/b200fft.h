@@ -324,17 +324,29 @@ b200fft_status b200fft_execute_host(b200fft_context *context, b200fft_transform 
 
 /* ---- FFT convolution (convolution_ir.rs, native_runtime.rs:257-337) ----- */
 typedef struct b200fft_convolution b200fft_convolution;
-/* NdRealConvolutionIr::build_from_spectrum (convolution_ir.rs:3885): config has
- * perform_convolution = 1, transform = R2C, rank >= 2, batch 1, coordinate_features C.
- * kernel_spectrum: host array in the reference layout, C copies of the compact R2C
- * spectrum (C * prod(dims[:-1]) * (dims[-1]/2+1) complex values), or 1 copy which is
- * broadcast to every coordinate.  spectrum_copies is 1 or C. */
+/* build_from_spectrum of the reference's convolution applications; config has
+ * perform_convolution = 1 and selects the family:
+ *  - transform R2C, rank >= 2: NdRealConvolutionIr (convolution_ir.rs:3867-4250), batch 1,
+ *    coordinate_features C, K kernels: kernel_spectrum holds K*C compact R2C spectra
+ *    (prod(dims[:-1]) * (dims[-1]/2+1) complex values each), or 1 broadcast to every system;
+ *    spectrum_copies is 1 or K*C.
+ *  - transform C2C, rank 1: ConvolutionIr (:2520-3626); rank >= 2: NdConvolutionIr
+ *    (:3627-3866): kernel_spectrum holds planes*K tensors of prod(dims) complex values
+ *    (planes = 1, or the 2x2 / 3x3 matrix planes, 3 for a symmetric 2x2);
+ *    spectrum_copies = planes*K.
+ * The input holds batch x coordinates systems, the output (K > 1 ? K : batch) x
+ * coordinates systems; the inverse transform is normalised. */
 b200fft_status b200fft_convolution_build(const b200fft_config *config,
                                          const b200fft_device_profile *device,
                                          const void *kernel_spectrum, uint64_t spectrum_copies,
                                          b200fft_convolution **convolution);
 void b200fft_convolution_destroy(b200fft_convolution *convolution);
 uint64_t b200fft_convolution_workspace_bytes(const b200fft_convolution *convolution);
+/* Element counts of the input / output arrays (real for the ND real convolution, complex
+ * for ConvolutionIr / NdConvolutionIr). */
+uint64_t b200fft_convolution_input_elements(const b200fft_convolution *convolution);
+uint64_t b200fft_convolution_output_elements(const b200fft_convolution *convolution);
+int32_t b200fft_convolution_input_is_real(const b200fft_convolution *convolution);
 /* execute_nd_real_convolution_f32/f64 on device pointers (stream ordered). */
 b200fft_status b200fft_execute_convolution(b200fft_context *context, b200fft_convolution *convolution,
                                            const void *input, void *output, void *workspace,

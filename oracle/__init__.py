@@ -164,3 +164,40 @@ def convolve_nd(x, kernel_spectrum, dims, coordinates=1, kernels=1, conjugate_se
             out[k * C + c] = p
     half = dims[:-1] + (dims[-1] // 2 + 1,)
     return c2r_nd(out.reshape((K * C,) + half), dims[-1], len(dims), normalize=True, threads=threads)
+
+
+def conv_plane(m, symmetric, oc, ic):
+    """ConvolutionMatrixLayout::kernel_plane_index (convolution_ir.rs:127-149)."""
+    if not symmetric:
+        return oc * m + ic
+    return ic * m - ic * ic + oc if ic < oc else oc * m - oc * oc + ic
+
+
+def convolve_c2c(x, kernel_spectrum, dims, batch=1, coordinates=1, kernels=1, matrix=0, symmetric=False,
+                 conjugate_sequence=False, cross_power=False, threads=None):
+    """C2C FFT convolution (execute_convolution_ir / execute_nd_convolution_ir,
+    convolution_ir.rs:4252-4440): forward FFT of the batch x coordinate systems, the
+    scalar / K-kernel / matrix multiply with the sequence-conjugation and cross-power
+    policy, normalised inverse FFT of the output systems."""
+    dims = tuple(dims)
+    T = int(np.prod(dims))
+    C = matrix if matrix else coordinates
+    spec = fft_nd(np.asarray(x, dtype=np.complex128).reshape((batch * C,) + dims), len(dims), threads=threads)
+    spec = spec.reshape(batch * C, T)
+    ker = np.asarray(kernel_spectrum, dtype=np.complex128).reshape(-1, T)
+    planes = (matrix * (matrix + 1) // 2 if symmetric else matrix * matrix) if matrix else 1
+    out_systems = kernels if kernels > 1 else batch
+    prep = (lambda v: np.conj(v)) if conjugate_sequence else (lambda v: v)
+    norm = (lambda p: p / np.sqrt(p.real * p.real + p.imag * p.imag)) if cross_power else (lambda p: p)
+    out = np.empty((out_systems * C, T), dtype=np.complex128)
+    for s in range(out_systems):
+        in_s, kid = (0, s) if kernels > 1 else (s, 0)
+        for oc in range(C):
+            if matrix:
+                acc = np.zeros(T, dtype=np.complex128)
+                for ic in range(C):
+                    acc += prep(spec[in_s * C + ic]) * ker[kid * planes + conv_plane(matrix, symmetric, oc, ic)]
+                out[s * C + oc] = norm(acc)
+            else:
+                out[s * C + oc] = norm(prep(spec[in_s * C + oc]) * ker[kid])
+    return fft_nd(out.reshape((out_systems * C,) + dims), len(dims), inverse=True, normalize=True, threads=threads)

@@ -72,6 +72,19 @@ static void run_program(const Program &prog, const void *in, void *out, const Pe
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scratch[k].empty() ? nullptr : scratch[k].data();
     int err = 0;
     for (const PassPlan &pp : prog.passes) {
+        if (pp.kernel == KERNEL_CMUL) {
+            ConvMultiply cm = pp.cm;
+            cm.src = bufs[pp.src_buf];
+            cm.dst = bufs[pp.dst_buf];
+            cm.ker = tables[pp.reg_table].data();
+            for (int64_t L = 0; L < cm.total; L++) {
+                if (prog.is_double)
+                    conv_multiply_one<double>(cm, L);
+                else
+                    conv_multiply_one<float>(cm, L);
+            }
+            continue;
+        }
         if (pp.kernel == KERNEL_COPY) {
             BoundaryCopy bc = pp.bc;
             bc.src = bufs[pp.src_buf];
@@ -151,9 +164,10 @@ extern "C" int b200fft_emu_convolution_run(const b200fft_config *cfg, const b200
         d.supports_f64 = dev->supports_f64;
         auto c = build_convolution(FftConfig::from_c(*cfg), d, spectrum, copies);
         const Program &prog = c->prog;
-        const size_t esz = prog.is_double ? 8 : 4;
-        if (in_bytes != prog.input_elems * esz || out_bytes != prog.output_elems * esz)
-            fail_input_length(prog.input_elems, in_bytes / esz);
+        const size_t csz = prog.is_double ? 16 : 8;
+        const size_t isz = prog.input_real ? csz / 2 : csz, osz = prog.output_real ? csz / 2 : csz;
+        if (in_bytes != prog.input_elems * isz || out_bytes != prog.output_elems * osz)
+            fail_input_length(prog.input_elems, in_bytes / isz);
         std::vector<unsigned char> din((const unsigned char *)in, (const unsigned char *)in + in_bytes);
         std::vector<unsigned char> dout(out_bytes, 0xff);
         run_program(prog, din.data(), dout.data());

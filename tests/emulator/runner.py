@@ -60,6 +60,23 @@ def run(case, V, lib):
         return run_slab(case, V, lib, dev, cfg, rng, cdt, rdt)
     elif kind == "bnd":
         return run_boundary(case, V, lib, dev, cfg, rng, cdt, rdt)
+    elif kind == "cconv":
+        return run_cconv(case, V, lib, dev, cfg, rng, cdt, rdt)
+    elif kind == "kprep":
+        # kernelConvolution preparation: the forward transform of batch x coordinate systems
+        C = case["coords"]
+        cfg = cfg.with_kernel_convolution(True).with_coordinate_features(C)
+        n = int(np.prod(dims))
+        if case.get("real"):
+            x = rng.uniform(-1, 1, (batch * C,) + tuple(dims)).astype(rdt)
+            cfg = cfg.with_transform(V.TransformKind.R2C)
+            ref = oracle.r2c_nd(x.astype(np.float64), len(dims), threads=4)
+        else:
+            x = (rng.uniform(-1, 1, (batch * C,) + tuple(dims))
+                 + 1j * rng.uniform(-1, 1, (batch * C,) + tuple(dims))).astype(cdt)
+            ref = oracle.fft_nd(x.astype(np.complex128), len(dims), threads=4)
+        y, n = emulate(V, lib, cfg, V.Direction.FORWARD, dev, x, ref.size, cdt)
+        return {"err": rel_l2(y, ref), "launches": n}
     else:
         x = rng.uniform(-1, 1, shape)
         spec = oracle.r2c_nd(x, len(dims), threads=4).astype(cdt)
@@ -237,6 +254,46 @@ def run_boundary(case, V, lib, dev, cfg, rng, cdt, rdt):
     y, n = emulate(V, lib, cfg, direction, dev, phys_in, bs * batch, out_dt)
     got = _unpack(y, out_dims, case.get("out_strides"), case.get("out_batch_stride"), batch)
     return {"err": rel_l2(got, ref), "launches": n}
+
+
+def run_cconv(case, V, lib, dev, cfg, rng, cdt, rdt):
+    """C2C convolution (kind "cconv"): batch, coords, kernels, matrix, symmetric, conj, cross."""
+    import ctypes
+    dims, B = case["dims"], case["batch"]
+    M, K = case.get("matrix", 0), case.get("kernels", 1)
+    C = M if M else case.get("coords", 1)
+    sym = case.get("symmetric", False)
+    cfg = cfg.with_convolution(True).with_convolution_kernel_count(K)
+    if M:
+        cfg = cfg.with_matrix_convolution(M)
+        if sym:
+            cfg = cfg.with_symmetric_convolution_kernel(True)
+    elif C > 1:
+        cfg = cfg.with_coordinate_features(C)
+    if case.get("conj"):
+        cfg = cfg.with_convolution_conjugation(1)
+    if case.get("cross"):
+        cfg = cfg.with_cross_power_spectrum_normalization(True)
+    T = int(np.prod(dims))
+    planes = (M * (M + 1) // 2 if sym else M * M) if M else 1
+    x = (rng.uniform(-1, 1, (B * C,) + tuple(dims)) + 1j * rng.uniform(-1, 1, (B * C,) + tuple(dims))).astype(cdt)
+    ker = (rng.uniform(-1, 1, planes * K * T) + 1j * rng.uniform(-1, 1, planes * K * T)).astype(cdt)
+    ref = oracle.convolve_c2c(x, ker, dims, B, C, K, M, sym, case.get("conj", False), case.get("cross", False),
+                              threads=4)
+    out = np.empty(ref.size, dtype=cdt)
+    err = ctypes.create_string_buffer(512)
+    launches = ctypes.c_int(0)
+    fn = lib.b200fft_emu_convolution_run
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p,
+                   ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t,
+                   ctypes.c_void_p]
+    d = dev._c()
+    st = fn(ctypes.addressof(cfg._s), ctypes.addressof(d), ker.ctypes.data, planes * K, x.ctypes.data, x.nbytes,
+            out.ctypes.data, out.nbytes, err, 512, ctypes.addressof(launches))
+    if st != 0:
+        raise V.VkFftError(st, err.value.decode())
+    return {"err": rel_l2(out, ref), "launches": launches.value}
 
 
 def main():

@@ -88,6 +88,21 @@ CASES = [
     dict(kind="bnd", mode="c2r", dims=[6, 8], batch=2, prec="F64", in_strides={"0": 6}, in_batch_stride=40,
          out_strides={"0": 10}),
     dict(kind="bnd", mode="c2c", dims=[4099], batch=2, prec="F32", pad={"0": [2000, 4099]}),
+    # C2C convolution (ConvolutionIr / NdConvolutionIr) and kernelConvolution preparation
+    dict(kind="cconv", dims=[64], batch=3, prec="F64"),
+    dict(kind="cconv", dims=[64], batch=1, prec="F64", kernels=3),
+    dict(kind="cconv", dims=[60], batch=1, prec="F64", matrix=2),
+    dict(kind="cconv", dims=[60], batch=1, prec="F64", matrix=2, symmetric=True),
+    dict(kind="cconv", dims=[48], batch=1, prec="F64", matrix=3, kernels=2),
+    dict(kind="cconv", dims=[64], batch=2, prec="F32", conj=True, cross=True),
+    dict(kind="cconv", dims=[16, 12], batch=2, prec="F64"),
+    dict(kind="cconv", dims=[16, 12], batch=1, prec="F64", kernels=3),
+    dict(kind="cconv", dims=[8, 6, 10], batch=1, prec="F64", matrix=3),
+    dict(kind="cconv", dims=[16, 12], batch=1, prec="F64", matrix=2, symmetric=True, conj=True),
+    dict(kind="cconv", dims=[4099], batch=1, prec="F32"),
+    dict(kind="kprep", dims=[64], batch=2, prec="F64", coords=3),
+    dict(kind="kprep", dims=[60], batch=1, prec="F32", coords=2, real=True),
+    dict(kind="kprep", dims=[16, 10], batch=2, prec="F64", coords=2, real=True),
 ]
 
 

@@ -1,5 +1,7 @@
-"""FFT convolution (NdRealConvolutionIr, convolution_ir.rs:3867-4250) on the B200 against
-the oracle's R2C -> policy multiply -> normalised C2R restatement."""
+"""FFT convolution on the B200 against the oracle: NdRealConvolutionIr
+(convolution_ir.rs:3867-4250; R2C -> policy multiply -> normalised C2R), the C2C
+ConvolutionIr / NdConvolutionIr (:2520-3866; scalar, K-kernel and matrix multiplies) and the
+kernelConvolution preparation transform."""
 import numpy as np
 import pytest
 
@@ -87,3 +89,63 @@ def test_convolution_build_validation(V):
         V.NdRealConvolutionIr.build_from_spectrum(cfg, np.zeros(3 * 32 * 25, dtype=np.complex64), dev)
     ir = V.NdRealConvolutionIr.build_from_spectrum(cfg, np.zeros(2 * 32 * 25, dtype=np.complex64), dev)
     assert ir.input_elements == 2 * 32 * 48 and ir.output_elements == 2 * 32 * 48
+
+
+C2C_CASES = [
+    dict(dims=[4096], batch=64, prec="F32"),
+    dict(dims=[4096], batch=1, prec="F64", kernels=4),
+    dict(dims=[1000], batch=1, prec="F64", matrix=2),
+    dict(dims=[2048], batch=1, prec="F32", matrix=2, symmetric=True, conj=True),
+    dict(dims=[510], batch=1, prec="F64", matrix=3, kernels=2),
+    dict(dims=[256, 256], batch=2, prec="F32", cross=True),
+    dict(dims=[64, 64, 64], batch=1, prec="F32", matrix=3),
+    dict(dims=[4099], batch=2, prec="F64"),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", C2C_CASES, ids=[str(c) for c in C2C_CASES])
+def test_c2c_convolution_matches_oracle(V, ctx, case):
+    """ConvolutionIr / NdConvolutionIr: scalar, K-kernel, matrix (symmetric) and policy variants."""
+    dims, B, prec = case["dims"], case["batch"], case["prec"]
+    cdt = NP[prec][0]
+    M, K, sym = case.get("matrix", 0), case.get("kernels", 1), case.get("symmetric", False)
+    C = M if M else 1
+    cfg = (V.FftConfig(dims).with_batch_count(B).with_precision(V.Precision[prec]).with_convolution(True)
+           .with_convolution_kernel_count(K))
+    if M:
+        cfg = cfg.with_matrix_convolution(M).with_symmetric_convolution_kernel(sym)
+    if case.get("conj"):
+        cfg = cfg.with_convolution_conjugation(V.ConvolutionConjugation.SEQUENCE)
+    if case.get("cross"):
+        cfg = cfg.with_cross_power_spectrum_normalization(True)
+    T = int(np.prod(dims))
+    planes = (M * (M + 1) // 2 if sym else M * M) if M else 1
+    rng = np.random.default_rng(T + B)
+    x = (rng.uniform(-1, 1, (B * C, T)) + 1j * rng.uniform(-1, 1, (B * C, T))).astype(cdt)
+    ker = (rng.uniform(-1, 1, planes * K * T) + 1j * rng.uniform(-1, 1, planes * K * T)).astype(cdt)
+    cls = V.ConvolutionIr if len(dims) == 1 else V.NdConvolutionIr
+    ir = cls.build_from_spectrum(cfg, ker, ctx.device_profile())
+    y = ctx.execute_convolution(ir, x)
+    ref = oracle.convolve_c2c(x, ker, dims, B, C, K, M, sym, case.get("conj", False), case.get("cross", False))
+    assert rel_l2(y, ref) <= TOL[prec]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("real", [False, True])
+def test_kernel_convolution_preparation(V, ctx, real):
+    """kernelConvolution: the forward transform of batch x coordinate kernel systems."""
+    B, C = (1, 3) if not real else (2, 2)
+    dims = [4096] if not real else [256, 200]
+    cfg = V.FftConfig(dims).with_batch_count(B).with_kernel_convolution(True).with_coordinate_features(C)
+    rng = np.random.default_rng(9)
+    if real:
+        cfg = cfg.with_transform(V.TransformKind.R2C)
+        x = rng.uniform(-1, 1, (B * C,) + tuple(dims)).astype(np.float32)
+        ref = oracle.r2c_nd(x.astype(np.float64), len(dims))
+    else:
+        x = (rng.uniform(-1, 1, (B * C,) + tuple(dims)) + 1j * rng.uniform(-1, 1, (B * C,) + tuple(dims))).astype(
+            np.complex64)
+        ref = oracle.fft_nd(x.astype(np.complex128), len(dims))
+    ir = V.TransformIr.build(cfg, V.Direction.FORWARD, ctx.device_profile())
+    assert rel_l2(ctx.execute_transform(ir, x), ref) <= TOL["F32"]

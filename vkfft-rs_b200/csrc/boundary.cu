@@ -1,4 +1,5 @@
-// Boundary copy kernel: gathers a caller's (formatted, zero-padded) input into a dense
+// Convolution multiply kernel (one thread per output element) and boundary copy kernel,
+// which gathers a caller's (formatted, zero-padded) input into a dense
 // scratch tensor, or scatters a dense result into the caller's formatted output with the
 // zero-padding interval applied.  One thread per logical element, grid-stride.
 #include <cuda_runtime.h>
@@ -12,6 +13,22 @@ namespace b200fft {
 __global__ void __launch_bounds__(256) boundary_copy_kernel(const __grid_constant__ BoundaryCopy b) {
     for (int64_t L = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; L < b.total; L += (int64_t)gridDim.x * blockDim.x)
         boundary_copy_one(b, L);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) conv_multiply_kernel(const __grid_constant__ ConvMultiply m) {
+    for (int64_t L = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; L < m.total; L += (int64_t)gridDim.x * blockDim.x)
+        conv_multiply_one<T>(m, L);
+}
+
+cudaError_t launch_conv_multiply(const ConvMultiply &m, bool dbl, cudaStream_t stream) {
+    if (m.total <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((m.total + 255) / 256, 148 * 32);
+    if (dbl)
+        conv_multiply_kernel<double><<<(unsigned)blocks, 256, 0, stream>>>(m);
+    else
+        conv_multiply_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(m);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_boundary_copy(const BoundaryCopy &b, cudaStream_t stream) {

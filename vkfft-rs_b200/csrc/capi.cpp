@@ -520,3 +520,7 @@ void b200fft_ticket_destroy(b200fft_ticket *ticket) {
     wait_ticket(*ticket->t);
     delete ticket;
 }
+
+uint64_t b200fft_convolution_input_elements(const b200fft_convolution *c) { return c ? c->c->prog.input_elems : 0; }
+uint64_t b200fft_convolution_output_elements(const b200fft_convolution *c) { return c ? c->c->prog.output_elems : 0; }
+int32_t b200fft_convolution_input_is_real(const b200fft_convolution *c) { return c ? c->c->prog.input_real : 0; }

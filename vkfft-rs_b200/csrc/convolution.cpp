@@ -1,5 +1,5 @@
-// FFT convolution application: the ND real independent-coordinate path of
-// NdRealConvolutionIr (convolution_ir.rs:3867-4250).
+// FFT convolution applications: the C2C ConvolutionIr / NdConvolutionIr (build_c2c_convolution)
+// and the ND real independent-coordinate path of NdRealConvolutionIr (convolution_ir.rs:3867-4250).
 //
 // Reference semantics: the C coordinate images are R2C-transformed (batch C), every
 // output system (kernel k, coordinate c) is out[(k C + c) L + i] =
@@ -12,6 +12,8 @@
 // memory), inverse middle axes, normalised C2R rows into the output.  K > 1 fans out
 // through an explicit multiply pass.  The reference requires K C copies of the kernel
 // spectrum; a single copy is accepted too and broadcast to every coordinate.
+#include <algorithm>
+#include <cmath>
 #include <cstring>
 
 #include "transform.hpp"
@@ -31,9 +33,135 @@ static size_t prod(const std::vector<size_t> &v, size_t a, size_t b) {
     return r;
 }
 
+// Appends the passes and tables of `src` to `dst`, renaming buffers through `remap`.
+static void append_program(Program &dst, const Program &src, const int (&remap)[2 + kScratchBuffers]) {
+    const int off = (int)dst.tables.size();
+    dst.tables.insert(dst.tables.end(), src.tables.begin(), src.tables.end());
+    for (PassPlan pp : src.passes) {
+        for (auto &row : pp.op_tables)
+            for (int &id : row)
+                if (id >= 0) id += off;
+        if (pp.reg_table >= 0) pp.reg_table += off;
+        if (pp.reg_table2 >= 0) pp.reg_table2 += off;
+        pp.src_buf = remap[pp.src_buf];
+        pp.dst_buf = remap[pp.dst_buf];
+        dst.passes.push_back(pp);
+    }
+    for (int k = 0; k < kScratchBuffers; k++) dst.scratch_elems[k] = std::max(dst.scratch_elems[k], src.scratch_elems[k]);
+}
+
+// C2C convolution: ConvolutionIr (rank 1, convolution_ir.rs:2520-3626) and NdConvolutionIr
+// (rank >= 2, :3627-3866).  Forward transform of the batch x coordinate systems (into the
+// output buffer), the multiply (scalar, K-kernel fan-out or 2x2 / 3x3 matrix, with the
+// conjugation / cross-power policy) into scratch 4, normalised inverse transform of the
+// output systems.  The kernel spectrum holds `planes x K` tensors of T elements.
+static std::unique_ptr<Convolution> build_c2c_convolution(const FftConfig &c, const DeviceProfile &device,
+                                                          const void *spectrum, uint64_t copies) {
+    const size_t R = c.dimensions.size();
+    const size_t T = prod(c.dimensions, 0, R);
+    const int M = c.matrix_convolution > 1 ? (int)c.matrix_convolution : 0;
+    if (M && M != 2 && M != 3) fail_invalid_ir("matrix convolution IR requires a 2x2 or 3x3 matrix");
+    if (M == 3 && c.symmetric_convolution_kernel)
+        fail_unsupported(
+            "pinned VkFFT 1.3.4 3x3 symmetric-kernel code aliases yz and zz while the API guide documents six planes");
+    if (c.convolution_conjugation == ConvolutionConjugation::Kernel)
+        fail_unsupported("kernel-conjugated convolution is not executable in the pinned VkFFT codegen");
+    const size_t C = M ? (size_t)M : c.coordinate_features, K = c.convolution_kernel_count, B = c.batch_count;
+    bool padded = c.has_formatted_strides();
+    for (auto &z : c.zero_padding) padded |= z.has_value();
+    for (size_t a = 0; a < R; a++) padded |= c.omit_dimension.size() > a && c.omit_dimension[a];
+    if (R >= 2) {
+        const bool scalar_ok = !M && C == 1 && (K == 1 || B == 1);
+        const bool matrix_ok = M && B == 1 && K == 1;
+        if (!scalar_ok && !matrix_ok)
+            fail_unsupported(
+                "multidimensional performConvolution IR supports scalar K=1/K>1 ownership or batch1/K1 matrix "
+                "coordinates");
+        if (padded) fail_unsupported("multidimensional performConvolution currently requires dense unpadded active dimensions");
+    } else {
+        if ((!M && C != 1) || (K > 1 && B != 1))
+            fail_unsupported("performConvolution supports one coordinate plane (or matrix coordinates) and K > 1 "
+                             "kernels on one input batch");
+        if (padded) fail_unsupported("B200 engine: padded or formatted performConvolution is not implemented");
+    }
+    const size_t planes = M ? (c.symmetric_convolution_kernel ? (size_t)(M * (M + 1) / 2) : (size_t)(M * M)) : 1;
+    if (copies * T != T * planes * K)
+        fail_invalid_ir("convolution kernel spectrum length must match its scalar/independent/matrix plane layout");
+    const bool dbl = c.precision == Precision::F64;
+    const size_t esz = dbl ? 16 : 8;
+    const size_t n_scalars = copies * T * 2;
+    for (size_t k = 0; k < n_scalars; k++) {
+        const double v = dbl ? static_cast<const double *>(spectrum)[k] : (double)static_cast<const float *>(spectrum)[k];
+        if (!std::isfinite(v)) fail_invalid_ir("convolution kernel spectrum contains non-finite values");
+    }
+    auto conv = std::make_unique<Convolution>();
+    static uint64_t next_id = 1ull << 42;
+    conv->id = next_id++;
+    conv->config = c;
+    conv->device = device;
+    conv->spectrum_elems = T;
+    const size_t out_systems = K > 1 ? K : B;
+    FftConfig fc = c;
+    fc.perform_convolution = false;
+    fc.convolution_conjugation = ConvolutionConjugation::None;
+    fc.cross_power_spectrum_normalization = false;
+    fc.coordinate_features = 1;
+    fc.matrix_convolution = 1;
+    fc.symmetric_convolution_kernel = false;
+    fc.convolution_kernel_count = 1;
+    fc.batch_count = B * C;
+    fc.normalize_inverse = false;
+    conv->forward = build_transform(fc, B200FFT_FORWARD, device);
+    FftConfig ic = fc;
+    ic.batch_count = out_systems * C;
+    ic.normalize_inverse = true;
+    conv->inverse = build_transform(ic, B200FFT_INVERSE, device);
+
+    Program &prog = conv->prog;
+    prog.is_double = dbl;
+    prog.input_elems = B * C * T;
+    prog.output_elems = out_systems * C * T;
+    int same[2 + kScratchBuffers];
+    for (int k = 0; k < 2 + kScratchBuffers; k++) same[k] = k;
+    append_program(prog, conv->forward->prog, same);  // spectrum of the input systems -> out
+    HostTable st;
+    st.is_raw = true;
+    st.raw.assign(static_cast<const unsigned char *>(spectrum),
+                  static_cast<const unsigned char *>(spectrum) + copies * T * esz);
+    prog.tables.push_back(std::move(st));
+    PassPlan mp{};
+    mp.kernel = KERNEL_CMUL;
+    mp.reg_table = (int)prog.tables.size() - 1;
+    mp.cm.T = (int64_t)T;
+    mp.cm.total = (int64_t)(out_systems * C * T);
+    mp.cm.C = (int32_t)C;
+    mp.cm.K = (int32_t)K;
+    mp.cm.matrix = M;
+    mp.cm.symmetric = c.symmetric_convolution_kernel ? 1 : 0;
+    mp.cm.planes = (int32_t)planes;
+    mp.cm.conj_seq = c.convolution_conjugation == ConvolutionConjugation::Sequence ? 1 : 0;
+    mp.cm.cross_power = c.cross_power_spectrum_normalization ? 1 : 0;
+    mp.src_buf = BUF_OUT;
+    mp.dst_buf = BUF_SCRATCH4;
+    mp.label = "convolution multiply";
+    for (auto &row : mp.op_tables) row[0] = row[1] = row[2] = -1;
+    prog.passes.push_back(mp);
+    prog.scratch_elems[4] = std::max(prog.scratch_elems[4], out_systems * C * T);
+    int inv_map[2 + kScratchBuffers];
+    for (int k = 0; k < 2 + kScratchBuffers; k++) inv_map[k] = k;
+    inv_map[BUF_IN] = BUF_SCRATCH4;
+    append_program(prog, conv->inverse->prog, inv_map);  // normalised inverse -> out
+    return conv;
+}
+
 std::unique_ptr<Convolution> build_convolution(const FftConfig &config_in, const DeviceProfile &device,
                                                const void *spectrum, uint64_t copies) {
     config_in.validate();
+    if (config_in.perform_convolution && config_in.transform == TransformKind::C2C) {
+        if (!(config_in.precision == Precision::F32 || config_in.precision == Precision::F64))
+            fail_precision("B200 engine", precision_name(config_in.precision));
+        return build_c2c_convolution(config_in.resolve_tuning_for_device(device), device, spectrum, copies);
+    }
     if (!config_in.perform_convolution || config_in.transform != TransformKind::R2C ||
         config_in.dimensions.size() < 2 || config_in.batch_count != 1)
         fail_unsupported(

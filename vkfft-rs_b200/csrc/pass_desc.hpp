@@ -134,6 +134,29 @@ struct PassParams : PassShape {
     Op ops[kMaxOps];
 };
 
+// Convolution multiply (convolution_ir.rs:36-151, :4252-4440): out system s, coordinate
+// oc, element i of a T-element tensor:
+//   matrix:   sum_ic prep(spec[(in_s C + ic) T + i]) ker[(kid planes + plane(oc, ic)) T + i]
+//   scalar:   prep(spec[in_s T + i]) ker[kid T + i]
+// with in_s = 0, kid = s for K > 1 (one input system fanned out to K kernels) and in_s = s,
+// kid = 0 otherwise; prep conjugates the sequence (Sequence policy) and the product is
+// divided by its modulus with cross-power normalisation.
+struct ConvMultiply {
+    const void *src;
+    void *dst;
+    const void *ker;
+    int64_t T;            // tensor elements
+    int64_t total;        // output elements: out_systems * C * T
+    int32_t C;            // coordinates per system
+    int32_t K;            // kernels
+    int32_t matrix;       // 0 (scalar) or the matrix size
+    int32_t symmetric;
+    int32_t planes;       // kernel planes per kernel set
+    int32_t conj_seq;
+    int32_t cross_power;
+    int32_t _pad;
+};
+
 // Boundary copy between a caller's buffer and a dense scratch tensor, with the
 // zero-padding interval applied (zero_pad_ir.rs: elements whose coordinate on any padded
 // axis lies in [pad_lo, pad_hi) become zero) and formatted buffer strides

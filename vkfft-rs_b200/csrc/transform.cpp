@@ -34,7 +34,7 @@ static void check_executable(const FftConfig &c) {
         fail_precision("B200 engine", precision_name(c.precision));
     if (!(c.transform == TransformKind::C2C || c.transform == TransformKind::R2C || c.transform == TransformKind::C2R))
         fail_unsupported("B200 engine executes C2C, R2C and C2R transforms (R2R is outside the FFT hot path)");
-    if (c.kernel_convolution) fail_unsupported("B200 engine: kernelConvolution preparation is not implemented yet");
+
 }
 
 static std::vector<int64_t> dense_strides(const std::vector<size_t> &dims) {

@@ -262,6 +262,9 @@ def library():
         "b200fft_convolution_build": ([P(_Config), P(_Device), vp, u64, P(vp)], i32),
         "b200fft_convolution_destroy": ([vp], None),
         "b200fft_convolution_workspace_bytes": ([vp], u64),
+        "b200fft_convolution_input_elements": ([vp], u64),
+        "b200fft_convolution_output_elements": ([vp], u64),
+        "b200fft_convolution_input_is_real": ([vp], i32),
         "b200fft_execute_convolution": ([vp, vp, vp, vp, vp, vp], i32),
         "b200fft_execute_convolution_host": ([vp, vp, vp, ctypes.c_size_t, vp, ctypes.c_size_t], i32),
         "b200fft_slab_build": ([P(_Config), i32, u32, u32, P(_Device), P(vp)], i32),
@@ -722,35 +725,31 @@ class ConvolutionConjugation(enum.IntEnum):
     KERNEL = 2
 
 
-class NdRealConvolutionIr:
-    """convolution_ir.rs:3867-4183 (independent coordinates): build_from_spectrum(config,
-    kernel_spectrum, device).  kernel_spectrum holds K*C copies of the compact R2C spectrum
-    (the reference layout) or one copy broadcast to every coordinate."""
+class _ConvolutionApplication:
+    """Common part of the convolution applications: the library object, the element
+    counts and types of the input / output arrays."""
 
-    def __init__(self, handle, config, precision, in_elems, out_elems):
+    def __init__(self, handle, config):
         self._h = handle
         self.config = config
-        self.precision = precision
-        self.input_elements = in_elems
-        self.output_elements = out_elems
+        self.precision = config.precision
+        lib = library()
+        self.input_elements = int(lib.b200fft_convolution_input_elements(handle))
+        self.output_elements = int(lib.b200fft_convolution_output_elements(handle))
+        self.input_is_real = bool(lib.b200fft_convolution_input_is_real(handle))
 
     @classmethod
-    def build_from_spectrum(cls, config, kernel_spectrum, device):
-        prec = config.precision
-        cdt = np.complex64 if prec == Precision.F32 else np.complex128
+    def _build(cls, config, kernel_spectrum, device, plane_elems):
+        cdt = np.complex64 if config.precision == Precision.F32 else np.complex128
         spec = np.ascontiguousarray(kernel_spectrum, dtype=cdt).ravel()
-        dims = config.dimensions
-        compact = int(np.prod(dims[:-1])) * (dims[-1] // 2 + 1)
-        if spec.size % compact:
+        if spec.size % plane_elems:
             raise VkFftError(Status.InputLengthMismatch,
-                             f"input contains {spec.size} complex elements but kernel expects a multiple of {compact}")
+                             f"input contains {spec.size} complex elements but kernel expects a multiple of "
+                             f"{plane_elems}")
         h = ctypes.c_void_p()
         _check(library().b200fft_convolution_build(ctypes.byref(config._s), ctypes.byref(device._c()),
-                                                   spec.ctypes.data, spec.size // compact, ctypes.byref(h)))
-        c = config._s.coordinate_features
-        k = config._s.convolution_kernel_count
-        full = int(np.prod(dims))
-        return cls(h, config, prec, c * full, k * c * full)
+                                                   spec.ctypes.data, spec.size // plane_elems, ctypes.byref(h)))
+        return cls(h, config)
 
     def __del__(self):
         h = getattr(self, "_h", None)
@@ -764,6 +763,39 @@ class NdRealConvolutionIr:
 
     def real_dtype(self):
         return np.float32 if self.precision == Precision.F32 else np.float64
+
+    def complex_dtype(self):
+        return np.complex64 if self.precision == Precision.F32 else np.complex128
+
+    def input_dtype(self):
+        return self.real_dtype() if self.input_is_real else self.complex_dtype()
+
+    def output_dtype(self):
+        return self.input_dtype()
+
+
+class NdRealConvolutionIr(_ConvolutionApplication):
+    """convolution_ir.rs:3867-4183 (independent coordinates): build_from_spectrum(config,
+    kernel_spectrum, device).  kernel_spectrum holds K*C copies of the compact R2C spectrum
+    (the reference layout) or one copy broadcast to every coordinate."""
+
+    @classmethod
+    def build_from_spectrum(cls, config, kernel_spectrum, device):
+        dims = config.dimensions
+        return cls._build(config, kernel_spectrum, device, int(np.prod(dims[:-1])) * (dims[-1] // 2 + 1))
+
+
+class ConvolutionIr(_ConvolutionApplication):
+    """convolution_ir.rs:2520-3626: 1D C2C performConvolution from a pre-transformed kernel
+    spectrum (scalar, K-kernel fan-out or 2x2 / 3x3 matrix coordinates)."""
+
+    @classmethod
+    def build_from_spectrum(cls, config, kernel_spectrum, device):
+        return cls._build(config, kernel_spectrum, device, int(np.prod(config.dimensions)))
+
+
+class NdConvolutionIr(ConvolutionIr):
+    """convolution_ir.rs:3627-3866: multidimensional C2C performConvolution."""
 
 
 # ---- backend/cuda/runtime.rs --------------------------------------------------------
@@ -942,13 +974,17 @@ class CudaExecutionContext:
         return self.execute_transform(ir, data)
 
     def execute_nd_real_convolution(self, ir, data, out=None):
-        """execute_nd_real_convolution_f32/f64 (native_runtime.rs:257-337): host arrays."""
-        x = np.ascontiguousarray(data, dtype=ir.real_dtype()).ravel()
+        """execute_nd_real_convolution_f32/f64 / execute_convolution_f32/f64 /
+        execute_nd_convolution_f32/f64 (native_runtime.rs:197-337): host arrays."""
+        x = np.ascontiguousarray(data, dtype=ir.input_dtype()).ravel()
         if out is None:
-            out = np.empty(ir.output_elements, dtype=ir.real_dtype())
+            out = np.empty(ir.output_elements, dtype=ir.output_dtype())
         _check(library().b200fft_execute_convolution_host(self._h, ir._h, x.ctypes.data, x.nbytes,
                                                           out.ctypes.data, out.nbytes))
         return out
+
+    execute_convolution = execute_nd_real_convolution
+    execute_nd_convolution = execute_nd_real_convolution
 
     def execute_nd_real_convolution_resident(self, ir, input_ptr, output_ptr, workspace_ptr=0, stream=0):
         _check(library().b200fft_execute_convolution(self._h, ir._h, ctypes.c_void_p(input_ptr),
