@@ -75,6 +75,33 @@ int table_reg_twiddles(Program &prog, size_t n, int variant) {
     return add_table(prog, key, std::move(t));
 }
 
+// Twiddles of one radix-R Stockham stage of span P, transposed: entry (q-1)*P + j holds
+// W_{P R}^{j q} (q = 1..R-1), so the butterflies of a warp (consecutive j) read
+// consecutive entries.
+int table_stage_twiddles(Program &prog, size_t R, size_t P) {
+    std::string key = "stw" + std::to_string(R) + "_" + std::to_string(P);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    HostTable t;
+    t.c.reserve((R - 1) * P);
+    for (size_t q = 1; q < R; q++)
+        for (size_t j = 0; j < P; j++) t.c.push_back(root(j * q, P * R));
+    return add_table(prog, key, std::move(t));
+}
+
+// Four-step twiddles W_N^{c e} for line (column) c < ncols and element e < nrows, stored
+// element-major (entry e*ncols + c): lines-fastest passes read consecutive entries.
+int table_twiddle_transposed(Program &prog, size_t ncols, size_t nrows, size_t N) {
+    std::string key = "ttw" + std::to_string(ncols) + "_" + std::to_string(nrows) + "_" + std::to_string(N);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    HostTable t;
+    t.c.reserve(ncols * nrows);
+    for (size_t e = 0; e < nrows; e++)
+        for (size_t c = 0; c < ncols; c++) t.c.push_back(root((c * e) % N, N));
+    return add_table(prog, key, std::move(t));
+}
+
 // Bluestein chirp exactly as the reference evaluates it (reference.rs:121-125,
 // lut.rs:295-299): angle = sign * PI * (i as f64) * (i as f64) / (n as f64), not
 // reduced modulo 2n, then libm cos / sin.  Forward sign (-1); inverse transforms
@@ -419,11 +446,13 @@ class PassBuilder {
 
     // global -> line region A.  own_em > 0: the table index of the multiply is e*own_em
     // (instead of the side's logical index).
-    void load(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0, int own_em = 0) {
+    void load(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0, int own_em = 0,
+              int own_cm = 0) {
         Op &o = push(OP_LOAD);
         o.len = len;
         o.flags = flags | (own_em ? F_OWN_INDEX : 0);
         o.em = own_em;
+        o.cm = own_cm;
         o.mul = mul;
         o.dst_base = A_;
         o.sub_stride = sh_.ls;
@@ -449,8 +478,10 @@ class PassBuilder {
         o.mul = MUL_LUT_N;
         o.cm = cm;
         o.em = em;
-        o.flags = flags;
+        // a table indexed line-fastest (cm = 1) is read coalesced when threads walk lines
+        o.flags = flags | (cm == 1 && em > 1 ? F_LINE_FAST : 0);
         o.div_a = make_fastdiv((uint32_t)L_);
+        o.div_b = make_fastdiv((uint32_t)sh_.G);
         set_tables(table);
     }
 
@@ -515,11 +546,13 @@ class PassBuilder {
         o.nfull = slot;
     }
 
-    void store(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0, int own_em = 0) {
+    void store(int len, int flags, int mul = MUL_NONE, int table = -1, double scale = 1.0, int own_em = 0,
+               int own_cm = 0) {
         Op &o = push(OP_STORE);
         o.len = len;
         o.flags = flags | (own_em ? F_OWN_INDEX : 0);
         o.em = own_em;
+        o.cm = own_cm;
         o.mul = mul;
         o.src_base = cur_;
         o.sub_stride = sh_.ls;
@@ -577,7 +610,7 @@ class PassBuilder {
                 o.sub_stride = ls;
                 o.div_a = make_fastdiv((uint32_t)(L / st.radix));
                 o.div_b = make_fastdiv((uint32_t)P);
-                set_tables(tw);
+                set_tables(P > 1 ? table_stage_twiddles(prog_, (size_t)st.radix, (size_t)P) : -1);
                 std::swap(cur, other);
             } else {
                 emit_rader(st, L, nsub, ls, P, tw, cur, other, extra);
@@ -844,14 +877,13 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         size_t N1, N2;
         if (four_step_split(dbl, N, *alg, N1, N2)) {
             const AxisAlgorithm a1 = restrict_algorithm(*alg, N1), a2 = restrict_algorithm(*alg, N2);
-            const int tw = table_twiddle(prog, N);
             const int64_t scr_os = (int64_t)N * S;
             prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * N * S));
             {
                 PassBuilder b(prog, (int)N1, line_stages(N1, &a1), true, no * S * N2, kMaxOps);
                 b.load((int)N1, cin);
                 b.fft();
-                b.store((int)N1, 0, MUL_TWIDDLE_CE, tw);
+                b.store((int)N1, 0, MUL_TWIDDLE_CE, table_twiddle_transposed(prog, N2, N1, N), 1.0, (int)N2, 1);
                 prog.passes.push_back(b.finish(
                     no, S, (int64_t)N2, make_side(job.in_os, 1, S, (int64_t)N2 * S, job.in_real, N, 1, (int)N2, herm),
                     make_side(scr_os, 1, S, (int64_t)N2 * S, false, N, 1, (int)N2), job.in_buf, job.in_off,
@@ -949,7 +981,6 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         if (line_fits_on_chip(dbl, MB, nullptr, true) && line_fits_on_chip(dbl, A, nullptr, true)) {
             const int chirpB = table_bluestein_chirp(prog, B);
             const int specB = table_bluestein_spectrum(prog, B, MB);
-            const int tw = table_twiddle(prog, N);
             const int64_t scr_os = (int64_t)N * S;
             prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * N * S));
             {
@@ -959,7 +990,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
                 b.mul_region(specB, F_CONJ_OUT, 0, 1);
                 b.fft();
                 b.mul_region(chirpB, F_CONJ_IN, 0, 1, (int)B);
-                b.store((int)B, 0, MUL_TWIDDLE_CE, tw);
+                b.store((int)B, 0, MUL_TWIDDLE_CE, table_twiddle_transposed(prog, A, B, N), 1.0, (int)A, 1);
                 prog.passes.push_back(b.finish(
                     no, S, (int64_t)A, make_side(job.in_os, 1, S, (int64_t)A * S, job.in_real, N, 1, (int)A, herm),
                     make_side(scr_os, 1, S, (int64_t)A * S, false, N, 1, (int)A), job.in_buf, job.in_off,
@@ -982,7 +1013,6 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     AxisAlgorithm smooth;
     if (!four_step_split(dbl, M, smooth, M1, M2)) fail_unsupported("B200 engine: Bluestein length not decomposable");
     const int spec = table_bluestein_spectrum(prog, N, M);
-    const int twM = table_twiddle(prog, M);
     const int64_t scr_os = (int64_t)M * S;
     prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * M * S));
     // pass A: columns n2: x[n2 + M2 n1] * chirp (n < N, else 0), FFT over n1, * W_M^{n2 k1}
@@ -990,7 +1020,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         PassBuilder b(prog, (int)M1, line_stages(M1, nullptr), true, no * S * M2, kMaxOps);
         b.load((int)M1, cin, MUL_LUT_N, chirp);
         b.fft();
-        b.store((int)M1, 0, MUL_TWIDDLE_CE, twM);
+        b.store((int)M1, 0, MUL_TWIDDLE_CE, table_twiddle_transposed(prog, M2, M1, M), 1.0, (int)M2, 1);
         prog.passes.push_back(b.finish(no, S, (int64_t)M2,
                                        make_side(job.in_os, 1, S, (int64_t)M2 * S, job.in_real, N, 1, (int)M2, herm),
                                        make_side(scr_os, 1, S, (int64_t)M2 * S, false, M, 1, (int)M2), job.in_buf,
@@ -1004,7 +1034,8 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         b.fft();
         b.mul_region(spec, F_CONJ_OUT, 1, (int)M1);
         b.fft();
-        b.store((int)M2, F_CONJ_IN | F_CONJ_LUT, MUL_TWIDDLE_CE, twM);
+        b.store((int)M2, F_CONJ_IN | F_CONJ_LUT, MUL_TWIDDLE_CE, table_twiddle_transposed(prog, M1, M2, M), 1.0,
+                (int)M1, 1);
         prog.passes.push_back(b.finish(no, S, (int64_t)M1,
                                        make_side(scr_os, 1, (int64_t)M2 * S, S, false, M, (int)M2, 1),
                                        make_side(scr_os, 1, (int64_t)M2 * S, S, false, M, (int)M2, 1), BUF_SCRATCH0,

@@ -49,6 +49,7 @@ enum OpFlags : int32_t {
     F_SCALE = 32,     // apply Op::scale
     F_OWN_INDEX = 64, // LOAD/STORE multiply: table index = c*op.cm + e*op.em (not the side's n)
     F_NORMALIZE = 128,  // OP_MUL: divide the product by its modulus (cross-power spectrum)
+    F_LINE_FAST = 256,  // OP_MUL: threads walk the lines fastest (the table's fast index is the line)
 };
 
 // Fast unsigned division by a run-time constant (round-up multiply-shift, valid for n < 2^31).

@@ -176,7 +176,6 @@ __device__ __forceinline__ void op_stage(const Op &op, cplx<T> *sm) {
     const int NBL = op.len / R;
     const int NB = op.nsub * NBL;
     const int P = op.P;
-    const int tstep = op.len / (P * R);
     for (int b = threadIdx.x; b < NB; b += blockDim.x) {
         const int s = fdiv(b, op.div_a);
         const int bb = b - s * NBL;
@@ -188,7 +187,7 @@ __device__ __forceinline__ void op_stage(const Op &op, cplx<T> *sm) {
         for (int q = 0; q < R; q++) v[q] = src[spad(bb + q * NBL)];
         if (P > 1) {
 #pragma unroll
-            for (int q = 1; q < R; q++) v[q] = cmul(v[q], ld_ro<T>(op.lut, j * q * tstep));
+            for (int q = 1; q < R; q++) v[q] = cmul(v[q], ld_ro<T>(op.lut, (q - 1) * P + j));
         }
         dft<R, T>(v);
         const int e0 = (bb - j) * R + j;
@@ -222,9 +221,16 @@ template <typename T>
 __device__ __forceinline__ void op_mul(const Op &op, cplx<T> *sm, const LineMeta &lm) {
     const int len = op.len;
     const int total = op.nsub * len;
+    const bool line_fast = op.flags & F_LINE_FAST;
     for (int f = threadIdx.x; f < total; f += blockDim.x) {
-        const int s = fdiv(f, op.div_a);
-        const int e = f - s * len;
+        int s, e;
+        if (line_fast) {
+            e = fdiv(f, op.div_b);
+            s = f - e * op.nsub;
+        } else {
+            s = fdiv(f, op.div_a);
+            e = f - s * len;
+        }
         cplx<T> *ptr = sm + op.src_base + s * op.sub_stride + spad(e);
         const cplx<T> v = *ptr;
         if ((op.flags & F_SAVE_DC) && e == 0) sm[op.x0_base + 2 * s + 1] = v;
