@@ -18,6 +18,7 @@ EmuDim threadIdx, blockIdx, blockDim;
 #include <vector>
 
 #include "../../vkfft-rs_b200/csrc/kernels.cu"
+#include "../../vkfft-rs_b200/csrc/boundary_device.cuh"
 #include "../../vkfft-rs_b200/csrc/slab.hpp"
 #include "../../vkfft-rs_b200/csrc/transform.hpp"
 
@@ -131,9 +132,8 @@ extern "C" int b200fft_emu_run(const b200fft_config *cfg, int direction, const b
         d.supports_f64 = dev->supports_f64;
         auto t = build_transform(FftConfig::from_c(*cfg), direction, d);
         const Program &prog = t->prog;
-        const size_t esz = prog.is_double ? 16 : 8;
-        size_t in_need = prog.input_elems * (prog.input_real ? esz / 2 : esz);
-        size_t out_need = prog.output_elems * (prog.output_real ? esz / 2 : esz);
+        size_t in_need = prog.input_bytes();
+        size_t out_need = prog.output_bytes();
         if (in_bytes != in_need || out_bytes != out_need) fail_input_length(in_need, in_bytes);
         // private copies so AddressSanitizer sees exact-size heap buffers
         std::vector<unsigned char> din((const unsigned char *)in, (const unsigned char *)in + in_need);

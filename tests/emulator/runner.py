@@ -62,6 +62,24 @@ def run(case, V, lib):
         return run_boundary(case, V, lib, dev, cfg, rng, cdt, rdt)
     elif kind == "cconv":
         return run_cconv(case, V, lib, dev, cfg, rng, cdt, rdt)
+    elif kind == "mixed":
+        # F16 storage / F32 compute, F64 compute / F32 storage: the caller's buffers hold
+        # the storage type; results are the compute-precision transform of the quantised
+        # input, quantised to the storage type
+        store = np.float16 if case["precision"] == "F16_STORAGE_F32_COMPUTE" else np.float32
+        cfg = V.FftConfig(dims).with_batch_count(batch).with_precision(V.Precision[case["precision"]])
+        real = case.get("real", False)
+        if real:
+            cfg = cfg.with_transform(V.TransformKind.R2C)
+            x = rng.uniform(-1, 1, (batch,) + tuple(dims)).astype(store)
+            ref = oracle.r2c_nd(x.astype(np.float64), len(dims), threads=4)
+        else:
+            x = rng.uniform(-1, 1, (batch,) + tuple(dims) + (2,)).astype(store)
+            ref = oracle.fft_nd(x[..., 0].astype(np.float64) + 1j * x[..., 1].astype(np.float64), len(dims),
+                                threads=4)
+        ref_q = ref.view(np.float64).astype(store).astype(np.float64).view(np.complex128)
+        y, n = emulate(V, lib, cfg, V.Direction.FORWARD, dev, x, ref.size * 2, store)
+        return {"err": rel_l2(y.astype(np.float64).view(np.complex128), ref_q), "launches": n}
     elif kind == "kprep":
         # kernelConvolution preparation: the forward transform of batch x coordinate systems
         C = case["coords"]

@@ -103,6 +103,12 @@ CASES = [
     dict(kind="kprep", dims=[64], batch=2, prec="F64", coords=3),
     dict(kind="kprep", dims=[60], batch=1, prec="F32", coords=2, real=True),
     dict(kind="kprep", dims=[16, 10], batch=2, prec="F64", coords=2, real=True),
+    # mixed storage / compute precision (config.rs:107-161)
+    dict(kind="mixed", dims=[64], batch=3, prec="F32", precision="F16_STORAGE_F32_COMPUTE"),
+    dict(kind="mixed", dims=[60], batch=2, prec="F32", precision="F16_STORAGE_F32_COMPUTE", real=True),
+    dict(kind="mixed", dims=[64], batch=3, prec="F64", precision="F64_COMPUTE_F32_STORAGE"),
+    dict(kind="mixed", dims=[16, 10], batch=2, prec="F64", precision="F64_COMPUTE_F32_STORAGE", real=True),
+    dict(kind="mixed", dims=[4099], batch=1, prec="F64", precision="F64_COMPUTE_F32_STORAGE"),
 ]
 
 
@@ -114,7 +120,8 @@ def results():
 
 @pytest.mark.parametrize("i", range(len(CASES)), ids=[f"{c['kind']}{'-' + c['mode'] if 'mode' in c else ''}-{c['dims']}-{c['prec']}"
                               + (f"-P{c['nranks']}" if "nranks" in c else "") + (f"-pad{c['pad']}" if "pad" in c else "")
-                              + ("-strided" if "in_strides" in c or "out_strides" in c else "") for c in CASES])
+                              + ("-strided" if "in_strides" in c or "out_strides" in c else "")
+                              + (f"-{c['precision']}" if "precision" in c else "") for c in CASES])
 def test_emulated_program_matches_oracle(results, i):
     r = results[i]
     assert "error" not in r, r

@@ -283,3 +283,40 @@ def test_async_submissions_match_synchronous_execution(V, ctx):
     bad = ctx.submit_transform(irs[0], xs[0], out=np.empty(irs[0].output_elements - 1, dtype=np.complex64))
     with pytest.raises(V.VkFftError):
         bad.wait()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision,real", [("F16_STORAGE_F32_COMPUTE", False), ("F16_STORAGE_F32_COMPUTE", True),
+                                            ("F64_COMPUTE_F32_STORAGE", False), ("F64_COMPUTE_F32_STORAGE", True)])
+def test_mixed_storage_compute_precision(V, ctx, precision, real):
+    """F16 storage / F32 compute and F64 compute / F32 storage (config.rs:107-161): host arrays
+    of the API type (f32 / f64) through execute_transform, storage-typed device buffers
+    through execute_resident; both equal the compute-precision transform of the input
+    quantised to storage, quantised to storage again (the reference's mixed-precision
+    expectation, tests/convolution_runtime.rs:116-140)."""
+    torch = pytest.importorskip("torch")
+    store = np.float16 if precision.startswith("F16") else np.float32
+    api = np.float32 if precision.startswith("F16") else np.float64
+    dims, batch = ([4096], 16) if not real else ([2048], 8)
+    cfg = V.FftConfig(dims).with_batch_count(batch).with_precision(V.Precision[precision])
+    if real:
+        cfg = cfg.with_transform(V.TransformKind.R2C)
+    ir = V.TransformIr.build(cfg, V.Direction.FORWARD, ctx.device_profile())
+    rng = np.random.default_rng(17)
+    n_in = ir.input_elements * (1 if real else 2)
+    xq = rng.uniform(-1, 1, n_in).astype(store)                     # values representable in storage
+    x64 = xq.astype(np.float64)
+    ref = (oracle.r2c_nd(x64.reshape(batch, *dims), 1) if real
+           else oracle.fft_nd(x64.view(np.complex128).reshape(batch, *dims), 1))
+    ref_q = ref.view(np.float64).astype(store).astype(np.float64)
+    host_in = xq.astype(api)
+    host = ctx.execute_transform(ir, host_in if real else host_in.view(np.complex64 if api == np.float32
+                                                                       else np.complex128))
+    tol = 2e-3 if store == np.float16 else 1e-6
+    assert rel_l2(np.asarray(host).view(api).astype(np.float64), ref_q) <= tol
+    tdt = torch.float16 if store == np.float16 else torch.float32
+    xd = torch.from_numpy(xq).cuda()
+    yd = torch.empty(ir.output_elements * 2, dtype=tdt, device="cuda")
+    ctx.execute_resident(ir, xd.data_ptr(), yd.data_ptr(), stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rel_l2(yd.cpu().numpy().astype(np.float64), ref_q) <= tol

@@ -6,7 +6,7 @@
 
 #include <algorithm>
 
-#include "pass_device.cuh"
+#include "boundary_device.cuh"
 
 namespace b200fft {
 

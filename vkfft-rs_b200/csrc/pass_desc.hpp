@@ -169,7 +169,9 @@ struct BoundaryCopy {
     void *dst;
     int64_t total;       // logical elements over all batches
     int32_t rank;
-    int32_t elem_bytes;  // 4, 8 or 16
+    int32_t scalars;     // scalars per element: 1 (real) or 2 (complex)
+    int32_t src_bytes;   // bytes per scalar of the source: 2 (f16), 4 (f32), 8 (f64)
+    int32_t dst_bytes;   // ... of the destination (a conversion when they differ)
     int64_t dims[kMaxCopyRank];
     int64_t src_stride[kMaxCopyRank], dst_stride[kMaxCopyRank];
     int64_t src_batch, dst_batch;

@@ -73,6 +73,12 @@ struct Program {
     size_t input_elems = 0, output_elems = 0;
     bool input_real = false, output_real = false;
     double algorithmic_flops = 0;  // 5 N log2 N per complex transform (for reports)
+    int storage_scalar_bytes = 0;  // bytes of one stored scalar of the caller's buffers: 2 (f16),
+                                   // 4, 8; 0 = the compute precision's
+
+    size_t io_scalar_bytes() const { return storage_scalar_bytes ? (size_t)storage_scalar_bytes : (is_double ? 8 : 4); }
+    size_t input_bytes() const { return input_elems * io_scalar_bytes() * (input_real ? 1 : 2); }
+    size_t output_bytes() const { return output_elems * io_scalar_bytes() * (output_real ? 1 : 2); }
 
     size_t scratch_offset(int k) const {  // byte offset of scratch buffer k (256-byte aligned)
         size_t off = 0;

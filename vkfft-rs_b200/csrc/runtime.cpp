@@ -1,6 +1,8 @@
 // CUDA runtime side of the B200 FFT engine.
 #include "runtime.hpp"
 
+#include <cuda_fp16.h>
+
 #include <algorithm>
 #include <atomic>
 #include <cstdlib>
@@ -289,11 +291,10 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
 
 void execute_program_host(Context *ctx, uint64_t id, const Program &prog, const void *in, size_t in_bytes, void *out,
                           size_t out_bytes) {
-    const size_t esz = prog.is_double ? 16 : 8;
-    const size_t in_need = prog.input_elems * (prog.input_real ? esz / 2 : esz);
-    const size_t out_need = prog.output_elems * (prog.output_real ? esz / 2 : esz);
-    if (in_bytes != in_need) fail_input_length(prog.input_elems, in_bytes / (prog.input_real ? esz / 2 : esz));
-    if (out_bytes != out_need) fail_input_length(prog.output_elems, out_bytes / (prog.output_real ? esz / 2 : esz));
+    const size_t in_need = prog.input_bytes(), out_need = prog.output_bytes();
+    const size_t in_el = in_need / std::max<size_t>(prog.input_elems, 1), out_el = out_need / std::max<size_t>(prog.output_elems, 1);
+    if (in_bytes != in_need) fail_input_length(prog.input_elems, in_bytes / std::max<size_t>(in_el, 1));
+    if (out_bytes != out_need) fail_input_length(prog.output_elems, out_bytes / std::max<size_t>(out_el, 1));
     check(cudaSetDevice(ctx->device), "cudaSetDevice");
     void *din, *dout;
     {
@@ -370,6 +371,36 @@ static Transform *chunk_transform(Transform &t, size_t batch) {
     return t.chunks.emplace(batch, std::move(c)).first->second.get();
 }
 
+// Mixed precision through the host API: the arrays are of the API type (f32 for F16
+// storage, f64 for F64 compute / F32 storage, as execute_transform_f32 / _f64 take them);
+// they are converted to and from the storage type around the execution.
+static void execute_mixed_host(Context *ctx, Transform &t, const void *in, size_t in_bytes, void *out,
+                               size_t out_bytes) {
+    const Program &prog = t.prog;
+    const size_t api = t.config.precision == Precision::F16StorageF32Compute ? 4 : 8;
+    const size_t sb = prog.io_scalar_bytes();
+    const size_t n_in = prog.input_elems * (prog.input_real ? 1 : 2), n_out = prog.output_elems * (prog.output_real ? 1 : 2);
+    if (in_bytes != n_in * api) fail_input_length(prog.input_elems, in_bytes / (api * (prog.input_real ? 1 : 2)));
+    if (out_bytes != n_out * api) fail_input_length(prog.output_elems, out_bytes / (api * (prog.output_real ? 1 : 2)));
+    std::vector<unsigned char> si(n_in * sb), so(n_out * sb);
+    for (size_t k = 0; k < n_in; k++) {
+        const double v = api == 8 ? static_cast<const double *>(in)[k] : static_cast<const float *>(in)[k];
+        if (sb == 2)
+            reinterpret_cast<__half *>(si.data())[k] = __float2half_rn((float)v);
+        else
+            reinterpret_cast<float *>(si.data())[k] = (float)v;
+    }
+    execute_program_host(ctx, t.id, prog, si.data(), si.size(), so.data(), so.size());
+    for (size_t k = 0; k < n_out; k++) {
+        const double v = sb == 2 ? (double)__half2float(reinterpret_cast<const __half *>(so.data())[k])
+                                 : (double)reinterpret_cast<const float *>(so.data())[k];
+        if (api == 8)
+            static_cast<double *>(out)[k] = v;
+        else
+            static_cast<float *>(out)[k] = (float)v;
+    }
+}
+
 // Host arrays are logical tensors (the reference packs formatted layouts internally,
 // nd_real_ir.rs:715-750): a transform with formatted buffer strides runs its dense twin.
 static Transform &host_view(Transform &t) {
@@ -391,9 +422,11 @@ void execute_transform_host(Context *ctx, Transform &t_in, const void *in, size_
     std::lock_guard<std::mutex> host_lock(ctx->host_mu);  // the worker thread may run one too
     Transform &t = host_view(t_in);
     const Program &prog = t.prog;
-    const size_t esz = prog.is_double ? 16 : 8;
-    const size_t in_need = prog.input_elems * (prog.input_real ? esz / 2 : esz);
-    const size_t out_need = prog.output_elems * (prog.output_real ? esz / 2 : esz);
+    if (prog.storage_scalar_bytes) {
+        execute_mixed_host(ctx, t, in, in_bytes, out, out_bytes);
+        return;
+    }
+    const size_t in_need = prog.input_bytes(), out_need = prog.output_bytes();
     const size_t batch = t.plan.config.kernel_preparation_system_count();
     constexpr size_t kChunkBytes = size_t(128) << 20;  // input bytes per sub-batch
     const size_t in_per = batch ? in_need / batch : 0, out_per = batch ? out_need / batch : 0;

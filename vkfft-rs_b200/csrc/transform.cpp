@@ -29,8 +29,15 @@ static size_t product(const std::vector<size_t> &v, size_t from, size_t to) {
     return acc;
 }
 
+// Bytes of one compute / stored scalar of a precision (config.rs:107-161 layouts).
+static bool compute_is_f64(Precision p) { return p == Precision::F64 || p == Precision::F64ComputeF32Storage; }
+static int storage_scalar_bytes(Precision p) {
+    return p == Precision::F16StorageF32Compute ? 2 : (p == Precision::F64 ? 8 : 4);
+}
+
 static void check_executable(const FftConfig &c) {
-    if (!(c.precision == Precision::F32 || c.precision == Precision::F64))
+    if (!(c.precision == Precision::F32 || c.precision == Precision::F64 ||
+          c.precision == Precision::F16StorageF32Compute || c.precision == Precision::F64ComputeF32Storage))
         fail_precision("B200 engine", precision_name(c.precision));
     if (!(c.transform == TransformKind::C2C || c.transform == TransformKind::R2C || c.transform == TransformKind::C2R))
         fail_unsupported("B200 engine executes C2C, R2C and C2R transforms (R2R is outside the FFT hot path)");
@@ -74,7 +81,12 @@ static void add_boundaries(Transform &t) {
     t.logical_in_elems = prog.input_elems;
     t.logical_out_elems = prog.output_elems;
     t.formatted = fmt_in || fmt_out;
-    if (!pad_in && !pad_out && !fmt_in && !fmt_out) return;
+    // mixed precision (F16 storage / F32 compute, F64 compute / F32 storage): the caller's
+    // buffers hold the storage type, converted at the boundary copies
+    const int sbytes = storage_scalar_bytes(c.precision), cbytes = prog.is_double ? 8 : 4;
+    const bool mixed = sbytes != cbytes;
+    if (mixed) prog.storage_scalar_bytes = sbytes;
+    if (!pad_in && !pad_out && !fmt_in && !fmt_out && !mixed) return;
     if (c.dimensions.size() > (size_t)kMaxCopyRank) fail_unsupported("boundary copies support rank <= 8");
     const size_t batch = c.kernel_preparation_system_count();
     const size_t esz = prog.is_double ? 16 : 8;
@@ -89,7 +101,9 @@ static void add_boundaries(Transform &t) {
         for (size_t d : dims) tensor *= d;
         b.total = (int64_t)(tensor * batch);
         b.rank = (int32_t)dims.size();
-        b.elem_bytes = (int32_t)elem_bytes;
+        b.scalars = (int32_t)(elem_bytes / (size_t)cbytes);
+        b.src_bytes = input ? sbytes : cbytes;
+        b.dst_bytes = input ? cbytes : sbytes;
         for (size_t a = 0; a < dims.size(); a++) {
             b.dims[a] = (int64_t)dims[a];
             const int64_t formatted = (int64_t)fst[a], dense = dst_dense[a];
@@ -109,7 +123,7 @@ static void add_boundaries(Transform &t) {
         for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
         return std::make_pair(pp, fbatch * batch);
     };
-    if (pad_in || fmt_in) {
+    if (pad_in || fmt_in || mixed) {
         const size_t eb = r2c ? esz / 2 : esz;
         for (PassPlan &pp : prog.passes)
             if (pp.src_buf == BUF_IN) pp.src_buf = BUF_SCRATCH4;
@@ -118,7 +132,7 @@ static void add_boundaries(Transform &t) {
         prog.passes.insert(prog.passes.begin(), pp);
         prog.input_elems = physical;
     }
-    if (pad_out || fmt_out) {
+    if (pad_out || fmt_out || mixed) {
         const size_t eb = c2r ? esz / 2 : esz;
         for (PassPlan &pp : prog.passes) {
             if (pp.src_buf == BUF_OUT) pp.src_buf = BUF_SCRATCH5;
@@ -159,7 +173,7 @@ static std::unique_ptr<Transform> build_transform_core(const FftConfig &config_i
     const size_t batch = c.kernel_preparation_system_count();
     t->children.assign(rank, std::nullopt);
     Program &prog = t->prog;
-    prog.is_double = c.precision == Precision::F64;
+    prog.is_double = compute_is_f64(c.precision);
 
     if (c.transform == TransformKind::C2C) {
         const size_t tensor = product(c.dimensions, 0, rank);

@@ -618,9 +618,13 @@ def upstream_bluestein_auto_padding(sequence_len, batch_count, precision, device
 
 # ---- application.rs ----------------------------------------------------------------
 
+# host-API array types (execute_transform_f32 / _f64): mixed precisions take the API type,
+# the device buffers of execute_resident hold the storage type (float16 / float32)
 _np_dtype = {
     (Precision.F32, True): np.float32, (Precision.F32, False): np.complex64,
     (Precision.F64, True): np.float64, (Precision.F64, False): np.complex128,
+    (Precision.F16_STORAGE_F32_COMPUTE, True): np.float32, (Precision.F16_STORAGE_F32_COMPUTE, False): np.complex64,
+    (Precision.F64_COMPUTE_F32_STORAGE, True): np.float64, (Precision.F64_COMPUTE_F32_STORAGE, False): np.complex128,
 }
 
 
