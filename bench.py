@@ -322,6 +322,11 @@ WORKLOADS = {
     "c2c-65537-f32": dict(kind="c2c", dims=[65537], batch=2048, prec="F32", config=4),
     "c2c-65537-f64": dict(kind="c2c", dims=[65537], batch=2048, prec="F64", config=4),
     "conv-2048": dict(kind="conv", dims=[2048, 2048], batch=64, prec="F32", config=5),
+    # DCT / DST (not a headline config): forward DCT-II + normalised inverse (DCT-III)
+    "dct2-4096-f32": dict(kind="r2r", r2r="DCT2", dims=[4096], batch=16384, prec="F32", config=0),
+    "dct2-4096-f64": dict(kind="r2r", r2r="DCT2", dims=[4096], batch=8192, prec="F64", config=0),
+    "dct4-4096-f32": dict(kind="r2r", r2r="DCT4", dims=[4096], batch=16384, prec="F32", config=0),
+    "dct2-512^2-f32": dict(kind="r2r", r2r="DCT2", dims=[512, 512], batch=256, prec="F32", config=0),
 }
 
 
@@ -463,6 +468,14 @@ def run_workload(args):
             b = torch.empty_like(a)
             flop = 2 * 5.0 * n * math.log2(n) * batch
             alg_bytes = [2 * batch * n * 2 * rsz] * 2
+        elif kind == "r2r":
+            rc = cfg.with_transform(V.TransformKind[wl["r2r"]])
+            fwd = V.TransformIr.build(rc, V.Direction.FORWARD, dev)
+            inv = V.TransformIr.build(rc, V.Direction.INVERSE, dev)
+            a = torch.rand((batch * n,), device="cuda", generator=gen, dtype=tdt) * 2 - 1
+            b = torch.empty_like(a)
+            flop = 2 * 2.5 * n * math.log2(n) * batch
+            alg_bytes = [2 * batch * n * rsz] * 2
         else:
             fwd = V.TransformIr.build(cfg.with_transform(V.TransformKind.R2C), V.Direction.FORWARD, dev)
             inv = V.TransformIr.build(cfg.with_transform(V.TransformKind.C2R), V.Direction.INVERSE, dev)
@@ -505,10 +518,11 @@ def run_workload(args):
     achieved = [alg_bytes[j] / (part_ms[j] * 1e-3) / 1e9 for j in range(len(launches))]
     value = flop * ws / (ms * 1e-3) / 1e9
     line = {
-        "metric": f"{args.workload} GFLOP/s (5N*log2N complex, 2.5N*log2N real)", "value": value, "unit": "GFLOP/s",
+        "metric": f"{args.workload} GFLOP/s (5N*log2N complex, 2.5N*log2N real and DCT/DST)", "value": value, "unit": "GFLOP/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": prec.lower(), "data": "synthetic (torch generator)",
-        "config": {"workload": f"BASELINE config {wl['config']}: {kind} {dims} x batch {batch}"
+        "config": {"workload": (f"BASELINE config {wl['config']}: " if wl["config"] else f"{wl.get('r2r')} ")
+                               + f"{kind} {dims} x batch {batch}"
                                + (" recursive Rader tuning" if wl.get("tuning") else ""),
                    "global_batch": batch * ws, "parallelism": f"replicas x{ws}" if ws > 1 else "1 GPU"},
         "parts_ms": part_ms,

@@ -180,7 +180,8 @@ typedef enum b200fft_real_algorithm { B200FFT_REAL_FULL_COMPLEX = 0, B200FFT_REA
 /* TransformIr family (application.rs:31-45), the non-DD members */
 typedef enum b200fft_family {
     B200FFT_FAMILY_COMPLEX_1D = 0, B200FFT_FAMILY_COMPLEX_ND = 1,
-    B200FFT_FAMILY_REAL = 2, B200FFT_FAMILY_REAL_ND = 3
+    B200FFT_FAMILY_REAL = 2, B200FFT_FAMILY_REAL_ND = 3,
+    B200FFT_FAMILY_REAL_TO_REAL = 4, B200FFT_FAMILY_REAL_TO_REAL_ND = 5
 } b200fft_family;
 
 typedef struct b200fft_plan b200fft_plan;           /* FftPlan */
@@ -248,7 +249,8 @@ uint64_t b200fft_transform_real_transform_len(const b200fft_transform *transform
 /* The device-scored plan the transform executes (top level) */
 const b200fft_plan *b200fft_transform_plan(const b200fft_transform *transform);
 /* The 1D child plan executed for one tensor axis (nd_ir.rs:676-708 child plans;
- * real_ir.rs:326-345 internal plan for the real axis) */
+ * real_ir.rs:326-345 internal plan for the real axis; for DCT/DST the internal FFT of
+ * the axis's reduction, r2r_ir.rs:689-940) */
 b200fft_status b200fft_transform_axis_child_info(const b200fft_transform *transform, uint32_t axis,
                                                  b200fft_axis_info *info);
 /* Element counts (complex or real) of the logical input / output tensors: the sizes of

@@ -201,3 +201,80 @@ def convolve_c2c(x, kernel_spectrum, dims, batch=1, coordinates=1, kernels=1, ma
             else:
                 out[s * C + oc] = norm(prep(spec[in_s * C + oc]) * ker[kid])
     return fft_nd(out.reshape((out_systems * C,) + dims), len(dims), inverse=True, normalize=True, threads=threads)
+
+
+# ---- DCT / DST ----------------------------------------------------------------------
+# The eight FFTW real-to-real kinds as the reference's direct evaluator states them
+# (r2r_ir.rs:2351-2433, evaluate_bin): REDFT00/10/01/11 = DCT-I..IV, RODFT00/10/01/11 =
+# DST-I..IV, unnormalised.  The inverse direction evaluates the inverse partner
+# (II <-> III, the others self, r2r_ir.rs:2317-2325) and, with normalisation, scales
+# by inverse_pair_scale (r2r_ir.rs:2327-2349).  Each bin is a direct O(N) sum; the
+# trigonometric arguments are reduced exactly in integers before the cosine/sine.
+R2R_KINDS = ("DCT1", "DCT2", "DCT3", "DCT4", "DST1", "DST2", "DST3", "DST4")
+
+
+def _trig(fn, num, den):
+    """fn(pi * num / den) with num reduced modulo 2 * den first."""
+    num = np.mod(num, 2 * den)
+    return fn(np.pi * num / den)
+
+
+def r2r_matrix(kind, n):
+    """n x n matrix of one unnormalised FFTW R2R kind (r2r_ir.rs:2351-2433)."""
+    k = np.arange(n, dtype=np.int64)[:, None]
+    j = np.arange(n, dtype=np.int64)[None, :]
+    alt = np.where(k % 2 == 0, 1.0, -1.0)[:, 0]
+    if kind == "DCT1":
+        if n < 2:
+            raise ValueError("DCT-I needs n >= 2")
+        m = 2.0 * _trig(np.cos, j * k, n - 1)
+        m[:, 0] = 1.0
+        m[:, n - 1] = alt
+    elif kind == "DCT2":
+        m = 2.0 * _trig(np.cos, (2 * j + 1) * k, 2 * n)
+    elif kind == "DCT3":
+        m = 2.0 * _trig(np.cos, j * (2 * k + 1), 2 * n)
+        m[:, 0] = 1.0
+    elif kind == "DCT4":
+        m = 2.0 * _trig(np.cos, (2 * j + 1) * (2 * k + 1), 4 * n)
+    elif kind == "DST1":
+        m = 2.0 * _trig(np.sin, (j + 1) * (k + 1), n + 1)
+    elif kind == "DST2":
+        m = 2.0 * _trig(np.sin, (2 * j + 1) * (k + 1), 2 * n)
+    elif kind == "DST3":
+        m = 2.0 * _trig(np.sin, (j + 1) * (2 * k + 1), 2 * n)
+        m[:, n - 1] = alt
+    elif kind == "DST4":
+        m = 2.0 * _trig(np.sin, (2 * j + 1) * (2 * k + 1), 4 * n)
+    else:
+        raise ValueError(kind)
+    return m
+
+
+def r2r_inverse_partner(kind):
+    return {"DCT2": "DCT3", "DCT3": "DCT2", "DST2": "DST3", "DST3": "DST2"}.get(kind, kind)
+
+
+def r2r_inverse_pair_scale(kind, n):
+    if kind == "DCT1":
+        return 1.0 / (2 * (n - 1))
+    if kind == "DST1":
+        return 1.0 / (2 * (n + 1))
+    return 1.0 / (2 * n)
+
+
+def r2r_nd(x, kind, ndim, inverse=False, normalize=False, omitted=()):
+    """DCT/DST over the last ``ndim`` axes of ``x`` (leading axes are batch): the 1D
+    definition applied along every non-omitted axis (NdR2rIr, r2r_ir.rs:1795-2017)."""
+    x = np.asarray(x, dtype=np.float64)
+    eff = r2r_inverse_partner(kind) if inverse else kind
+    for a in range(ndim):
+        if a in omitted:
+            continue
+        axis = x.ndim - ndim + a
+        n = x.shape[axis]
+        m = r2r_matrix(eff, n)
+        if inverse and normalize:
+            m = m * r2r_inverse_pair_scale(kind, n)
+        x = np.moveaxis(np.tensordot(m, np.moveaxis(x, axis, 0), axes=(1, 0)), 0, axis)
+    return x

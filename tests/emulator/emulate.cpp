@@ -73,6 +73,18 @@ static void run_program(const Program &prog, const void *in, void *out, const Pe
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scratch[k].empty() ? nullptr : scratch[k].data();
     int err = 0;
     for (const PassPlan &pp : prog.passes) {
+        if (pp.kernel == KERNEL_R2R) {
+            R2rPass rr = pp.rr;
+            rr.src = bufs[pp.src_buf];
+            rr.dst = bufs[pp.dst_buf];
+            for (int64_t t = 0; t < rr.total; t++) {
+                if (prog.is_double)
+                    r2r_one<double>(rr, t);
+                else
+                    r2r_one<float>(rr, t);
+            }
+            continue;
+        }
         if (pp.kernel == KERNEL_CMUL) {
             ConvMultiply cm = pp.cm;
             cm.src = bufs[pp.src_buf];

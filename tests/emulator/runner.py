@@ -80,6 +80,26 @@ def run(case, V, lib):
         ref_q = ref.view(np.float64).astype(store).astype(np.float64).view(np.complex128)
         y, n = emulate(V, lib, cfg, V.Direction.FORWARD, dev, x, ref.size * 2, store)
         return {"err": rel_l2(y.astype(np.float64).view(np.complex128), ref_q), "launches": n}
+    elif kind == "r2r":
+        # DCT / DST (r2r_ir.rs): real in, real out; inverse = partner kind x pair scale
+        x = rng.uniform(-1, 1, shape).astype(rdt)
+        inverse = case.get("inverse", False)
+        cfg = cfg.with_transform(V.TransformKind[case["r2r"]])
+        for a, (lo, hi) in case.get("pad", {}).items():
+            cfg = cfg.with_zero_padding(int(a), lo, hi)
+        for a in case.get("omit", []):
+            cfg = cfg.with_omit_dimension(a, True)
+        d = V.Direction.INVERSE if inverse else V.Direction.FORWARD
+        xin = x.astype(np.float64)
+        pads = {int(a): v for a, v in case.get("pad", {}).items()}
+        if pads and not inverse:
+            xin = xin * _pad_keep(dims, pads)
+        ref = oracle.r2r_nd(xin, case["r2r"], len(dims), inverse=inverse, normalize=case.get("normalize", False),
+                            omitted=tuple(case.get("omit", [])))
+        if pads and inverse:
+            ref = ref * _pad_keep(dims, pads)
+        y, n = emulate(V, lib, cfg, d, dev, x, ref.size, rdt)
+        return {"err": rel_l2(y, ref), "launches": n}
     elif kind == "kprep":
         # kernelConvolution preparation: the forward transform of batch x coordinate systems
         C = case["coords"]
@@ -184,6 +204,16 @@ def run_slab(case, V, lib, dev, cfg, rng, cdt, rdt):
     if st != 0:
         raise V.VkFftError(st, err.value.decode())
     return {"err": rel_l2(out, ref), "launches": launches.value}
+
+
+def _pad_keep(dims, pads):
+    """1 outside and 0 inside the zero-padding ranges [lo, hi) of the given axes."""
+    keep = np.ones(tuple(dims))
+    for a, (lo, hi) in pads.items():
+        idx = [slice(None)] * len(dims)
+        idx[a] = slice(lo, hi)
+        keep[tuple(idx)] = 0.0
+    return keep
 
 
 def _pad_mask(dims, pads):

@@ -2,17 +2,18 @@
 
 The vkfft-rs crate commits FFTW 3.3.9 outputs under ``tests/fixtures/`` (see
 ``tests/fixtures/README.md`` of the crate).  The GPU box has no copy of the
-reference, so this script parses the C2C and R2C cases (DCT cases are outside
-the FFT hot path) and stores them as ``fftw_golden.npz`` next to itself.
+reference, so this script parses the C2C, R2C and DCT-II (FFTW REDFT10) cases and
+stores them as ``fftw_golden.npz`` next to itself.
 
 Run once in a container that has the reference mounted::
 
     python tests/golden/make_golden.py /path/to/vkfft-rs
 
 Layout of the archive: for every case ``<set>/<name>`` there are arrays
-``<set>/<name>/shape`` (int64), ``<set>/<name>/kind`` (0 = c2c, 1 = r2c),
-``<set>/<name>/output`` (complex128) and, for the compact set whose inputs are
-stored inline, ``<set>/<name>/input`` (complex128 or float64).
+``<set>/<name>/shape`` (int64), ``<set>/<name>/kind`` (0 = c2c, 1 = r2c,
+2 = dct2), ``<set>/<name>/output`` (complex128; float64 for dct2) and, for the
+compact set whose inputs are stored inline, ``<set>/<name>/input`` (complex128 or
+float64).
 
 Sets: ``medium`` (fftw_precision_medium_v1.txt, f64 input formulas),
 ``medium_f32`` (fftw_precision_medium_f32_v1.txt, inputs evaluated in float),
@@ -40,10 +41,11 @@ def parse_medium(path):
         count = int(lines[i + 4][len("output "):])
         body = lines[i + 5:i + 5 + count]
         i += 5 + count
-        if kind not in ("c2c", "r2c"):
+        if kind not in ("c2c", "r2c", "dct2"):
             continue
         vals = np.array([[float(v) for v in ln.split()] for ln in body])
-        cases[name] = dict(kind=kind, shape=shape, output=vals[:, 0] + 1j * vals[:, 1])
+        out = vals[:, 0] if kind == "dct2" else vals[:, 0] + 1j * vals[:, 1]
+        cases[name] = dict(kind=kind, shape=shape, output=out)
     return cases
 
 
@@ -71,8 +73,12 @@ def parse_compact(path):
             vals = np.array([[float(v) for v in ln.split()] for ln in lines[i + 1:i + 1 + count]])
             i += 1 + count
             cases[name] = dict(kind=kind, shape=[n], input=inp, output=vals[:, 0] + 1j * vals[:, 1])
+        elif kind == "dct2":
+            vals = np.array([[float(v) for v in ln.split()] for ln in lines[i:i + n]])
+            i += n
+            cases[name] = dict(kind=kind, shape=[n], input=vals[:, 0], output=vals[:, 1])
         else:
-            # skip a non-FFT case (DCT): consume until the next "case" line
+            # skip any other case kind: consume until the next "case" line
             while i < len(lines) and not lines[i].startswith("case "):
                 i += 1
     return cases
@@ -90,8 +96,9 @@ def main(ref_root):
         for name, case in cases.items():
             key = f"{set_name}/{name}"
             arrays[key + "/shape"] = np.array(case["shape"], dtype=np.int64)
-            arrays[key + "/kind"] = np.array(0 if case["kind"] == "c2c" else 1, dtype=np.int64)
-            arrays[key + "/output"] = np.asarray(case["output"], dtype=np.complex128)
+            arrays[key + "/kind"] = np.array({"c2c": 0, "r2c": 1, "dct2": 2}[case["kind"]], dtype=np.int64)
+            arrays[key + "/output"] = np.asarray(case["output"],
+                                                 dtype=np.float64 if case["kind"] == "dct2" else np.complex128)
             if "input" in case:
                 arrays[key + "/input"] = np.asarray(case["input"])
     out = os.path.join(HERE, "fftw_golden.npz")

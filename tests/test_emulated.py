@@ -103,6 +103,18 @@ CASES = [
     dict(kind="kprep", dims=[64], batch=2, prec="F64", coords=3),
     dict(kind="kprep", dims=[60], batch=1, prec="F32", coords=2, real=True),
     dict(kind="kprep", dims=[16, 10], batch=2, prec="F64", coords=2, real=True),
+    # DCT / DST (r2r_ir.rs): every kind, odd/even lengths, ND, inverse pairs, padding
+    *[dict(kind="r2r", r2r=k, dims=[n], batch=3, prec=p) for k in
+      ("DCT1", "DCT2", "DCT3", "DCT4", "DST1", "DST2", "DST3", "DST4") for n in (2, 17, 64) for p in ("F32", "F64")],
+    *[dict(kind="r2r", r2r=k, dims=[n], batch=2, prec="F64") for k in ("DCT1", "DST4", "DCT4") for n in (3, 257, 4097)],
+    dict(kind="r2r", r2r="DCT1", dims=[1025], batch=2, prec="F32"),
+    dict(kind="r2r", r2r="DCT2", dims=[12, 10, 9], batch=2, prec="F64"),
+    dict(kind="r2r", r2r="DST3", dims=[16, 33], batch=1, prec="F32"),
+    dict(kind="r2r", r2r="DCT4", dims=[8, 12], batch=2, prec="F64", omit=[0]),
+    dict(kind="r2r", r2r="DCT2", dims=[40], batch=2, prec="F64", inverse=True, normalize=True),
+    dict(kind="r2r", r2r="DST1", dims=[6, 20], batch=2, prec="F64", inverse=True, normalize=True),
+    dict(kind="r2r", r2r="DCT3", dims=[32, 6], batch=1, prec="F32", pad={0: (20, 32)}),
+    dict(kind="r2r", r2r="DST2", dims=[32], batch=2, prec="F64", inverse=True, pad={0: (5, 9)}),
     # mixed storage / compute precision (config.rs:107-161)
     dict(kind="mixed", dims=[64], batch=3, prec="F32", precision="F16_STORAGE_F32_COMPUTE"),
     dict(kind="mixed", dims=[60], batch=2, prec="F32", precision="F16_STORAGE_F32_COMPUTE", real=True),
@@ -118,7 +130,8 @@ def results():
     return emulator.run_cases(CASES)
 
 
-@pytest.mark.parametrize("i", range(len(CASES)), ids=[f"{c['kind']}{'-' + c['mode'] if 'mode' in c else ''}-{c['dims']}-{c['prec']}"
+@pytest.mark.parametrize("i", range(len(CASES)), ids=[f"{c['kind']}{'-' + c['mode'] if 'mode' in c else ''}{'-' + c['r2r'] if 'r2r' in c else ''}"
+                              f"{'-inv' if c.get('inverse') else ''}-{c['dims']}-{c['prec']}"
                               + (f"-P{c['nranks']}" if "nranks" in c else "") + (f"-pad{c['pad']}" if "pad" in c else "")
                               + ("-strided" if "in_strides" in c or "out_strides" in c else "")
                               + (f"-{c['precision']}" if "precision" in c else "") for c in CASES])

@@ -53,8 +53,10 @@ def test_oracle_matches_fftw_medium(name):
     n = int(np.prod(shape))
     if kind == 0:
         got = oracle.fft(complex_v1(n)).ravel()
-    else:
+    elif kind == 1:
         got = oracle.r2c_nd(real_v1(n).reshape(shape), len(shape)).ravel()
+    else:  # ND DCT-II (FFTW REDFT10 on every axis)
+        got = oracle.r2r_nd(real_v1(n).reshape(shape), "DCT2", len(shape)).ravel()
     assert np.abs(got - expected).max() <= 2e-10 * n
 
 
@@ -68,8 +70,10 @@ def test_oracle_matches_fftw_medium_f32_inputs(name):
     n = int(np.prod(shape))
     if kind == 0:
         got = oracle.fft(complex_f32_v1(n)).ravel()
-    else:
+    elif kind == 1:
         got = oracle.r2c_nd(real_f32_v1(n).reshape(shape), len(shape)).ravel()
+    else:
+        got = oracle.r2r_nd(real_f32_v1(n).reshape(shape), "DCT2", len(shape)).ravel()
     # libm sinf/cosf and numpy float32 sin/cos may differ by an ulp of the input
     assert np.abs(got - expected).max() <= 1e-4 * n
 
@@ -80,6 +84,17 @@ def test_oracle_matches_fftw_compact_inline_inputs():
     assert np.abs(oracle.fft(x) - z["compact/c2c-n47/output"]).max() <= 2e-10 * 47
     r = z["compact/r2c-n45/input"]
     assert np.abs(oracle.r2c(r) - z["compact/r2c-n45/output"]).max() <= 2e-10 * 45
+    d = z["compact/dct2-n37/input"]
+    assert np.abs(oracle.r2r_nd(d, "DCT2", 1) - z["compact/dct2-n37/output"]).max() <= 2e-10 * 37
+
+
+@pytest.mark.parametrize("kind", ["DCT1", "DCT2", "DCT3", "DCT4", "DST1", "DST2", "DST3", "DST4"])
+def test_oracle_r2r_inverse_pairs(kind):
+    """Normalised inverse of every kind restores the input (inverse_partner and
+    inverse_pair_scale, r2r_ir.rs:2317-2349), over two axes and a batch axis."""
+    x = sample(3 * 9 * 10).reshape(3, 9, 10).real
+    y = oracle.r2r_nd(oracle.r2r_nd(x, kind, 2), kind, 2, inverse=True, normalize=True)
+    assert np.abs(y - x).max() <= 1e-13
 
 
 def sample(n):

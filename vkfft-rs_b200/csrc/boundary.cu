@@ -31,6 +31,22 @@ cudaError_t launch_conv_multiply(const ConvMultiply &m, bool dbl, cudaStream_t s
     return cudaGetLastError();
 }
 
+template <typename T>
+__global__ void __launch_bounds__(256) r2r_kernel(const __grid_constant__ R2rPass r) {
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < r.total; t += (int64_t)gridDim.x * blockDim.x)
+        r2r_one<T>(r, t);
+}
+
+cudaError_t launch_r2r(const R2rPass &r, bool dbl, cudaStream_t stream) {
+    if (r.total <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((r.total + 255) / 256, 148 * 32);
+    if (dbl)
+        r2r_kernel<double><<<(unsigned)blocks, 256, 0, stream>>>(r);
+    else
+        r2r_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(r);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_boundary_copy(const BoundaryCopy &b, cudaStream_t stream) {
     if (b.total <= 0) return cudaSuccess;
     const int64_t blocks = std::min<int64_t>((b.total + 255) / 256, 148 * 32);

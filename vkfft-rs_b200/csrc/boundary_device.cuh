@@ -1,9 +1,11 @@
-// Device routines of the element-wise passes: convolution multiply and boundary copy
-// (zero padding, formatted strides, storage <-> compute precision).  Included by
-// boundary.cu and by the CPU emulator.
+// Device routines of the element-wise passes: convolution multiply, boundary copy
+// (zero padding, formatted strides, storage <-> compute precision) and the DCT/DST
+// pre/post passes.  Included by boundary.cu and by the CPU emulator.
 #pragma once
 
 #include <cuda_fp16.h>
+
+#include <cmath>
 
 #include "pass_device.cuh"
 
@@ -92,6 +94,92 @@ B200FFT_HD void boundary_copy_one(const BoundaryCopy &b, int64_t L) {
     for (int k = 0; k < b.scalars; k++) {  // storage <-> compute precision
         const double v = zero ? 0.0 : load_scalar(b.src, so * b.scalars + k, b.src_bytes);
         store_scalar(b.dst, dof * b.scalars + k, b.dst_bytes, v);
+    }
+}
+
+// e^{i pi num / den} for an integer ratio, the argument reduced to [0, 2) exactly first.
+template <typename T>
+B200FFT_HD cplx<T> r2r_phase(int64_t num, int64_t den) {
+    const int64_t period = 2 * den;
+    num %= period;
+    if (num < 0) num += period;
+#ifdef __CUDA_ARCH__
+    T s, c;
+    if constexpr (sizeof(T) == 8)
+        sincospi((double)num / (double)den, &s, &c);
+    else
+        sincospif((float)num / (float)den, &s, &c);
+    return cplx<T>{c, s};
+#else
+    const double a = 3.14159265358979323846 * (double)num / (double)den;
+    return cplx<T>{(T)std::cos(a), (T)std::sin(a)};
+#endif
+}
+
+template <typename T>
+B200FFT_HD cplx<T> r2r_cmul(cplx<T> a, cplx<T> b) {
+    return cplx<T>{a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x};
+}
+
+// One element of an R2R pre pass (real tensor -> complex work array) or post pass
+// (FFT output -> real tensor).
+template <typename T>
+B200FFT_HD void r2r_one(const R2rPass &r, int64_t t) {
+    const int64_t n = r.n, L = r.L, inner = r.inner;
+    const int64_t i = t % inner;
+    const int64_t rest = t / inner;
+    const bool dst = r.kind >= 4;
+    const int type = r.kind & 3;  // 0..3 = I..IV
+    if (r.pre) {
+        const int64_t m = rest % L, o = rest / L;
+        const T *x = reinterpret_cast<const T *>(r.src) + o * n * inner + i;
+        auto at = [&](int64_t j) { return x[j * inner]; };
+        cplx<T> v{T(0), T(0)};
+        if (type == 0) {
+            if (!dst)
+                v.x = m < n ? at(m) : at(L - m);
+            else if (m != 0 && m != n + 1)
+                v.x = m <= n ? at(m - 1) : -at(L - m - 1);
+        } else if (type == 1) {
+            const int64_t split = (n + 1) / 2;
+            const int64_t s = m < split ? 2 * m : 2 * (n - m) - 1;
+            v.x = (dst && (s & 1)) ? -at(s) : at(s);
+        } else if (type == 2) {
+            const T a = dst ? at(n - 1 - m) : at(m);
+            const T b = m == 0 ? T(0) : (dst ? at(m - 1) : at(n - m));
+            v = r2r_cmul(cplx<T>{a, -b}, r2r_phase<T>(m, 2 * n));
+        } else if ((n & 1) == 0) {
+            const T a = at(2 * m), b = at(n - 1 - 2 * m);
+            v = r2r_cmul(cplx<T>{a, dst ? b : -b}, r2r_phase<T>(m, n));
+        } else if (m < n) {
+            const cplx<T> w = r2r_phase<T>(-m, 2 * n);
+            const T a = at(m);
+            v = cplx<T>{a * w.x, a * w.y};
+        }
+        reinterpret_cast<cplx<T> *>(r.dst)[(o * L + m) * inner + i] = v;
+    } else {
+        const int64_t k = rest % n, o = rest / n;
+        const cplx<T> *Y = reinterpret_cast<const cplx<T> *>(r.src) + o * L * inner + i;
+        auto at = [&](int64_t j) { return Y[j * inner]; };
+        T v;
+        if (type == 0) {
+            v = dst ? -at(k + 1).y : at(k).x;
+        } else if (type == 1) {
+            const int64_t q = dst ? n - 1 - k : k;
+            v = T(2) * r2r_cmul(at(q), r2r_phase<T>(-q, 2 * n)).x;
+        } else if (type == 2) {
+            v = at((k & 1) == 0 ? k / 2 : n - 1 - k / 2).x;
+            if (dst && (k & 1)) v = -v;
+        } else if ((n & 1) == 0) {
+            cplx<T> y = (k & 1) == 0 ? at(k / 2) : at(L - (k + 1) / 2);
+            if (k & 1) y.y = -y.y;
+            const cplx<T> rot = r2r_cmul(y, r2r_phase<T>(2 * k + 1, 4 * n));
+            v = T(2) * (dst ? rot.y : rot.x);
+        } else {
+            const cplx<T> rot = r2r_cmul(at(k), r2r_phase<T>(-(2 * k + 1), 4 * n));
+            v = T(2) * (dst ? -rot.y : rot.x);
+        }
+        reinterpret_cast<T *>(r.dst)[(o * n + k) * inner + i] = v * T(r.scale);
     }
 }
 

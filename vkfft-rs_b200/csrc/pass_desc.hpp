@@ -158,6 +158,32 @@ struct ConvMultiply {
     int32_t _pad;
 };
 
+// DCT / DST of one axis (r2r_ir.rs:621-1110) as pre pass -> complex FFT of length L ->
+// post pass, the reductions of the reference's FFT-reduction IR (r2r_ir.rs:1282-1500):
+//   DCT-I   L = 2(N-1) even extension, forward      X_k = Re Y_k
+//   DST-I   L = 2(N+1) odd extension, forward       X_k = -Im Y_{k+1}
+//   DCT-II  L = N  even/odd reorder, forward         X_k = 2 Re(Y_k e^{-i pi k/2N})
+//   DCT-III L = N  half-shifted spectrum, inverse     unreorder Re
+//   DST-II/III: the same with alternating signs and reversed index
+//   IV, N even: L = N/2 packed pairs with pre/post twiddles, inverse
+//   IV, N odd:  L = 2N  pre-twiddled zero-extended, forward
+// The tensor is [outer][N][inner]; the complex work array is [outer][L][inner], so a
+// thread index with `inner` fastest reads and writes coalesced lines for every axis.
+// kind: 0..3 DCT-I..IV, 4..7 DST-I..IV (the effective transform: II and III swap
+// for the inverse direction).
+struct R2rPass {
+    const void *src;
+    void *dst;
+    int64_t outer;  // batch x product of the slower dims
+    int64_t inner;  // product of the faster dims
+    int64_t n;      // logical length of the axis
+    int64_t L;      // FFT length
+    int64_t total;  // threads: outer * L * inner (pre) or outer * n * inner (post)
+    int32_t kind;
+    int32_t pre;    // 1: real tensor -> complex work array, 0: spectrum -> real tensor
+    double scale;
+};
+
 // Boundary copy between a caller's buffer and a dense scratch tensor, with the
 // zero-padding interval applied (zero_pad_ir.rs: elements whose coordinate on any padded
 // axis lies in [pad_lo, pad_hi) become zero) and formatted buffer strides

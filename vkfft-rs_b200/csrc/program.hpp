@@ -39,7 +39,7 @@ struct HostTable {
     }
 };
 
-enum KernelKind : int { KERNEL_PASS = 0, KERNEL_REG = 1, KERNEL_COPY = 2, KERNEL_CMUL = 3 };
+enum KernelKind : int { KERNEL_PASS = 0, KERNEL_REG = 1, KERNEL_COPY = 2, KERNEL_CMUL = 3, KERNEL_R2R = 4 };
 
 struct PassPlan {
     int kernel = KERNEL_PASS;     // KERNEL_REG: register-resident Stockham (reg_kernels.cu)
@@ -53,6 +53,7 @@ struct PassPlan {
     PassParams p{};               // device pointers are patched at upload / launch
     BoundaryCopy bc{};            // KERNEL_COPY parameters (pointers patched at launch)
     ConvMultiply cm{};            // KERNEL_CMUL parameters; reg_table holds the kernel spectrum
+    R2rPass rr{};                 // KERNEL_R2R parameters
     int op_tables[kMaxOps][3];    // table ids per op (lut, lut2, lut3) or -1
     int src_buf = BUF_IN, dst_buf = BUF_OUT;
     int64_t src_off = 0, dst_off = 0;  // element offsets (units of the side's element type)

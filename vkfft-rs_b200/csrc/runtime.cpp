@@ -18,6 +18,7 @@ void set_reg_kernel_smem_limits();
 cudaError_t launch_reg(int variant, const RegParams &rp, cudaStream_t stream);
 cudaError_t launch_boundary_copy(const BoundaryCopy &b, cudaStream_t stream);
 cudaError_t launch_conv_multiply(const ConvMultiply &m, bool dbl, cudaStream_t stream);
+cudaError_t launch_r2r(const R2rPass &r, bool dbl, cudaStream_t stream);
 
 // ---- host-side fault injection (no GPU fault is ever provoked) ------------------
 // B200FFT_FAULT=alloc:<n> or launch:<n> makes the n-th device allocation or kernel
@@ -231,6 +232,13 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
     const int variant = kernel_variant_for(prog.is_double);
     for (size_t pi = 0; pi < prog.passes.size(); pi++) {
         const PassPlan &pp = prog.passes[pi];
+        if (pp.kernel == KERNEL_R2R) {
+            R2rPass rr = pp.rr;
+            rr.src = bufs[pp.src_buf];
+            rr.dst = bufs[pp.dst_buf];
+            check(launch_r2r(rr, prog.is_double, stream), "kernel launch");
+            continue;
+        }
         if (pp.kernel == KERNEL_CMUL) {
             ConvMultiply cm = pp.cm;
             cm.src = bufs[pp.src_buf];

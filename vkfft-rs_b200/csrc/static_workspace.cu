@@ -20,6 +20,7 @@ cudaError_t launch_pass(int variant, const PassParams &p, int64_t grid, int thre
 cudaError_t launch_reg(int variant, const RegParams &rp, cudaStream_t stream);
 cudaError_t launch_boundary_copy(const BoundaryCopy &b, cudaStream_t stream);
 cudaError_t launch_conv_multiply(const ConvMultiply &m, bool dbl, cudaStream_t stream);
+cudaError_t launch_r2r(const R2rPass &r, bool dbl, cudaStream_t stream);
 
 constexpr size_t kStaticWorkspaceBytes = size_t(16) << 20;  // B200FFT_STATIC_WORKSPACE_BYTES
 constexpr int kMaxStaticDevices = 64;
@@ -108,6 +109,13 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scr + prog.scratch_offset(k);
     const int variant = kernel_variant_for(prog.is_double);
     for (const PassPlan &pp : prog.passes) {
+        if (pp.kernel == KERNEL_R2R) {
+            R2rPass rr = pp.rr;
+            rr.src = bufs[pp.src_buf];
+            rr.dst = bufs[pp.dst_buf];
+            check(launch_r2r(rr, prog.is_double, stream), "kernel launch");
+            continue;
+        }
         if (pp.kernel == KERNEL_CMUL) {
             ConvMultiply cm = pp.cm;
             cm.src = bufs[pp.src_buf];

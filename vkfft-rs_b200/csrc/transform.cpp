@@ -39,10 +39,48 @@ static void check_executable(const FftConfig &c) {
     if (!(c.precision == Precision::F32 || c.precision == Precision::F64 ||
           c.precision == Precision::F16StorageF32Compute || c.precision == Precision::F64ComputeF32Storage))
         fail_precision("B200 engine", precision_name(c.precision));
-    if (!(c.transform == TransformKind::C2C || c.transform == TransformKind::R2C || c.transform == TransformKind::C2R))
-        fail_unsupported("B200 engine executes C2C, R2C and C2R transforms (R2R is outside the FFT hot path)");
-
 }
+
+static bool is_r2r(TransformKind k) {
+    return !(k == TransformKind::C2C || k == TransformKind::R2C || k == TransformKind::C2R);
+}
+
+// Effective R2R kind index (0..3 DCT-I..IV, 4..7 DST-I..IV) of a transform and direction:
+// inverse_partner (r2r_ir.rs) swaps II and III, the others are their own inverses.
+static int r2r_effective_kind(TransformKind k, bool inverse) {
+    int kind = 0;
+    switch (k) {
+        case TransformKind::Dct1: kind = 0; break;
+        case TransformKind::Dct2: kind = 1; break;
+        case TransformKind::Dct3: kind = 2; break;
+        case TransformKind::Dct4: kind = 3; break;
+        case TransformKind::Dst1: kind = 4; break;
+        case TransformKind::Dst2: kind = 5; break;
+        case TransformKind::Dst3: kind = 6; break;
+        default: kind = 7; break;
+    }
+    if (inverse && ((kind & 3) == 1 || (kind & 3) == 2)) kind ^= 3;
+    return kind;
+}
+
+// inverse_pair_scale (r2r_ir.rs): 1/(2(N-1)) for DCT-I, 1/(2(N+1)) for DST-I, 1/(2N) otherwise.
+static double r2r_inverse_pair_scale(TransformKind k, size_t n) {
+    if (k == TransformKind::Dct1) return 1.0 / (2.0 * (double)(n - 1));
+    if (k == TransformKind::Dst1) return 1.0 / (2.0 * (double)(n + 1));
+    return 1.0 / (2.0 * (double)n);
+}
+
+// r2r_fft_reduction_expected_len (r2r_ir.rs:355-385) and the FFT direction of each
+// reduction (r2r_ir.rs:705-716, 819, 916): III and even IV run the inverse FFT.
+static size_t r2r_fft_len(int kind, size_t n) {
+    switch (kind & 3) {
+        case 0: return kind == 0 ? checked_mul(n - 1, 2, "DCT-I FFT reduction length")
+                                 : checked_mul(n + 1, 2, "DST-I FFT reduction length");
+        case 3: return n % 2 == 0 ? n / 2 : checked_mul(n, 2, "odd DCT/DST-IV FFT reduction length");
+        default: return n;
+    }
+}
+static bool r2r_fft_inverse(int kind, size_t n) { return (kind & 3) == 2 || ((kind & 3) == 3 && n % 2 == 0); }
 
 static std::vector<int64_t> dense_strides(const std::vector<size_t> &dims) {
     std::vector<int64_t> st(dims.size(), 1);
@@ -61,6 +99,7 @@ static void add_boundaries(Transform &t) {
     const FftConfig &c = t.plan.config;
     Program &prog = t.prog;
     const bool r2c = c.transform == TransformKind::R2C, c2r = c.transform == TransformKind::C2R;
+    const bool r2r = is_r2r(c.transform);
     const bool inverse = t.direction == B200FFT_INVERSE;
     std::vector<size_t> compact = c.dimensions;
     compact.back() = compact.back() / 2 + 1;
@@ -70,7 +109,9 @@ static void add_boundaries(Transform &t) {
     for (auto &z : c.zero_padding) any_pad |= z.has_value();
     bool pad_in = false, pad_out = false;
     if (any_pad) {
-        if (r2c || c2r)
+        if (r2r)  // spatial masking of the forward input / inverse output (r2r_ir.rs:1241-1277)
+            (inverse ? pad_out : pad_in) = true;
+        else if (r2c || c2r)
             (r2c ? pad_in : pad_out) = true;
         else
             ((c.zero_padding_domain == ZeroPaddingDomain::Spatial) != inverse ? pad_in : pad_out) = true;
@@ -124,7 +165,7 @@ static void add_boundaries(Transform &t) {
         return std::make_pair(pp, fbatch * batch);
     };
     if (pad_in || fmt_in || mixed) {
-        const size_t eb = r2c ? esz / 2 : esz;
+        const size_t eb = (r2c || r2r) ? esz / 2 : esz;
         for (PassPlan &pp : prog.passes)
             if (pp.src_buf == BUF_IN) pp.src_buf = BUF_SCRATCH4;
         auto [pp, physical] = copy(in_dims, true, pad_in, eb, BUF_IN, BUF_SCRATCH4);
@@ -133,7 +174,7 @@ static void add_boundaries(Transform &t) {
         prog.input_elems = physical;
     }
     if (pad_out || fmt_out || mixed) {
-        const size_t eb = c2r ? esz / 2 : esz;
+        const size_t eb = (c2r || r2r) ? esz / 2 : esz;
         for (PassPlan &pp : prog.passes) {
             if (pp.src_buf == BUF_OUT) pp.src_buf = BUF_SCRATCH5;
             if (pp.dst_buf == BUF_OUT) pp.dst_buf = BUF_SCRATCH5;
@@ -222,6 +263,78 @@ static std::unique_ptr<Transform> build_transform_core(const FftConfig &config_i
             job.in_os = job.out_os = (int64_t)(len * inner);
             job.tuning = c.tuning;
             lower_c2c_axis(prog, job);
+            first = false;
+        }
+        return t;
+    }
+
+    if (is_r2r(c.transform)) {
+        // DCT / DST (application.rs:134-165): R2rIr for rank 1, NdR2rIr (r2r_ir.rs:1795-2017)
+        // otherwise, one FFT reduction per non-omitted axis from the last to the first.
+        // Each axis runs pre pass (tensor -> complex work array [outer][L][inner]),
+        // the internal FFT as a strided (or, for the last axis, contiguous) axis of the
+        // work array, and post pass (work array -> tensor); the first axis reads the
+        // input, every post pass writes the output.
+        const size_t tensor = product(c.dimensions, 0, rank);
+        prog.input_elems = prog.output_elems = checked_mul(tensor, batch, "DCT/DST element count");
+        prog.input_real = prog.output_real = true;
+        t->family = rank == 1 ? B200FFT_FAMILY_REAL_TO_REAL : B200FFT_FAMILY_REAL_TO_REAL_ND;
+        bool first = true;
+        for (size_t a = rank; a-- > 0;) {
+            if (c.axis_is_omitted(a)) continue;
+            const size_t n = c.dimensions[a];
+            if (c.transform == TransformKind::Dct1 && n < 2)
+                throw FftError(B200FFT_INVALID_TRANSFORM_LENGTH,
+                               "axis " + std::to_string(a) + " length " + std::to_string(n) + " is invalid for DCT-I");
+            const size_t inner = product(c.dimensions, a + 1, rank);
+            const size_t outer = checked_mul(batch, product(c.dimensions, 0, a), "DCT/DST axis batch count");
+            const int kind = r2r_effective_kind(c.transform, inverse);
+            const size_t L = r2r_fft_len(kind, n);
+            const double scale = (inverse && c.normalize_inverse) ? r2r_inverse_pair_scale(c.transform, n) : 1.0;
+            FftConfig ac = FftConfig::make({L});
+            ac.batch_count = checked_mul(outer, inner, "DCT/DST internal FFT batch count");
+            ac.precision = c.precision == Precision::F16StorageF32Compute ? Precision::F32
+                           : c.precision == Precision::F64ComputeF32Storage ? Precision::F64
+                                                                            : c.precision;
+            ac.normalize_inverse = false;
+            ac.bandwidth_boost = c.bandwidth_boost;
+            ac.with_tuning(c.tuning);
+            if (auto gb = c.grouped_batch_for_axis(a)) ac.grouped_batch[0] = gb;
+            t->children[a] = FftPlan::build_c2c_child_for_device(ac, device,
+                                                                 inner == 1 ? AxisClass::Contiguous : AxisClass::Strided);
+            const size_t work = checked_mul(checked_mul(outer, L, "DCT/DST work array"), inner, "DCT/DST work array");
+            prog.scratch_elems[1] = std::max(prog.scratch_elems[1], work);
+            auto r2r_pass = [&](bool pre) {
+                PassPlan pp{};
+                pp.kernel = KERNEL_R2R;
+                R2rPass &r = pp.rr;
+                r.outer = (int64_t)outer;
+                r.inner = (int64_t)inner;
+                r.n = (int64_t)n;
+                r.L = (int64_t)L;
+                r.total = (int64_t)(outer * (pre ? L : n) * inner);
+                r.kind = kind;
+                r.pre = pre ? 1 : 0;
+                r.scale = scale;
+                pp.src_buf = pre ? (first ? BUF_IN : BUF_OUT) : BUF_SCRATCH1;
+                pp.dst_buf = pre ? BUF_SCRATCH1 : BUF_OUT;
+                pp.label = pre ? "r2r pre-process" : "r2r post-process";
+                for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
+                prog.passes.push_back(pp);
+            };
+            r2r_pass(true);
+            AxisJob job;
+            job.N = L;
+            job.alg = &t->children[a]->axes[0].algorithm;
+            job.no = (int64_t)outer;
+            job.S = (int64_t)inner;
+            job.inverse = r2r_fft_inverse(kind, n);
+            job.scale = 1.0;
+            job.in_buf = job.out_buf = BUF_SCRATCH1;
+            job.in_os = job.out_os = (int64_t)(L * inner);
+            job.tuning = c.tuning;
+            lower_c2c_axis(prog, job);
+            r2r_pass(false);
             first = false;
         }
         return t;

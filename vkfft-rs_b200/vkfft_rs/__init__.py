@@ -137,6 +137,8 @@ class Family(enum.IntEnum):
     COMPLEX_ND = 1
     REAL = 2
     REAL_ND = 3
+    REAL_TO_REAL = 4
+    REAL_TO_REAL_ND = 5
 
 
 u64 = ctypes.c_uint64
