@@ -1074,6 +1074,75 @@ static bool even_half_usable(const Program &prog, const RealAxisJob &job) {
 // FullComplex result is the real part of the Hermitian expansion, which ignores the
 // imaginary parts of X[0] and X[h]; for a FullComplex plan the kernel drops them, and the
 // even-half algebra then computes the same real inverse DFT.
+// DCT/DST reduction twiddles of a register pass, indexed by FFT position p < L:
+// [A | B] with A the pre-processing and B the post-processing factor of the type
+// (reg_kernels.cu r2r_load_all / r2r_store_all):
+//   II:  A[p] = W_4n^p                        (post)
+//   III: A[p] = conj W_4n^p                   (pre)
+//   IV, n even (L = n/2): A[p] = conj W_4n^2p (pre), B[p] = W_8n^(4p+1) (post)
+//   IV, n odd (L = 2n):   A[p] = W_4n^p (pre), B[p] = W_8n^(2p+1) (post), p < n
+static int table_r2r(Program &prog, int type, size_t n, size_t L) {
+    std::string key = "r2r" + std::to_string(type) + "_" + std::to_string(n) + "_" + std::to_string(L);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    HostTable t;
+    t.c.assign(2 * L, std::complex<double>(0.0, 0.0));
+    for (size_t p = 0; p < L; p++) {
+        if (type == 1) {
+            t.c[p] = root(p, 4 * n);
+        } else if (type == 2) {
+            t.c[p] = std::conj(root(p, 4 * n));
+        } else if (n % 2 == 0) {
+            t.c[p] = std::conj(root(2 * p, 4 * n));
+            t.c[L + p] = root(4 * p + 1, 8 * n);
+        } else if (p < n) {
+            t.c[p] = root(p, 4 * n);
+            t.c[L + p] = root(2 * p + 1, 8 * n);
+        }
+    }
+    return add_table(prog, key, std::move(t));
+}
+
+bool lower_r2r_axis_register(Program &prog, const R2rAxisJob &job) {
+    const size_t L = job.L;
+    if (!is_pow2(L) || !reg_kernels_enabled() || !job.alg || job.alg->kind != AlgorithmKind::Stockham) return false;
+    if (job.n > (size_t)INT32_MAX / 4) return false;
+    const bool strided = job.inner > 1;
+    const int rv = reg_variant_for(prog.is_double, L, REG_R2R, strided);
+    if (rv < 0) return false;
+    PassPlan pp{};
+    pp.kernel = KERNEL_REG;
+    pp.reg_variant = rv;
+    pp.reg_table = table_reg_twiddles(prog, L, rv);
+    pp.reg_table2 = (job.kind & 3) == 0 ? -1 : table_r2r(prog, job.kind & 3, job.n, L);
+    pp.rp.nlines = job.outer * job.inner;
+    pp.rp.ni = job.inner;
+    pp.rp.src = pp.rp.dst = RegSide{(int64_t)job.n * job.inner, strided ? 1 : 0, job.inner};
+    pp.rp.scale = job.scale;
+    pp.rp.conj = job.fft_inverse ? 1 : 0;
+    pp.rp.n = (int32_t)L;
+    pp.rp.r2r_kind = job.kind;
+    pp.rp.r2r_n = (int32_t)job.n;
+    pp.reg_in_real = pp.reg_out_real = true;
+    pp.src_buf = job.in_buf;
+    pp.dst_buf = job.out_buf;
+    pp.label = "register dct/dst";
+    // dense contiguous lines whose byte length is a multiple of 16: the persistent
+    // variant fetches each CTA's next line group with one bulk copy
+    const size_t line_bytes = job.n * (prog.is_double ? 8 : 4);
+    if (!strided && line_bytes % 16 == 0 && job.n <= 2 * L) {
+        const int pv = reg_variant_persistent_twin(rv);
+        if (pv >= 0) {
+            pp.reg_variant_plain = rv;
+            pp.reg_variant = pv;
+            pp.label = "register dct/dst (bulk prefetch)";
+        }
+    }
+    for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
+    prog.passes.push_back(pp);
+    return true;
+}
+
 static bool lower_real_axis_register(Program &prog, const RealAxisJob &job, bool r2c) {
     const size_t N = job.N, h = N / 2;
     if (N % 2 || !is_pow2(h) || !reg_kernels_enabled() || job.in_off || job.out_off) return false;

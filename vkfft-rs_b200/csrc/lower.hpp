@@ -37,6 +37,21 @@ struct RealAxisJob {
     int64_t in_off = 0, out_off = 0;
 };
 
+// DCT/DST of one axis of a real tensor [outer][n][inner] through its FFT reduction of
+// length L (effective kind 0..3 DCT-I..IV, 4..7 DST-I..IV; fft_inverse: the reduction's
+// FFT runs inverse).  Emits one register pass with the pre/post-processing fused into
+// its load and store when L is a power of two with a register variant; false otherwise.
+struct R2rAxisJob {
+    size_t n = 1, L = 1;
+    int kind = 0;
+    bool fft_inverse = false;
+    const AxisAlgorithm *alg = nullptr;  // algorithm of the internal FFT plan
+    int64_t outer = 1, inner = 1;
+    double scale = 1.0;
+    int in_buf = BUF_IN, out_buf = BUF_OUT;
+};
+bool lower_r2r_axis_register(Program &prog, const R2rAxisJob &job);
+
 std::vector<int> radix_schedule(size_t L);
 int reg_variant_for(bool is_double, size_t n, int mode, bool strided);  // reg_kernels.cu (-1: none)
 int reg_variant_radices(int v, int *out);

@@ -57,6 +57,151 @@ struct LineIO {
     bool valid;
 };
 
+// REG_R2R pre-processing (r2r_ir.rs:1282-1385): the values at the thread's FFT
+// positions p = t + m TT of the line's reduction, read from the real line through
+// `at(j)` (global memory, or the persistent variant's shared-memory copy).  Type I: even
+// / odd extension of length L = 2(n-1) / 2(n+1); II: even-odd reorder (odd sources
+// negated for DST); III: (a - i b) A[p] with a, b = x[p], x[n-p] (DST: x[n-1-p],
+// x[p-1]); IV with n even: (x[2p] -+ i x[n-1-2p]) A[p]; IV with n odd: x[p] A[p], zero
+// for p >= n.  tw2 = [A | B] indexed by FFT position (lower.cpp table_r2r).  The kind
+// is uniform, so the switch sits outside the unrolled point loops.
+template <typename T, int N, int E, typename At>
+__device__ __forceinline__ void r2r_load_all(const RegParams &rp, At at, int t, cplx<T> (&v)[E]) {
+    constexpr int TT = N / E;
+    const int n = rp.r2r_n;
+    const bool dst = rp.r2r_kind >= 4;
+    const cplx<T> *A = reinterpret_cast<const cplx<T> *>(rp.tw2);
+    switch (rp.r2r_kind & 3) {
+        case 0:
+#pragma unroll
+            for (int m = 0; m < E; m++) {
+                const int p = t + m * TT;
+                T x = T(0);
+                if (!dst)
+                    x = at(p < n ? p : N - p);
+                else if (p != 0 && p != n + 1)
+                    x = p <= n ? at(p - 1) : -at(N - p - 1);
+                v[m] = {x, T(0)};
+            }
+            break;
+        case 1: {
+            const int split = (n + 1) / 2;
+#pragma unroll
+            for (int m = 0; m < E; m++) {
+                const int p = t + m * TT;
+                const int s = p < split ? 2 * p : 2 * (n - p) - 1;
+                const T x = at(s);
+                v[m] = {(dst && (s & 1)) ? -x : x, T(0)};
+            }
+            break;
+        }
+        case 2:
+#pragma unroll
+            for (int m = 0; m < E; m++) {
+                const int p = t + m * TT;
+                const T a = dst ? at(n - 1 - p) : at(p);
+                const T b = p == 0 ? T(0) : (dst ? at(p - 1) : at(n - p));
+                v[m] = mul(cplx<T>{a, -b}, tw_load(A, p));
+            }
+            break;
+        default:
+            if ((n & 1) == 0) {
+#pragma unroll
+                for (int m = 0; m < E; m++) {
+                    const int p = t + m * TT;
+                    const T a = at(2 * p), b = at(n - 1 - 2 * p);
+                    v[m] = mul(cplx<T>{a, dst ? b : -b}, tw_load(A, p));
+                }
+            } else {
+#pragma unroll
+                for (int m = 0; m < E; m++) {
+                    const int p = t + m * TT;
+                    v[m] = {T(0), T(0)};
+                    if (p < n) {
+                        const cplx<T> w = tw_load(A, p);
+                        const T a = at(p);
+                        v[m] = {a * w.x, a * w.y};
+                    }
+                }
+            }
+            break;
+    }
+    if (rp.conj) {
+#pragma unroll
+        for (int m = 0; m < E; m++) v[m].y = -v[m].y;
+    }
+}
+
+// REG_R2R post-processing (r2r_ir.rs:1390-1500): the FFT outputs at the thread's
+// positions (v[m] at p = t + m TT) -> 0, 1 or 2 reals of the output line each.  With
+// z = B[p] = W_8n^(4p+1), IV with n even writes k0 = 2p from r0 = Y z* and k1 = n-1-2p
+// from conj(Y) W_8n^-(2 k1 + 1) = i conj(r0).
+template <typename T, int N, int E, bool UNIT>
+__device__ __forceinline__ void r2r_store_all(const RegParams &rp, T *out, int t, cplx<T> (&v)[E]) {
+    constexpr int TT = N / E;
+    const int64_t es = UNIT ? 1 : rp.dst.es;
+    const int n = rp.r2r_n;
+    const bool dst = rp.r2r_kind >= 4;
+    const T s = T(rp.scale);
+    const cplx<T> *A = reinterpret_cast<const cplx<T> *>(rp.tw2);
+    const cplx<T> *B = A + N;
+    if (rp.conj) {
+#pragma unroll
+        for (int m = 0; m < E; m++) v[m].y = -v[m].y;
+    }
+    auto put = [&](int k, T x) { __stcs(out + (int64_t)k * es, x * s); };
+    switch (rp.r2r_kind & 3) {
+        case 0:
+#pragma unroll
+            for (int m = 0; m < E; m++) {
+                const int p = t + m * TT;
+                if (!dst) {
+                    if (p < n) put(p, v[m].x);
+                } else if (p >= 1 && p <= n) {
+                    put(p - 1, -v[m].y);
+                }
+            }
+            break;
+        case 1:
+#pragma unroll
+            for (int m = 0; m < E; m++) {
+                const int p = t + m * TT;
+                const cplx<T> w = tw_load(A, p);
+                put(dst ? n - 1 - p : p, T(2) * (v[m].x * w.x - v[m].y * w.y));
+            }
+            break;
+        case 2:
+#pragma unroll
+            for (int m = 0; m < E; m++) {
+                const int p = t + m * TT;
+                const int k = 2 * p < n ? 2 * p : 2 * n - 2 * p - 1;
+                put(k, (dst && (k & 1)) ? -v[m].x : v[m].x);
+            }
+            break;
+        default:
+            if ((n & 1) == 0) {
+#pragma unroll
+                for (int m = 0; m < E; m++) {
+                    const int p = t + m * TT;
+                    const cplx<T> z = tw_load(B, p);
+                    const cplx<T> r0 = mul(v[m], cplx<T>{z.x, -z.y});
+                    put(2 * p, T(2) * (dst ? r0.y : r0.x));
+                    put(n - 1 - 2 * p, T(2) * (dst ? r0.x : r0.y));
+                }
+            } else {
+#pragma unroll
+                for (int m = 0; m < E; m++) {
+                    const int p = t + m * TT;
+                    if (p < n) {
+                        const cplx<T> r = mul(v[m], tw_load(B, p));
+                        put(p, T(2) * (dst ? -r.y : r.x));
+                    }
+                }
+            }
+            break;
+    }
+}
+
 // Store of one output point at line position p (last stage), per data mode.
 template <typename T, int N, int MODE>
 __device__ __forceinline__ void store_point(const RegParams &rp, const LineIO &io, int p, cplx<T> y) {
@@ -120,7 +265,7 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
             for (int q = 1; q < R; q++) x[q] = mul(x[q], w[q]);
         }
         dft<R, T>(x);
-        if (LAST && (MODE == REG_R2C_HALF || MODE == REG_CONV)) {
+        if (LAST && (MODE == REG_R2C_HALF || MODE == REG_CONV || MODE == REG_R2R)) {
             // output q of butterfly k sits at position t + (k + q NB) TT: back into v for
             // the post-processing epilogue
 #pragma unroll
@@ -173,7 +318,11 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
     cplx<T> *sline = reinterpret_cast<cplx<T> *>(smem_raw) + g * LS;
     const cplx<T> *tw = reinterpret_cast<const cplx<T> *>(rp.tw);
     cplx<T> v[E];
-    if (io.valid) {
+    if (MODE == REG_R2R && io.valid) {
+        const T *x = reinterpret_cast<const T *>(rp.in) + io.in_base;
+        const int64_t es = STRIDED ? rp.src.es : 1;
+        r2r_load_all<T, N, E>(rp, [&](int j) { return __ldcs(x + (int64_t)j * es); }, t, v);
+    } else if (MODE != REG_R2R && io.valid) {
 #pragma unroll
         for (int m = 0; m < E; m++) {
             const int p = t + m * TT;
@@ -236,6 +385,7 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
         return;
     }
     stages<T, N, E, MODE, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
+    if (MODE == REG_R2R && io.valid) r2r_store_all<T, N, E, !STRIDED>(rp, reinterpret_cast<T *>(rp.out) + io.out_base, t, v);
     // peer stores are visible system-wide before the rank's exchange signal
     if (MODE == REG_C2C_PEER) __threadfence_system();
     if (MODE == REG_R2C_HALF) {
@@ -264,8 +414,8 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
 }
 
 // ---- persistent variant: bulk-copy prefetch of the next line group -------------------
-// Dense contiguous C2C lines (line stride N, element stride 1): each CTA loops over
-// groups of G lines.  One thread fetches the group with cp.async.bulk into a shared
+// Dense contiguous lines (REG_C2C: N complex points; REG_R2R: the real line of rp.r2r_n
+// values, whose byte length is a multiple of 16): each CTA loops over groups of G lines.  One thread fetches the group with cp.async.bulk into a shared
 // buffer, tracked by an mbarrier; as soon as every thread has taken its points from the
 // buffer it fetches the CTA's next group, so the next load overlaps the radix stages and
 // the stores of the current one.  Waits are bounded: on expiry the kernel records error
@@ -295,11 +445,13 @@ __device__ __forceinline__ bool bar_wait(uint64_t *bar, unsigned parity) {
     return false;
 }
 
-template <typename T, int N, int E, int G, int MINB, int... Rs>
+template <typename T, int N, int E, int G, int MINB, int MODE, int... Rs>
 __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __grid_constant__ RegParams rp) {
     constexpr int TT = N / E;
     constexpr int LS = N + N / 16 + 1;
-    constexpr unsigned GROUP_BYTES = (unsigned)(G * N * sizeof(cplx<T>));
+    // bytes of one line in the input: N complex, or r2r_n reals (at most 2N of them)
+    const unsigned LINE_BYTES = MODE == REG_R2R ? (unsigned)(rp.r2r_n * sizeof(T)) : (unsigned)(N * sizeof(cplx<T>));
+    const unsigned GROUP_BYTES = G * LINE_BYTES;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem_raw);
     cplx<T> *buf = reinterpret_cast<cplx<T> *>(smem_raw + 128);
@@ -310,7 +462,10 @@ __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __g
     const int64_t ngroups = (rp.nlines + G - 1) / G;
     auto group_bytes = [&](int64_t grp) {
         const int64_t lines = rp.nlines - grp * G;
-        return lines >= G ? GROUP_BYTES : (unsigned)(lines * N * sizeof(cplx<T>));
+        return lines >= G ? GROUP_BYTES : (unsigned)(lines * LINE_BYTES);
+    };
+    auto group_src = [&](int64_t grp) {
+        return reinterpret_cast<const unsigned char *>(rp.in) + grp * (int64_t)GROUP_BYTES;
     };
     if (threadIdx.x == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)) : "memory");
@@ -320,7 +475,7 @@ __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __g
     int64_t grp = blockIdx.x;
     bool in_flight = false;
     if (threadIdx.x == 0 && grp < ngroups) {
-        bulk_fetch(buf, reinterpret_cast<const cplx<T> *>(rp.in) + grp * G * N, group_bytes(grp), bar);
+        bulk_fetch(buf, group_src(grp), group_bytes(grp), bar);
         in_flight = true;
     }
     unsigned parity = 0;
@@ -337,19 +492,25 @@ __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __g
         io.in_base = line * rp.src.os;
         io.out_base = line * rp.dst.os;
         cplx<T> v[E];
+        if (MODE == REG_R2R) {
+            const T *xs = reinterpret_cast<const T *>(buf) + g * rp.r2r_n;
+            r2r_load_all<T, N, E>(rp, [&](int j) { return xs[j]; }, t, v);
+        } else {
 #pragma unroll
-        for (int m = 0; m < E; m++) {
-            const cplx<T> w = buf[g * N + t + m * TT];
-            v[m] = {w.x, rp.conj ? -w.y : w.y};
+            for (int m = 0; m < E; m++) {
+                const cplx<T> w = buf[g * N + t + m * TT];
+                v[m] = {w.x, rp.conj ? -w.y : w.y};
+            }
         }
         __syncthreads();  // the group buffer is consumed
         const int64_t nxt = grp + gridDim.x;
         if (threadIdx.x == 0 && nxt < ngroups) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            bulk_fetch(buf, reinterpret_cast<const cplx<T> *>(rp.in) + nxt * G * N, group_bytes(nxt), bar);
+            bulk_fetch(buf, group_src(nxt), group_bytes(nxt), bar);
             in_flight = true;
         }
-        stages<T, N, E, REG_C2C, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
+        stages<T, N, E, MODE, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
+        if (MODE == REG_R2R && io.valid) r2r_store_all<T, N, E, true>(rp, reinterpret_cast<T *>(rp.out) + io.out_base, t, v);
     }
     // never leave with a bulk copy still writing this CTA's shared memory
     if (threadIdx.x == 0 && in_flight && !bar_wait(bar, parity)) atomicOr(rp.err, 64);
@@ -370,11 +531,15 @@ struct RegVariant {
 #define RV(T, MODE, STR, N, E, G, ...)                                                                      \
     {sizeof(T) == 8, N, MODE, STR, G *(N / E), G, (size_t)G *(N + N / 16 + 1) * sizeof(T) * 2,             \
      (const void *)regk::reg_fft_kernel<T, N, E, G, MODE, STR, __VA_ARGS__>, {__VA_ARGS__}, 0}
-// persistent contiguous C2C: barrier slot + one group buffer + the exchange buffer
-#define RVP(T, N, E, G, MINB, ...)                                                                          \
-    {sizeof(T) == 8, N, REG_C2C, 0, G *(N / E), G,                                                          \
+// persistent contiguous lines: barrier slot + one group buffer + the exchange buffer
+#define RVP(T, MODE, N, E, G, MINB, ...)                                                                    \
+    {sizeof(T) == 8, N, MODE, 0, G *(N / E), G,                                                             \
      128 + (size_t)G * N * sizeof(T) * 2 + (size_t)G *(N + N / 16 + 1) * sizeof(T) * 2,                     \
-     (const void *)regk::reg_fft_persistent<T, N, E, G, MINB, __VA_ARGS__>, {__VA_ARGS__}, 1}
+     (const void *)regk::reg_fft_persistent<T, N, E, G, MINB, MODE, __VA_ARGS__>, {__VA_ARGS__}, 1}
+#define RVP_ALL(T, MODE)                                                                                    \
+    RVP(T, MODE, 256, 16, 16, 3, 16, 16), RVP(T, MODE, 512, 16, 8, 3, 16, 16, 2),                           \
+        RVP(T, MODE, 1024, 16, 4, 3, 16, 16, 4), RVP(T, MODE, 2048, 16, 2, 3, 16, 16, 8),                   \
+        RVP(T, MODE, 4096, 16, 1, 3, 16, 16, 16)
 
 // contiguous lines, all modes
 #define RV_CONTIG(T, MODE)                                                                                  \
@@ -422,15 +587,21 @@ static const RegVariant kRegVariants[] = {
     RV_STRIDED(double, REG_C2C_PEER),
     RV_STRIDED(float, REG_CONV),
     RV_STRIDED(double, REG_CONV),
+    // DCT / DST reductions fused into the FFT of the axis
+    RV_CONTIG(float, REG_R2R),
+    RV_CONTIG(double, REG_R2R),
+    RV_STRIDED(float, REG_R2R),
+    RV_STRIDED(double, REG_R2R),
     // persistent twins of the contiguous C2C variants (bulk-copy prefetch)
     // (blocks per SM asked of the register allocator: the shared-memory limit)
-    RVP(float, 256, 16, 16, 3, 16, 16), RVP(float, 512, 16, 8, 3, 16, 16, 2), RVP(float, 1024, 16, 4, 3, 16, 16, 4),
-    RVP(float, 2048, 16, 2, 3, 16, 16, 8), RVP(float, 4096, 16, 1, 3, 16, 16, 16),
+    RVP_ALL(float, REG_C2C),
+    RVP_ALL(float, REG_R2R),
     // (f64 groups need twice the buffer and registers: one CTA per SM, slower than the
     // ordinary kernel's two, so f64 keeps the ordinary variants)
 };
 #undef RV_CONTIG
 #undef RV_STRIDED
+#undef RVP_ALL
 #undef RVP
 #undef RV
 
@@ -444,14 +615,16 @@ int reg_variant_for(bool is_double, size_t n, int mode, bool strided) {
     return -1;
 }
 
-// The persistent twin of a contiguous C2C variant (same precision, length, radices and
-// lines per CTA), or -1.
+// The persistent twin of a contiguous C2C or R2R variant (same mode, precision, length,
+// radices and lines per CTA), or -1.
 int reg_variant_persistent_twin(int v) {
     const RegVariant &a = kRegVariants[v];
-    if (a.mode != REG_C2C || a.strided || a.persistent) return -1;
+    if ((a.mode != REG_C2C && a.mode != REG_R2R) || a.strided || a.persistent) return -1;
     for (int i = 0; i < (int)(sizeof(kRegVariants) / sizeof(kRegVariants[0])); i++) {
         const RegVariant &b = kRegVariants[i];
-        if (b.persistent && b.is_double == a.is_double && b.n == a.n && b.g == a.g && b.smem <= 232448) return i;
+        if (b.persistent && b.mode == a.mode && b.is_double == a.is_double && b.n == a.n && b.g == a.g &&
+            b.smem <= 232448)
+            return i;
     }
     return -1;
 }

@@ -18,6 +18,9 @@ enum RegMode : int32_t {
                       // FFT_h -> 2h reals stored as h complex pairs
     REG_CONV = 6,     // strided lines: FFT, pointwise multiply by a spectrum table (tw2), inverse
                       // FFT (the fused outermost axis of the FFT convolution)
+    REG_R2R = 7,      // DCT/DST of one axis: the FFT reduction's pre-processing on load (reads the
+                      // real line), the FFT of length N = L, the post-processing on store (writes
+                      // the real line); tw2 holds the reduction's twiddles by FFT position
 };
 
 // Line l = o * ni + i; element p of the line is at o*os + i*is + p*es (units of the
@@ -41,6 +44,8 @@ struct RegParams {
     int32_t real_ends;   // REG_C2R_HALF: use only the real parts of X[0] and X[h] (the
                          // FullComplex C2R result: its real output ignores those imaginary parts)
     int32_t conv_flags;  // REG_CONV: F_CONJ_IN / F_NORMALIZE / F_CONJ_OUT of the multiply
+    int32_t r2r_kind;    // REG_R2R: effective kind 0..3 DCT-I..IV, 4..7 DST-I..IV
+    int32_t r2r_n;       // REG_R2R: logical length of the real line
     int64_t conv_em;     // REG_CONV: spectrum index = i + p * conv_em + o * conv_om
     int64_t conv_om;
     int *err;            // persistent variants: error word (a bulk copy that never completed)

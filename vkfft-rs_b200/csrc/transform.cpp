@@ -302,6 +302,23 @@ static std::unique_ptr<Transform> build_transform_core(const FftConfig &config_i
             if (auto gb = c.grouped_batch_for_axis(a)) ac.grouped_batch[0] = gb;
             t->children[a] = FftPlan::build_c2c_child_for_device(ac, device,
                                                                  inner == 1 ? AxisClass::Contiguous : AxisClass::Strided);
+            {
+                R2rAxisJob rj;
+                rj.n = n;
+                rj.L = L;
+                rj.kind = kind;
+                rj.fft_inverse = r2r_fft_inverse(kind, n);
+                rj.alg = &t->children[a]->axes[0].algorithm;
+                rj.outer = (int64_t)outer;
+                rj.inner = (int64_t)inner;
+                rj.scale = scale;
+                rj.in_buf = first ? BUF_IN : BUF_OUT;
+                rj.out_buf = BUF_OUT;
+                if (lower_r2r_axis_register(prog, rj)) {
+                    first = false;
+                    continue;
+                }
+            }
             const size_t work = checked_mul(checked_mul(outer, L, "DCT/DST work array"), inner, "DCT/DST work array");
             prog.scratch_elems[1] = std::max(prog.scratch_elems[1], work);
             auto r2r_pass = [&](bool pre) {
