@@ -41,6 +41,10 @@ def lib():
         l.oracle_fft_batch.argtypes = [dp, dp, sz, sz, ci, ci, ci]
         l.oracle_r2c_batch.argtypes = [dp, dp, sz, sz, ci]
         l.oracle_c2r_batch.argtypes = [dp, dp, sz, sz, ci, ci]
+        l.oracle_dd_dft_lines.argtypes = [dp, dp, sz, sz, ci, ci, ci]
+        l.oracle_dd_r2r_lines.argtypes = [dp, dp, sz, sz, ci, ci, ci, ci]
+        l.oracle_dd_dft_lines.restype = ci
+        l.oracle_dd_r2r_lines.restype = ci
         l.oracle_next_smooth_at_least.argtypes = [sz]
         l.oracle_next_smooth_at_least.restype = sz
         for f in (l.oracle_fft, l.oracle_dft, l.oracle_fft_axis, l.oracle_fft_batch,
@@ -278,3 +282,72 @@ def r2r_nd(x, kind, ndim, inverse=False, normalize=False, omitted=()):
             m = m * r2r_inverse_pair_scale(kind, n)
         x = np.moveaxis(np.tensordot(m, np.moveaxis(x, axis, 0), axes=(1, 0)), 0, axis)
     return x
+
+
+# ---- double-double ---------------------------------------------------------------------
+# Double-double arrays are float64 words: (..., 2) = (hi, lo) per real value and
+# (..., 4) = (re.hi, re.lo, im.hi, im.lo) per complex value, the crate's DD buffer layout
+# (double_double.rs encode_complex_double_double).  The transforms are direct binary128
+# DFTs / DCT-DST sums with Kahan summation, rounded to hi + lo (dd_oracle.c), the method
+# the crate's double-double golden vectors were generated with.
+
+def _dd_along(words, axis, ndim_words, fn):
+    """Apply fn(lines_array (lines, n, W)) along `axis` of a (..., n, ..., W) word array."""
+    x = np.moveaxis(np.asarray(words, dtype=np.float64), axis, -2)
+    shape = x.shape
+    lines = int(np.prod(shape[:-2])) if len(shape) > 2 else 1
+    y = fn(np.ascontiguousarray(x.reshape(lines, shape[-2], ndim_words)))
+    return np.moveaxis(y.reshape(shape[:-2] + y.shape[-2:]), -2, axis)
+
+
+def dd_fft_nd(words, ndim, inverse=False, normalize=False, threads=None):
+    """Complex double-double DFT over the last `ndim` tensor axes of words (..., 4)."""
+    x = np.asarray(words, dtype=np.float64)
+    t = threads or default_threads()
+    for a in range(ndim):
+        axis = x.ndim - 1 - ndim + a
+
+        def run(lines):
+            out = np.empty_like(lines)
+            rc = lib().oracle_dd_dft_lines(_dp(lines), _dp(out), lines.shape[1], lines.shape[0], int(inverse),
+                                           int(normalize), t)
+            assert rc == 0
+            return out
+        x = _dd_along(x, axis, 4, run)
+    return x
+
+
+def dd_r2c_nd(words, ndim, threads=None):
+    """R2C of real double-double words (..., 2): the first n/2+1 bins of the last axis of
+    the complex DFT of (x, 0)."""
+    r = np.asarray(words, dtype=np.float64)
+    c = np.zeros(r.shape[:-1] + (4,))
+    c[..., 0:2] = r
+    full = dd_fft_nd(c, ndim, threads=threads)
+    n = r.shape[-2]
+    return full[..., : n // 2 + 1, :]
+
+
+def dd_r2r_nd(words, kind, ndim, inverse=False, normalize=False, threads=None):
+    """DCT/DST of real double-double words (..., 2) over the last `ndim` axes."""
+    x = np.asarray(words, dtype=np.float64)
+    t = threads or default_threads()
+    k = R2R_KINDS.index(kind)
+    for a in range(ndim):
+        axis = x.ndim - 1 - ndim + a
+
+        def run(lines):
+            out = np.empty_like(lines)
+            rc = lib().oracle_dd_r2r_lines(_dp(lines), _dp(out), lines.shape[1], lines.shape[0], k, int(inverse),
+                                           int(normalize), t)
+            assert rc == 0
+            return out
+        x = _dd_along(x, axis, 2, run)
+    return x
+
+
+def dd_max_abs_diff(a, b):
+    """max |a - b| over double-double words (pairs (hi, lo) on the last axis, any width)."""
+    a = np.asarray(a, dtype=np.float64).reshape(-1, 2)
+    b = np.asarray(b, dtype=np.float64).reshape(-1, 2)
+    return float(np.max(np.abs((a[:, 0] - b[:, 0]) + (a[:, 1] - b[:, 1])))) if a.size else 0.0

@@ -48,23 +48,11 @@ static void emu_launch(const PassParams &p, int64_t grid, int threads, size_t sm
 }
 
 static void run_program(const Program &prog, const void *in, void *out, const PeerStore *peer = nullptr) {
-    const size_t esz = prog.is_double ? 16 : 8;
+    const size_t esz = (size_t)prog.cbytes();
     std::vector<std::vector<unsigned char>> tables;
     for (const HostTable &t : prog.tables) {
-        std::vector<unsigned char> v(t.bytes(prog.is_double));
-        if (t.is_raw) {
-            std::memcpy(v.data(), t.raw.data(), v.size());
-        } else if (t.is_int) {
-            std::memcpy(v.data(), t.i.data(), v.size());
-        } else if (prog.is_double) {
-            std::memcpy(v.data(), t.c.data(), v.size());
-        } else {
-            float *f = reinterpret_cast<float *>(v.data());
-            for (size_t m = 0; m < t.c.size(); m++) {
-                f[2 * m] = (float)t.c[m].real();
-                f[2 * m + 1] = (float)t.c[m].imag();
-            }
-        }
+        std::vector<unsigned char> v(t.bytes(prog.cbytes()));
+        pack_table(t, prog, v.data());
         tables.push_back(std::move(v));
     }
     std::vector<std::vector<unsigned char>> scratch(kScratchBuffers);
@@ -77,8 +65,11 @@ static void run_program(const Program &prog, const void *in, void *out, const Pe
             R2rPass rr = pp.rr;
             rr.src = bufs[pp.src_buf];
             rr.dst = bufs[pp.dst_buf];
+            rr.tb = pp.reg_table2 >= 0 ? tables[pp.reg_table2].data() : nullptr;
             for (int64_t t = 0; t < rr.total; t++) {
-                if (prog.is_double)
+                if (prog.is_dd)
+                    r2r_one<dd>(rr, t);
+                else if (prog.is_double)
                     r2r_one<double>(rr, t);
                 else
                     r2r_one<float>(rr, t);
@@ -91,7 +82,9 @@ static void run_program(const Program &prog, const void *in, void *out, const Pe
             cm.dst = bufs[pp.dst_buf];
             cm.ker = tables[pp.reg_table].data();
             for (int64_t L = 0; L < cm.total; L++) {
-                if (prog.is_double)
+                if (prog.is_dd)
+                    conv_multiply_one<dd>(cm, L);
+                else if (prog.is_double)
                     conv_multiply_one<double>(cm, L);
                 else
                     conv_multiply_one<float>(cm, L);
@@ -121,7 +114,9 @@ static void run_program(const Program &prog, const void *in, void *out, const Pe
             p.peer.sub = peer->chunk * pp.peer_es;
         }
         if (pp.threads > 1024 || pp.smem > 232448) fail_invalid_ir("pass launch exceeds sm_100 limits");
-        if (prog.is_double)
+        if (prog.is_dd)
+            emu_launch<dd>(p, pp.grid, pp.threads, pp.smem);
+        else if (prog.is_double)
             emu_launch<double>(p, pp.grid, pp.threads, pp.smem);
         else
             emu_launch<float>(p, pp.grid, pp.threads, pp.smem);
@@ -176,7 +171,7 @@ extern "C" int b200fft_emu_convolution_run(const b200fft_config *cfg, const b200
         d.supports_f64 = dev->supports_f64;
         auto c = build_convolution(FftConfig::from_c(*cfg), d, spectrum, copies);
         const Program &prog = c->prog;
-        const size_t csz = prog.is_double ? 16 : 8;
+        const size_t csz = (size_t)prog.cbytes();
         const size_t isz = prog.input_real ? csz / 2 : csz, osz = prog.output_real ? csz / 2 : csz;
         if (in_bytes != prog.input_elems * isz || out_bytes != prog.output_elems * osz)
             fail_input_length(prog.input_elems, in_bytes / isz);
@@ -211,7 +206,7 @@ extern "C" int b200fft_emu_slab_run(const b200fft_config *cfg, int direction, co
         std::vector<std::unique_ptr<Slab>> slabs;
         for (int r = 0; r < nranks; r++) slabs.push_back(build_slab(FftConfig::from_c(*cfg), direction, nranks, r, d));
         const Slab &s0 = *slabs[0];
-        const size_t esz = s0.pre.is_double ? 16 : 8;
+        const size_t esz = (size_t)s0.pre.cbytes();
         const size_t in_need = s0.input_elems * (s0.input_real ? esz / 2 : esz);
         const size_t out_need = s0.output_elems * (s0.output_real ? esz / 2 : esz);
         if (in_bytes_per_rank != in_need || out_bytes_per_rank != out_need) fail_input_length(in_need, in_bytes_per_rank);

@@ -33,6 +33,8 @@ def b200_profile(V):
 
 
 def run(case, V, lib):
+    if case["kind"] == "dd":
+        return run_dd(case, V, lib, b200_profile(V), np.random.default_rng(case.get("seed", 0)))
     dims, batch, prec = case["dims"], case["batch"], case["prec"]
     cdt, rdt = (np.complex64, np.float32) if prec == "F32" else (np.complex128, np.float64)
     dev = b200_profile(V)
@@ -204,6 +206,84 @@ def run_slab(case, V, lib, dev, cfg, rng, cdt, rdt):
     if st != 0:
         raise V.VkFftError(st, err.value.decode())
     return {"err": rel_l2(out, ref), "launches": launches.value}
+
+
+def dd_words(rng, shape, complex_):
+    """Random double-double words: hi uniform in [-1, 1], lo a canonical residual."""
+    w = 4 if complex_ else 2
+    x = np.zeros(tuple(shape) + (w,))
+    for k in range(0, w, 2):
+        hi = rng.uniform(-1, 1, shape)
+        x[..., k] = hi
+        x[..., k + 1] = hi * np.ldexp(rng.uniform(-1, 1, shape), -55)
+    return x
+
+
+def run_dd(case, V, lib, dev, rng):
+    """Double-double (kind "dd"): mode c2c | r2c | c2r (round trip through r2c) | r2r;
+    precision DOUBLE_DOUBLE (float64 words) or DOUBLE_DOUBLE_F64_STORAGE (f64 arrays).
+    err = max abs error / (2e-30 * N), the crate's GPU gate (must be <= 1); with f64
+    storage the outputs are compared to the oracle rounded to binary64 (relative L2)."""
+    dims, batch = case["dims"], case["batch"]
+    mode = case.get("mode", "c2c")
+    prec = case.get("precision", "DOUBLE_DOUBLE")
+    f64s = prec == "DOUBLE_DOUBLE_F64_STORAGE"
+    inverse, normalize = case.get("inverse", False), case.get("normalize", False)
+    cfg = (V.FftConfig(dims).with_batch_count(batch).with_precision(V.Precision[prec])
+           .with_inverse_normalization(normalize))
+    if case.get("tuning"):
+        cfg = cfg.with_tuning(V.PlannerTuning(**case["tuning"]))
+    shape = (batch,) + tuple(dims)
+    nd, N = len(dims), int(np.prod(dims))
+    half = tuple(dims[:-1]) + (dims[-1] // 2 + 1,)
+    d = V.Direction.INVERSE if inverse else V.Direction.FORWARD
+    launches = 0
+
+    def run(c, direction, x_words, out_words_shape, complex_in, complex_out):
+        nonlocal launches
+        if f64s:
+            x = x_words[..., 0::2] if complex_in else x_words[..., 0]
+            x = np.ascontiguousarray(x)
+            y, n = emulate(V, lib, c, direction, dev, x, int(np.prod(out_words_shape)) // 2, np.float64)
+            launches += n
+            w = np.zeros(out_words_shape)
+            w[..., 0::2] = y.reshape(out_words_shape[:-1] + (out_words_shape[-1] // 2,))
+            return w
+        y, n = emulate(V, lib, c, direction, dev, x_words, int(np.prod(out_words_shape)), np.float64)
+        launches += n
+        return y.reshape(out_words_shape)
+
+    def quantise(w):  # f64 storage: inputs are binary64
+        if f64s:
+            w = w.copy()
+            w[..., 1::2] = 0.0
+        return w
+
+    if mode == "c2c":
+        x = quantise(dd_words(rng, shape, True))
+        y = run(cfg, d, x, shape + (4,), True, True)
+        ref = oracle.dd_fft_nd(x, nd, inverse=inverse, normalize=normalize, threads=4)
+    elif mode == "r2c":
+        x = quantise(dd_words(rng, shape, False))
+        y = run(cfg.with_transform(V.TransformKind.R2C), V.Direction.FORWARD, x, (batch,) + half + (4,), False, True)
+        ref = oracle.dd_r2c_nd(x, nd, threads=4)
+    elif mode == "c2r":
+        x = quantise(dd_words(rng, shape, False))
+        spec = run(cfg.with_transform(V.TransformKind.R2C), V.Direction.FORWARD, x, (batch,) + half + (4,), False,
+                   True)
+        c = cfg.with_transform(V.TransformKind.C2R).with_inverse_normalization(True)
+        y = run(c, V.Direction.INVERSE, quantise(spec), shape + (2,), True, False)
+        ref = x
+    else:
+        x = quantise(dd_words(rng, shape, False))
+        c = cfg.with_transform(V.TransformKind[case["r2r"]])
+        y = run(c, d, x, shape + (2,), False, False)
+        ref = oracle.dd_r2r_nd(x, case["r2r"], nd, inverse=inverse, normalize=normalize, threads=4)
+    if f64s:
+        a = y[..., 0::2].ravel()
+        b = ref.reshape(-1, 2).sum(axis=1)
+        return {"err": rel_l2(a, b) / 1e-15, "launches": launches}
+    return {"err": oracle.dd_max_abs_diff(y, ref) / (2e-30 * N), "launches": launches}
 
 
 def _pad_keep(dims, pads):

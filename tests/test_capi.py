@@ -52,11 +52,21 @@ def test_baseline_programs_lower(V, cuda_profile):
     assert ir.output_is_real and ir.launch_count == 3
 
 
-def test_unsupported_precision_fails_closed(V, cuda_profile):
+def test_double_double_builds_and_convolution_fails_closed(V, cuda_profile):
+    """Double-double transforms build for every family (C2C, R2C, C2R, R2R; 1D and ND);
+    convolution stays rejected by FftConfig::validate as in the reference ("performConvolution
+    currently requires ordinary or mixed F16/F32/F64 storage")."""
+    for prec in (V.Precision.DOUBLE_DOUBLE, V.Precision.DOUBLE_DOUBLE_F64_STORAGE):
+        for kind, d in ((V.TransformKind.C2C, V.Direction.FORWARD), (V.TransformKind.R2C, V.Direction.FORWARD),
+                        (V.TransformKind.C2R, V.Direction.INVERSE), (V.TransformKind.DCT2, V.Direction.INVERSE)):
+            for dims in ([64], [12, 34]):
+                ir = V.TransformIr.build(V.FftConfig(dims).with_precision(prec).with_transform(kind), d, cuda_profile)
+                assert ir.launch_count >= 1
+    cfg = (V.FftConfig([32, 48]).with_transform(V.TransformKind.R2C).with_precision(V.Precision.DOUBLE_DOUBLE)
+           .with_convolution(True))
     with pytest.raises(V.VkFftError) as e:
-        V.TransformIr.build(V.FftConfig([64]).with_precision(V.Precision.DOUBLE_DOUBLE), V.Direction.FORWARD,
-                            cuda_profile)
-    assert e.value.variant == "UnsupportedPrecision"
+        V.NdRealConvolutionIr.build_from_spectrum(cfg, np.zeros(32 * 25, dtype=np.complex128), cuda_profile)
+    assert e.value.variant == "UnsupportedKernelPath" and "F16/F32/F64 storage" in str(e.value)
 
 
 def test_probe_without_gpu_reports_native_unavailable(V):

@@ -8,7 +8,7 @@ import emulator
 
 pytestmark = pytest.mark.skipif(not emulator.available(), reason="AddressSanitizer runtime not installed")
 
-TOL = {"F32": 2e-6, "F64": 1e-13}
+TOL = {"F32": 2e-6, "F64": 1e-13, "DD": 1.0}  # DD: error / (2e-30 N) or relL2 / 1e-15 (f64 storage)
 REC = dict(min_rader_direct_prime=17, max_rader_direct_prime=89, min_rader_fft_prime=17, max_rader_fft_prime=16384,
            allow_recursive_fft_rader=True)
 
@@ -115,6 +115,22 @@ CASES = [
     dict(kind="r2r", r2r="DST1", dims=[6, 20], batch=2, prec="F64", inverse=True, normalize=True),
     dict(kind="r2r", r2r="DCT3", dims=[32, 6], batch=1, prec="F32", pad={0: (20, 32)}),
     dict(kind="r2r", r2r="DST2", dims=[32], batch=2, prec="F64", inverse=True, pad={0: (5, 9)}),
+    # double-double (double_double.rs; reference tolerance: the crate's GPU gate)
+    dict(kind="dd", dims=[16], batch=3, prec="DD"),
+    dict(kind="dd", dims=[60], batch=2, prec="DD", inverse=True, normalize=True),
+    dict(kind="dd", dims=[103], batch=1, prec="DD", tuning=dict(max_rader_fft_prime=100)),
+    dict(kind="dd", dims=[257], batch=2, prec="DD"),
+    dict(kind="dd", dims=[1536], batch=1, prec="DD"),
+    dict(kind="dd", dims=[4096], batch=1, prec="DD", inverse=True),
+    dict(kind="dd", dims=[8, 12, 10], batch=1, prec="DD"),
+    dict(kind="dd", dims=[17, 34], batch=1, prec="DD", mode="r2c"),
+    dict(kind="dd", dims=[64, 64], batch=1, prec="DD", mode="c2r"),
+    dict(kind="dd", dims=[90], batch=2, prec="DD", mode="c2r"),
+    dict(kind="dd", dims=[17, 34], batch=1, prec="DD", mode="r2r", r2r="DCT2"),
+    dict(kind="dd", dims=[33], batch=2, prec="DD", mode="r2r", r2r="DST4", inverse=True, normalize=True),
+    dict(kind="dd", dims=[64], batch=2, prec="DD", mode="r2r", r2r="DCT3"),
+    dict(kind="dd", dims=[60], batch=2, prec="DD", precision="DOUBLE_DOUBLE_F64_STORAGE"),
+    dict(kind="dd", dims=[16, 20], batch=1, prec="DD", precision="DOUBLE_DOUBLE_F64_STORAGE", mode="r2c"),
     # mixed storage / compute precision (config.rs:107-161)
     dict(kind="mixed", dims=[64], batch=3, prec="F32", precision="F16_STORAGE_F32_COMPUTE"),
     dict(kind="mixed", dims=[60], batch=2, prec="F32", precision="F16_STORAGE_F32_COMPUTE", real=True),

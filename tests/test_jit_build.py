@@ -1,7 +1,7 @@
 """The run-time specialised pass kernels compile (NVRTC for sm_100a, no GPU needed) for
 every kind of generic pass the lowering emits: mixed-radix Stockham, direct / FFT /
 nested / pass-level Rader, fused and three-pass Bluestein, four-step, even-half real
-pre/post processing, Hermitian expansion, f32 and f64."""
+pre/post processing, Hermitian expansion, f32, f64 and double-double."""
 import pytest
 
 REC = dict(min_rader_direct_prime=17, max_rader_direct_prime=89, min_rader_fft_prime=17, max_rader_fft_prime=16384,
@@ -12,6 +12,9 @@ CASES = [
     ("c2c", [4099], 2, "F32", None), ("c2c", [65537], 1, "F32", None), ("c2c", [4106], 1, "F64", None),
     ("c2c", [107], 3, "F64", REC), ("c2c", [4099], 2, "F32", REC), ("r2c", [30], 3, "F64", None),
     ("c2r", [206], 2, "F64", None), ("c2r", [45], 2, "F64", None), ("c2c", [17 * 4096], 1, "F32", None),
+    ("c2c", [360], 2, "DOUBLE_DOUBLE", None), ("c2c", [103], 1, "DOUBLE_DOUBLE", None),
+    ("c2c", [257], 1, "DOUBLE_DOUBLE", None), ("r2c", [34], 2, "DOUBLE_DOUBLE", None),
+    ("c2c", [4096], 1, "DOUBLE_DOUBLE_F64_STORAGE", None),
 ]
 
 

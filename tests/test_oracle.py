@@ -137,3 +137,51 @@ def test_oracle_next_smooth_and_c2r_round_trip():
     r = rng.standard_normal((3, 30))
     back = oracle.c2r(oracle.r2c(r), 30, normalize=True)
     assert np.abs(back - r).max() < 1e-12
+
+
+DD_GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "quad_dd_golden.npz")
+
+
+def dd_case(z, set_name, name):
+    pre = f"{set_name}/{name}/"
+    return (tuple(int(v) for v in z[pre + "shape"]), int(z[pre + "kind"]), z[pre + "input"], z[pre + "output"])
+
+
+def dd_oracle_for(kind, shape, words):
+    """The double-double oracle applied as the fixture's kind prescribes (forward)."""
+    nd = len(shape)
+    if kind == 0:
+        return oracle.dd_fft_nd(words.reshape(shape + (4,)), nd)
+    if kind == 1:
+        return oracle.dd_r2c_nd(words.reshape(shape + (2,)), nd)
+    return oracle.dd_r2r_nd(words.reshape(shape + (2,)), "DCT2", nd)
+
+
+@pytest.mark.parametrize("name", sorted({k.split("/")[1] for k in np.load(DD_GOLDEN).files if k.startswith("dd/")}))
+def test_dd_oracle_matches_quad_goldens(name):
+    """The double-double oracle (dd_oracle.c) against the crate's binary128 fixtures at the
+    crate's CPU gate (tests/quad_medium_double_double_golden.rs:269: max abs <= 2e-31 * n)."""
+    z = np.load(DD_GOLDEN)
+    shape, kind, inp, out = dd_case(z, "dd", name)
+    got = dd_oracle_for(kind, shape, inp)
+    n = int(np.prod(shape))
+    assert oracle.dd_max_abs_diff(got, out) <= 2e-31 * n
+
+
+@pytest.mark.parametrize("name", sorted({k.split("/")[1] for k in np.load(DD_GOLDEN).files if k.startswith("dd_f64/")}))
+def test_dd_oracle_matches_f64_storage_goldens(name):
+    """DoubleDoubleF64Storage fixtures: binary64 inputs, outputs rounded to binary64."""
+    z = np.load(DD_GOLDEN)
+    shape, kind, inp, out = dd_case(z, "dd_f64", name)
+    if kind == 0:
+        words = np.zeros(inp.shape[:-1] + (4,))
+        words[..., 0], words[..., 2] = inp[..., 0], inp[..., 1]
+    else:
+        words = np.zeros(inp.shape + (2,))
+        words[..., 0] = inp
+    got = dd_oracle_for(kind, shape, words)
+    rounded = got.reshape(-1, 2).sum(axis=1)  # hi + lo rounded to binary64
+    # the crate's CPU gate (tests/quad_medium_dd_f64_storage_golden.rs:210-216); only the
+    # mathematically zero bins (quad residues near 1e-30) differ at all
+    n = int(np.prod(shape))
+    assert np.abs(rounded - out.reshape(-1)).max() <= 8e-13 * n

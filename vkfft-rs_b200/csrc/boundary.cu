@@ -21,10 +21,13 @@ __global__ void __launch_bounds__(256) conv_multiply_kernel(const __grid_constan
         conv_multiply_one<T>(m, L);
 }
 
-cudaError_t launch_conv_multiply(const ConvMultiply &m, bool dbl, cudaStream_t stream) {
+// kind: Program::scalar_kind (0 f32, 1 f64, 2 double-double)
+cudaError_t launch_conv_multiply(const ConvMultiply &m, int kind, cudaStream_t stream) {
     if (m.total <= 0) return cudaSuccess;
     const int64_t blocks = std::min<int64_t>((m.total + 255) / 256, 148 * 32);
-    if (dbl)
+    if (kind == 2)
+        conv_multiply_kernel<dd><<<(unsigned)blocks, 256, 0, stream>>>(m);
+    else if (kind == 1)
         conv_multiply_kernel<double><<<(unsigned)blocks, 256, 0, stream>>>(m);
     else
         conv_multiply_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(m);
@@ -37,10 +40,12 @@ __global__ void __launch_bounds__(256) r2r_kernel(const __grid_constant__ R2rPas
         r2r_one<T>(r, t);
 }
 
-cudaError_t launch_r2r(const R2rPass &r, bool dbl, cudaStream_t stream) {
+cudaError_t launch_r2r(const R2rPass &r, int kind, cudaStream_t stream) {
     if (r.total <= 0) return cudaSuccess;
     const int64_t blocks = std::min<int64_t>((r.total + 255) / 256, 148 * 32);
-    if (dbl)
+    if (kind == 2)
+        r2r_kernel<dd><<<(unsigned)blocks, 256, 0, stream>>>(r);
+    else if (kind == 1)
         r2r_kernel<double><<<(unsigned)blocks, 256, 0, stream>>>(r);
     else
         r2r_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(r);

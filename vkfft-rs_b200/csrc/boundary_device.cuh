@@ -49,19 +49,30 @@ B200FFT_HD void conv_multiply_one(const ConvMultiply &m, int64_t L) {
     reinterpret_cast<cplx<T> *>(m.dst)[L] = r;
 }
 
-B200FFT_HD double load_scalar(const void *base, int64_t idx, int bytes) {
-    if (bytes == 8) return reinterpret_cast<const double *>(base)[idx];
-    if (bytes == 4) return reinterpret_cast<const float *>(base)[idx];
-    return (double)__half2float(reinterpret_cast<const __half *>(base)[idx]);
+// One stored scalar as a double-double value (lo = 0 unless the storage is
+// double-double, 16 bytes: hi then lo) and its store, rounded to the storage type.
+B200FFT_HD dd load_scalar(const void *base, int64_t idx, int bytes) {
+    if (bytes == 16) {
+        const double *q = reinterpret_cast<const double *>(base) + 2 * idx;
+        return dd(q[0], q[1]);
+    }
+    if (bytes == 8) return dd(reinterpret_cast<const double *>(base)[idx]);
+    if (bytes == 4) return dd((double)reinterpret_cast<const float *>(base)[idx]);
+    return dd((double)__half2float(reinterpret_cast<const __half *>(base)[idx]));
 }
 
-B200FFT_HD void store_scalar(void *base, int64_t idx, int bytes, double v) {
-    if (bytes == 8)
-        reinterpret_cast<double *>(base)[idx] = v;
-    else if (bytes == 4)
-        reinterpret_cast<float *>(base)[idx] = (float)v;
-    else
-        reinterpret_cast<__half *>(base)[idx] = __float2half_rn((float)v);
+B200FFT_HD void store_scalar(void *base, int64_t idx, int bytes, dd v) {
+    if (bytes == 16) {
+        double *q = reinterpret_cast<double *>(base) + 2 * idx;
+        q[0] = v.hi;
+        q[1] = v.lo;
+    } else if (bytes == 8) {
+        reinterpret_cast<double *>(base)[idx] = v.hi + v.lo;
+    } else if (bytes == 4) {
+        reinterpret_cast<float *>(base)[idx] = (float)v.hi;
+    } else {
+        reinterpret_cast<__half *>(base)[idx] = __float2half_rn((float)v.hi);
+    }
 }
 
 // One element of a boundary copy (pass_desc.hpp BoundaryCopy).
@@ -92,28 +103,9 @@ B200FFT_HD void boundary_copy_one(const BoundaryCopy &b, int64_t L) {
         return;
     }
     for (int k = 0; k < b.scalars; k++) {  // storage <-> compute precision
-        const double v = zero ? 0.0 : load_scalar(b.src, so * b.scalars + k, b.src_bytes);
+        const dd v = zero ? dd(0.0) : load_scalar(b.src, so * b.scalars + k, b.src_bytes);
         store_scalar(b.dst, dof * b.scalars + k, b.dst_bytes, v);
     }
-}
-
-// e^{i pi num / den} for an integer ratio, the argument reduced to [0, 2) exactly first.
-template <typename T>
-B200FFT_HD cplx<T> r2r_phase(int64_t num, int64_t den) {
-    const int64_t period = 2 * den;
-    num %= period;
-    if (num < 0) num += period;
-#ifdef __CUDA_ARCH__
-    T s, c;
-    if constexpr (sizeof(T) == 8)
-        sincospi((double)num / (double)den, &s, &c);
-    else
-        sincospif((float)num / (float)den, &s, &c);
-    return cplx<T>{c, s};
-#else
-    const double a = 3.14159265358979323846 * (double)num / (double)den;
-    return cplx<T>{(T)std::cos(a), (T)std::sin(a)};
-#endif
 }
 
 template <typename T>
@@ -121,8 +113,14 @@ B200FFT_HD cplx<T> r2r_cmul(cplx<T> a, cplx<T> b) {
     return cplx<T>{a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x};
 }
 
+template <typename T>
+B200FFT_HD cplx<T> r2r_tab(const R2rPass &r, int64_t idx) {
+    return reinterpret_cast<const cplx<T> *>(r.tb)[idx];
+}
+
 // One element of an R2R pre pass (real tensor -> complex work array) or post pass
-// (FFT output -> real tensor).
+// (FFT output -> real tensor); the algebra of reg_kernels.cu r2r_load_all /
+// r2r_store_all, with the twiddles from the per-position table r.tb = [A | B].
 template <typename T>
 B200FFT_HD void r2r_one(const R2rPass &r, int64_t t) {
     const int64_t n = r.n, L = r.L, inner = r.inner;
@@ -147,12 +145,12 @@ B200FFT_HD void r2r_one(const R2rPass &r, int64_t t) {
         } else if (type == 2) {
             const T a = dst ? at(n - 1 - m) : at(m);
             const T b = m == 0 ? T(0) : (dst ? at(m - 1) : at(n - m));
-            v = r2r_cmul(cplx<T>{a, -b}, r2r_phase<T>(m, 2 * n));
+            v = r2r_cmul(cplx<T>{a, -b}, r2r_tab<T>(r, m));
         } else if ((n & 1) == 0) {
             const T a = at(2 * m), b = at(n - 1 - 2 * m);
-            v = r2r_cmul(cplx<T>{a, dst ? b : -b}, r2r_phase<T>(m, n));
+            v = r2r_cmul(cplx<T>{a, dst ? b : -b}, r2r_tab<T>(r, m));
         } else if (m < n) {
-            const cplx<T> w = r2r_phase<T>(-m, 2 * n);
+            const cplx<T> w = r2r_tab<T>(r, m);
             const T a = at(m);
             v = cplx<T>{a * w.x, a * w.y};
         }
@@ -166,20 +164,28 @@ B200FFT_HD void r2r_one(const R2rPass &r, int64_t t) {
             v = dst ? -at(k + 1).y : at(k).x;
         } else if (type == 1) {
             const int64_t q = dst ? n - 1 - k : k;
-            v = T(2) * r2r_cmul(at(q), r2r_phase<T>(-q, 2 * n)).x;
+            v = T(2) * r2r_cmul(at(q), r2r_tab<T>(r, q)).x;
         } else if (type == 2) {
             v = at((k & 1) == 0 ? k / 2 : n - 1 - k / 2).x;
             if (dst && (k & 1)) v = -v;
         } else if ((n & 1) == 0) {
-            cplx<T> y = (k & 1) == 0 ? at(k / 2) : at(L - (k + 1) / 2);
-            if (k & 1) y.y = -y.y;
-            const cplx<T> rot = r2r_cmul(y, r2r_phase<T>(2 * k + 1, 4 * n));
+            // k even: Y[k/2] conj(B[k/2]); k odd: conj(Y[p]) i B[p], p = L - (k+1)/2
+            cplx<T> rot;
+            if ((k & 1) == 0) {
+                const cplx<T> z = r2r_tab<T>(r, L + k / 2);
+                rot = r2r_cmul(at(k / 2), cplx<T>{z.x, -z.y});
+            } else {
+                const int64_t p = L - (k + 1) / 2;
+                const cplx<T> z = r2r_tab<T>(r, L + p);
+                const cplx<T> y = at(p);
+                rot = r2r_cmul(cplx<T>{y.x, -y.y}, cplx<T>{-z.y, z.x});
+            }
             v = T(2) * (dst ? rot.y : rot.x);
         } else {
-            const cplx<T> rot = r2r_cmul(at(k), r2r_phase<T>(-(2 * k + 1), 4 * n));
+            const cplx<T> rot = r2r_cmul(at(k), r2r_tab<T>(r, L + k));
             v = T(2) * (dst ? -rot.y : rot.x);
         }
-        reinterpret_cast<T *>(r.dst)[(o * n + k) * inner + i] = v * T(r.scale);
+        reinterpret_cast<T *>(r.dst)[(o * n + k) * inner + i] = v * kc<T>(r.scale, r.scale_lo);
     }
 }
 

@@ -10,17 +10,41 @@ Cooley-Tukey split R = R1 * R2 with literal twiddles; trivial twiddles
 (+-1, +-i, (+-1 +-i)/sqrt2) are emitted without multiplications.
 Inverse transforms are obtained by the caller through conjugation.
 
-Constants are computed with numpy longdouble and printed with 21 significant
-digits, so the double literals are correctly rounded.
+Constants are computed with Python decimal arithmetic at 60 digits and emitted as
+``kc<T>(hi, lo)``: hi is the correctly rounded double of the constant and lo the
+correctly rounded double of the remainder, both as exact hex-float literals.  f32 and
+f64 codelets use hi; the double-double type takes both words (its 106-bit constants).
 
 Usage: python gen_codelets.py  (writes dft_codelets.cuh beside this file)
 """
 import os
+from decimal import Decimal, getcontext
 
-import numpy as np
-
+getcontext().prec = 60
 HERE = os.path.dirname(os.path.abspath(__file__))
-PI = np.longdouble("3.14159265358979323846264338327950288")
+PI = Decimal("3.14159265358979323846264338327950288419716939937510582097494459")
+
+
+def _sin_cos(a):
+    """Taylor series of sin and cos at |a| <= 2 pi in 60-digit decimal arithmetic."""
+    s, c = Decimal(0), Decimal(0)
+    term = a
+    k = 1
+    while True:
+        s += term
+        term = -term * a * a / ((k + 1) * (k + 2))
+        k += 2
+        if abs(term) < Decimal(10) ** -58:
+            break
+    term = Decimal(1)
+    k = 0
+    while True:
+        c += term
+        term = -term * a * a / ((k + 1) * (k + 2))
+        k += 2
+        if abs(term) < Decimal(10) ** -58:
+            break
+    return s, c
 
 PRIMES = [2, 3, 5, 7, 11, 13]
 SPLITS = {4: (2, 2), 8: (2, 4), 9: (3, 3), 16: (4, 4), 6: (2, 3), 10: (2, 5), 12: (3, 4), 14: (2, 7),
@@ -29,13 +53,18 @@ RADICES = [2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 32]
 
 
 def lit(x):
-    s = np.format_float_scientific(np.longdouble(x), precision=20, unique=False)
-    return f"T({s})"
+    x = x.quantize(Decimal(10) ** -45)  # drop the series' last-digit noise (exact values stay exact)
+    hi = float(x)
+    lo = float(x - Decimal(hi))
+    return f"kc<T>({hi.hex()}, {lo.hex()})"
 
 
 def cs(m, r):
-    a = 2 * PI * np.longdouble(m % r) / np.longdouble(r)
-    return np.cos(a), np.sin(a)
+    a = 2 * PI * Decimal(m % r) / Decimal(r)
+    if a > PI:
+        a -= 2 * PI
+    s, c = _sin_cos(a)
+    return c, s
 
 
 def emit_prime(r):
@@ -80,7 +109,7 @@ def twiddle_stmt(dst, m, r):
     # reduce to eighths when exact
     if (8 * m) % r == 0:
         e = (8 * m) // r  # angle = -e*pi/4
-        sq = lit(np.sqrt(np.longdouble(0.5)))
+        sq = lit(Decimal(2).sqrt() / 2)
         if e == 2:  # -i
             return [f"{{ const T q = {dst}.x; {dst}.x = {dst}.y; {dst}.y = -q; }}"]
         if e == 4:  # -1
@@ -140,6 +169,13 @@ def main():
         "#endif",
         "",
         "template <typename T> struct alignas(2 * sizeof(T)) cplx { T x, y; };",
+        "",
+        "// A constant of the butterflies: hi + lo with hi the nearest double (the value the",
+        "// f32 / f64 codelets use) and lo the residual (used by the double-double type).",
+        "template <typename T> struct KConst {",
+        "    static B200FFT_HD T make(double hi, double) { return T(hi); }",
+        "};",
+        "template <typename T> B200FFT_HD T kc(double hi, double lo) { return KConst<T>::make(hi, lo); }",
         "",
     ]
     done = set()

@@ -50,13 +50,13 @@ bool stage_radix_supported(int r) { return (r >= 2 && r <= 13) || r == 16; }
 
 // CUDA C++ source of the specialised kernel of one pass, or "" when a pass uses
 // something the generator does not specialise.
-std::string jit_pass_source(const PassPlan &pp, bool dbl) {
+std::string jit_pass_source(const PassPlan &pp, int scalar_kind) {
     const PassParams &p = pp.p;
     std::ostringstream o;
     o << "#include \"pass_device.cuh\"\nusing namespace b200fft;\n"
       << "extern \"C\" __global__ void __launch_bounds__(" << pp.threads
       << ") b200fft_pass(const __grid_constant__ PassParams p) {\n"
-      << "  typedef " << (dbl ? "double" : "float") << " T;\n"
+      << "  typedef " << (scalar_kind == 2 ? "b200fft::dd" : scalar_kind == 1 ? "double" : "float") << " T;\n"
       << "  extern __shared__ __align__(16) unsigned char smem_raw[];\n"
       << "  cplx<T> *sm = reinterpret_cast<cplx<T> *>(smem_raw);\n"
       << "  PassShape sh = p;\n"
@@ -81,8 +81,10 @@ std::string jit_pass_source(const PassPlan &pp, bool dbl) {
           << "; op.nfull = " << op.nfull << ";\n"
           << "    op.div_a = " << fastdiv_literal(op.div_a) << "; op.div_b = " << fastdiv_literal(op.div_b)
           << "; op.div_c = " << fastdiv_literal(op.div_c) << ";\n";
-        std::snprintf(num, sizeof num, "%.17g", op.scale);
-        o << "    op.scale = " << num << "; op.om = " << (int64_t)op.om << "LL; op.lut_off = " << (int64_t)op.lut_off
+        std::snprintf(num, sizeof num, "%a", op.scale);
+        o << "    op.scale = " << num << ";";
+        std::snprintf(num, sizeof num, "%a", op.scale_lo);
+        o << " op.scale_lo = " << num << "; op.om = " << (int64_t)op.om << "LL; op.lut_off = " << (int64_t)op.lut_off
           << "LL;\n    ";
         switch (op.type) {
             case OP_LOAD: o << "op_load<T>(sh, op, sm, lm);"; break;
@@ -180,7 +182,7 @@ int jit_compile_check(const Program &prog, std::string &log) {
     int n = 0;
     for (const PassPlan &pp : prog.passes) {
         if (pp.kernel != KERNEL_PASS) continue;
-        const std::string src = jit_pass_source(pp, prog.is_double);
+        const std::string src = jit_pass_source(pp, prog.scalar_kind());
         if (src.empty()) continue;
         nvrtcProgram np;
         if (nvrtcCreateProgram(&np, src.c_str(), "b200fft_pass.cu", kJitHeaderCount, kJitHeaderSources,
@@ -214,7 +216,7 @@ std::vector<const void *> jit_kernels_for(const Program &prog, int device) {
     std::vector<size_t> todo;
     for (size_t i = 0; i < prog.passes.size(); i++) {
         if (prog.passes[i].kernel != KERNEL_PASS) continue;
-        srcs[i] = jit_pass_source(prog.passes[i], prog.is_double);
+        srcs[i] = jit_pass_source(prog.passes[i], prog.scalar_kind());
         if (srcs[i].empty()) continue;
         std::lock_guard<std::mutex> g(g_mu);
         if (!g_cache[srcs[i]].done) todo.push_back(i);

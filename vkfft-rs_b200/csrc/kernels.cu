@@ -40,19 +40,20 @@ __global__ void __launch_bounds__(MAXT) fft_pass_kernel(const __grid_constant__ 
 // ---- host launch table ------------------------------------------------------
 
 struct KernelVariant {
-    int is_double;
     int maxt;
     const void *fn;
 };
 
-#define B200FFT_VARIANT(T, M) {sizeof(T) == 8, M, (const void *)fft_pass_kernel<T, M>}
+// one variant per compute type (Program::scalar_kind): f32, f64, double-double
+#define B200FFT_VARIANT(T, M) {M, (const void *)fft_pass_kernel<T, M>}
 static const KernelVariant kVariants[] = {
     B200FFT_VARIANT(float, 1024),
     B200FFT_VARIANT(double, 512),
+    B200FFT_VARIANT(dd, 256),
 };
 #undef B200FFT_VARIANT
 
-int kernel_variant_for(bool is_double) { return is_double ? 1 : 0; }
+int kernel_variant_for(int scalar_kind) { return scalar_kind; }
 int kernel_variant_max_threads(int v) { return kVariants[v].maxt; }
 
 // Opt every variant in to the full dynamic shared memory of an sm_100 CTA (227 KB).

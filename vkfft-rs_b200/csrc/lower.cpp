@@ -11,6 +11,8 @@
 #include <cstdlib>
 #include <cstring>
 
+#include <quadmath.h>
+
 #include "lower.hpp"
 
 namespace b200fft {
@@ -34,6 +36,65 @@ static std::complex<double> root(size_t m, size_t n) {
     return {(double)cosl(a), (double)sinl(a)};
 }
 
+// ---- double-double tables: computed in binary128 (libquadmath), each value split into
+// the nearest double (hi) and the nearest double of the remainder (lo) ---------------
+using q128 = __float128;
+struct QC {
+    q128 re, im;
+};
+
+static QC qmul(QC a, QC b) { return {a.re * b.re - a.im * b.im, a.re * b.im + a.im * b.re}; }
+
+static QC root_q(size_t m, size_t n) {
+    // exp(-2 pi i m / n), the ratio reduced exactly before the angle is formed
+    static const q128 pi = 4 * atanq((q128)1);
+    const q128 a = -2 * pi * (q128)(m % n) / (q128)n;
+    return {cosq(a), sinq(a)};
+}
+
+static void put_q(HostTable &t, size_t idx, QC v) {
+    if (t.c.size() <= idx) t.c.resize(idx + 1);
+    if (t.lo.size() <= idx) t.lo.resize(idx + 1);
+    const double hr = (double)v.re, hi_ = (double)v.im;
+    t.c[idx] = {hr, hi_};
+    t.lo[idx] = {(double)(v.re - (q128)hr), (double)(v.im - (q128)hi_)};
+}
+
+// Table entry idx = W_n^m (conjugated when `conj`), in the program's table precision.
+static void put_root(HostTable &t, const Program &prog, size_t idx, size_t m, size_t n, bool conj = false);
+
+// The host Stockham FFT of host_fft_inplace in binary128 (double-double spectra).
+static void host_fft_q(std::vector<QC> &x) {
+    const size_t n = x.size();
+    if (n <= 1) return;
+    auto f = prime_factorization(n);
+    std::vector<QC> w(n), y(n);
+    for (size_t m = 0; m < n; m++) w[m] = root_q(m, n);
+    size_t P = 1;
+    for (size_t r : f) {
+        const size_t nbl = n / r;
+        const size_t tstep = n / (P * r);
+        std::vector<QC> v(r), o(r);
+        for (size_t bb = 0; bb < nbl; bb++) {
+            const size_t j = bb % P;
+            for (size_t q = 0; q < r; q++) v[q] = qmul(x[bb + q * nbl], w[(j * q * tstep) % n]);
+            for (size_t k = 0; k < r; k++) {
+                QC acc{0, 0};
+                for (size_t q = 0; q < r; q++) {
+                    const QC u = qmul(v[q], w[((q * k) % r) * (n / r)]);
+                    acc.re += u.re;
+                    acc.im += u.im;
+                }
+                o[k] = acc;
+            }
+            const size_t e0 = (bb - j) * r + j;
+            for (size_t q = 0; q < r; q++) y[e0 + q * P] = o[q];
+        }
+        std::swap(x, y);
+        P *= r;
+    }
+}
+
 static int add_table(Program &prog, const std::string &key, HostTable t) {
     auto it = prog.table_cache.find(key);
     if (it != prog.table_cache.end()) return it->second;
@@ -49,8 +110,20 @@ int table_twiddle(Program &prog, size_t n) {
     if (it != prog.table_cache.end()) return it->second;
     HostTable t;
     t.c.resize(n);
-    for (size_t m = 0; m < n; m++) t.c[m] = root(m, n);
+    for (size_t m = 0; m < n; m++) put_root(t, prog, m, m, n);
     return add_table(prog, key, std::move(t));
+}
+
+static void put_root(HostTable &t, const Program &prog, size_t idx, size_t m, size_t n, bool conj) {
+    if (prog.is_dd) {
+        QC v = root_q(m, n);
+        if (conj) v.im = -v.im;
+        put_q(t, idx, v);
+        return;
+    }
+    if (t.c.size() <= idx) t.c.resize(idx + 1);
+    const std::complex<double> v = root(m, n);
+    t.c[idx] = conj ? std::conj(v) : v;
 }
 
 // Stage twiddles of a register-kernel variant: for every stage s > 0 (span P, radix R)
@@ -85,7 +158,7 @@ int table_stage_twiddles(Program &prog, size_t R, size_t P) {
     HostTable t;
     t.c.reserve((R - 1) * P);
     for (size_t q = 1; q < R; q++)
-        for (size_t j = 0; j < P; j++) t.c.push_back(root(j * q, P * R));
+        for (size_t j = 0; j < P; j++) put_root(t, prog, (q - 1) * P + j, j * q, P * R);
     return add_table(prog, key, std::move(t));
 }
 
@@ -98,7 +171,7 @@ int table_twiddle_transposed(Program &prog, size_t ncols, size_t nrows, size_t N
     HostTable t;
     t.c.reserve(ncols * nrows);
     for (size_t e = 0; e < nrows; e++)
-        for (size_t c = 0; c < ncols; c++) t.c.push_back(root((c * e) % N, N));
+        for (size_t c = 0; c < ncols; c++) put_root(t, prog, e * ncols + c, (c * e) % N, N);
     return add_table(prog, key, std::move(t));
 }
 
@@ -122,7 +195,12 @@ int table_bluestein_chirp(Program &prog, size_t n) {
     auto it = prog.table_cache.find(key);
     if (it != prog.table_cache.end()) return it->second;
     HostTable t;
-    t.c = reference_chirp(n);
+    if (prog.is_dd) {
+        // double-double: the chirp reduced exactly, W_2n^(i^2 mod 2n) (lut.rs:325-371)
+        for (size_t i = 0; i < n; i++) put_q(t, i, root_q((size_t)(((unsigned __int128)i * i) % (2 * n)), 2 * n));
+    } else {
+        t.c = reference_chirp(n);
+    }
     return add_table(prog, key, std::move(t));
 }
 
@@ -131,6 +209,19 @@ int table_bluestein_spectrum(Program &prog, size_t n, size_t m) {
     std::string key = "bspec" + std::to_string(n) + "_" + std::to_string(m);
     auto it = prog.table_cache.find(key);
     if (it != prog.table_cache.end()) return it->second;
+    if (prog.is_dd) {
+        std::vector<QC> b(m, QC{0, 0});
+        for (size_t i = 0; i < n; i++) {
+            QC ic = root_q((size_t)(((unsigned __int128)i * i) % (2 * n)), 2 * n);
+            ic.im = -ic.im;
+            b[i] = ic;
+            if (i != 0) b[m - i] = ic;
+        }
+        host_fft_q(b);
+        HostTable t;
+        for (size_t k = 0; k < m; k++) put_q(t, k, QC{b[k].re / (q128)m, b[k].im / (q128)m});
+        return add_table(prog, key, std::move(t));
+    }
     auto chirp = reference_chirp(n);
     std::vector<std::complex<double>> b(m, {0.0, 0.0});
     for (size_t i = 0; i < n; i++) {
@@ -212,6 +303,16 @@ static RaderTables table_rader(Program &prog, size_t p, size_t g, bool fft_mode)
     ti.is_int = true;
     ti.i = ginv;
     rt.ginv = add_table(prog, ki, std::move(ti));
+    if (prog.is_dd) {
+        std::vector<QC> b(p - 1);
+        for (size_t m = 0; m < p - 1; m++) b[m] = root_q((size_t)ginv[m], p);
+        if (fft_mode) host_fft_q(b);
+        const q128 s = fft_mode ? (q128)1 / (q128)(p - 1) : (q128)1;
+        HostTable tk;
+        for (size_t m = 0; m < p - 1; m++) put_q(tk, m, QC{b[m].re * s, b[m].im * s});
+        rt.kernel = add_table(prog, kk, std::move(tk));
+        return rt;
+    }
     std::vector<std::complex<double>> b(p - 1);
     for (size_t m = 0; m < p - 1; m++) b[m] = root((size_t)ginv[m], p);
     if (fft_mode) {
@@ -370,10 +471,10 @@ static size_t budget_bytes() { return 200 * 1024; }
 
 // Choose lines per CTA, threads and shared-memory layout.  Returns false when one
 // line does not fit on chip.
-static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bool strided, int64_t nlines,
+static bool shape_pass(int ce, int L, const std::vector<StageSpec> &stages, bool strided, int64_t nlines,
                        int nops, CtaShape &sh) {
     if (!stages_ok(stages)) return false;
-    const size_t esz = dbl ? 16 : 8;
+    const size_t esz = (size_t)ce;  // bytes of one complex element (8 f32, 16 f64, 32 dd)
     sh.ls = line_stride_for(L);
     auto data_for = [&](int G) {
         size_t data = (2 * (size_t)G * sh.ls + rader_extra((size_t)L, stages, (size_t)G, (size_t)sh.ls)) * esz;
@@ -384,7 +485,7 @@ static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bo
         meta = (meta + 15) & ~size_t(15);
         return data_for(G) + meta + (size_t)nops * sizeof(Op);
     };
-    const int gmin = strided ? (dbl ? 4 : 8) : 1;
+    const int gmin = strided ? (ce >= 16 ? 4 : 8) : 1;
     int G = std::max(gmin, (int)((2048 + L - 1) / L));
     if (!strided) G = std::min<int64_t>(G, std::max<int64_t>(nlines, 1));
     const size_t soft = 96 * 1024;
@@ -395,7 +496,7 @@ static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bo
     sh.extra = rader_extra((size_t)L, stages, (size_t)G, (size_t)sh.ls);
     sh.meta_off = data_for(G);
     sh.smem = bytes_for(G);
-    const int maxt = dbl ? 512 : 1024;
+    const int maxt = ce == 8 ? 1024 : (ce == 16 ? 512 : 256);  // the pass kernel variants
     int64_t work = (int64_t)G * L / 8;
     int t = (int)std::min<int64_t>(std::max<int64_t>(work, 64), maxt);
     sh.threads = (t + 31) / 32 * 32;
@@ -403,16 +504,16 @@ static bool shape_pass(bool dbl, int L, const std::vector<StageSpec> &stages, bo
 }
 
 // Shared-memory capacity only (for passes without an FFT network, e.g. real pre/post).
-static bool line_capacity_ok(bool dbl, size_t L) {
+static bool line_capacity_ok(int ce, size_t L) {
     if (L > (1u << 20)) return false;
     CtaShape sh;
-    return shape_pass(dbl, (int)L, {}, false, 1 << 20, 8, sh);
+    return shape_pass(ce, (int)L, {}, false, 1 << 20, 8, sh);
 }
 
-bool line_fits_on_chip(bool dbl, size_t L, const AxisAlgorithm *alg, bool strided) {
+bool line_fits_on_chip(int ce, size_t L, const AxisAlgorithm *alg, bool strided) {
     if (L > (1u << 20)) return false;
     CtaShape sh;
-    return shape_pass(dbl, (int)L, line_stages(L, alg), strided, 1 << 20, kMaxOps, sh);
+    return shape_pass(ce, (int)L, line_stages(L, alg), strided, 1 << 20, kMaxOps, sh);
 }
 
 // Builds the op program of one pass.
@@ -420,8 +521,8 @@ class PassBuilder {
    public:
     PassBuilder(Program &prog, int L, std::vector<StageSpec> stages, bool strided, int64_t nlines, int nops_hint)
         : prog_(prog), L_(L), stages_(std::move(stages)) {
-        if (!shape_pass(prog.is_double, L, stages_, strided, nlines, std::max(nops_hint, (int)kMaxOps), sh_))
-            fail_resource("B200 FFT pass shared memory", (size_t)L * (prog.is_double ? 32 : 16), budget_bytes());
+        if (!shape_pass(prog.cbytes(), L, stages_, strided, nlines, std::max(nops_hint, (int)kMaxOps), sh_))
+            fail_resource("B200 FFT pass shared memory", (size_t)L * 2 * prog.cbytes(), budget_bytes());
         A_ = 0;
         B_ = sh_.G * sh_.ls;
         extra_base_ = 2 * sh_.G * sh_.ls;
@@ -738,7 +839,7 @@ static AxisAlgorithm restrict_algorithm(const AxisAlgorithm &alg, size_t n) {
 
 // Four-step split N = N1 (columns, strided) x N2 (rows) with both factors executable in
 // one CTA; the most balanced such split.
-static bool four_step_split(bool dbl, size_t N, const AxisAlgorithm &alg, size_t &N1, size_t &N2) {
+static bool four_step_split(int ce, size_t N, const AxisAlgorithm &alg, size_t &N1, size_t &N2) {
     size_t best = 0;
     double best_score = 1e300;
     for (size_t d = 2; d * d <= N; d++) {
@@ -746,7 +847,7 @@ static bool four_step_split(bool dbl, size_t N, const AxisAlgorithm &alg, size_t
         for (int flip = 0; flip < 2; flip++) {
             const size_t a = flip ? N / d : d, b = N / a;
             AxisAlgorithm ra = restrict_algorithm(alg, a), rb = restrict_algorithm(alg, b);
-            if (!line_fits_on_chip(dbl, a, &ra, true) || !line_fits_on_chip(dbl, b, &rb, true)) continue;
+            if (!line_fits_on_chip(ce, a, &ra, true) || !line_fits_on_chip(ce, b, &rb, true)) continue;
             const double score = std::fabs(std::log((double)a) - std::log((double)b)) + (flip ? 1e-9 : 0);
             if (score < best_score) {
                 best_score = score;
@@ -778,6 +879,13 @@ static bool reg_kernels_enabled() {
 #endif
 }
 
+// Register-kernel variant for the program's precision (none for double-double: its
+// 32-byte points do not fit the register budget of the register-resident kernels).
+static int reg_variant(const Program &prog, size_t n, int mode, bool strided) {
+    if (prog.is_dd) return -1;
+    return reg_variant_for(prog.is_double, n, mode, strided);
+}
+
 void lower_c2c_axis(Program &prog, const AxisJob &job) {
     const PlannerTuning *saved_tuning = g_tuning;
     g_tuning = &job.tuning;
@@ -786,6 +894,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         ~Restore() { g_tuning = t; }
     } restore{saved_tuning};
     const bool dbl = prog.is_double;
+    const int ce = prog.cbytes();
     const bool inv = job.inverse;
     const size_t N = job.N;
     const AxisAlgorithm *alg = job.alg;
@@ -821,7 +930,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
             mode = REG_R2C_FULL;
         else if (job.in_herm && job.out_real && out_count == N && !strided)
             mode = REG_C2R_FULL;
-        const int rv = mode >= 0 ? reg_variant_for(dbl, N, mode, strided) : -1;
+        const int rv = mode >= 0 ? reg_variant(prog, N, mode, strided) : -1;
         if (rv >= 0) {
             PassPlan pp{};
             pp.kernel = KERNEL_REG;
@@ -863,7 +972,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     if (alg->kind != AlgorithmKind::Bluestein) {
         // one pass: Stockham radices and Rader stages (nested when the convolution is
         // itself Rader) on chip
-        if (line_fits_on_chip(dbl, N, alg, strided)) {
+        if (line_fits_on_chip(ce, N, alg, strided)) {
             PassBuilder b(prog, (int)N, line_stages(N, alg), strided, no * S, kMaxOps);
             b.load((int)N, cin);
             b.fft();
@@ -875,7 +984,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         // four-step through scratch 0: columns (N1, stride N2) with the twiddle W_N^{n2 k1}
         // fused into their store, then rows (N2) with the transposed store
         size_t N1, N2;
-        if (four_step_split(dbl, N, *alg, N1, N2)) {
+        if (four_step_split(ce, N, *alg, N1, N2)) {
             const AxisAlgorithm a1 = restrict_algorithm(*alg, N1), a2 = restrict_algorithm(*alg, N2);
             const int64_t scr_os = (int64_t)N * S;
             prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * N * S));
@@ -958,7 +1067,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     // chirp and take N.  With the conjugation trick the inverse uses the forward chirp.
     const size_t M = alg->convolution_len;
     const int chirp = table_bluestein_chirp(prog, N);
-    if (line_fits_on_chip(dbl, M, nullptr, strided)) {
+    if (line_fits_on_chip(ce, M, nullptr, strided)) {
         const int spec = table_bluestein_spectrum(prog, N, M);
         PassBuilder b(prog, (int)M, line_stages(M, nullptr), strided, no * S, kMaxOps);
         b.load((int)M, cin, MUL_LUT_N, chirp);
@@ -978,7 +1087,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     const size_t A = small_prime_part(N), B = N / A;
     if (dbl && A > 1 && B > 1) {
         const size_t MB = next_smooth_at_least(2 * B - 1, {2, 3, 5, 7});
-        if (line_fits_on_chip(dbl, MB, nullptr, true) && line_fits_on_chip(dbl, A, nullptr, true)) {
+        if (line_fits_on_chip(ce, MB, nullptr, true) && line_fits_on_chip(ce, A, nullptr, true)) {
             const int chirpB = table_bluestein_chirp(prog, B);
             const int specB = table_bluestein_spectrum(prog, B, MB);
             const int64_t scr_os = (int64_t)N * S;
@@ -1011,7 +1120,7 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     }
     size_t M1, M2;
     AxisAlgorithm smooth;
-    if (!four_step_split(dbl, M, smooth, M1, M2)) fail_unsupported("B200 engine: Bluestein length not decomposable");
+    if (!four_step_split(ce, M, smooth, M1, M2)) fail_unsupported("B200 engine: Bluestein length not decomposable");
     const int spec = table_bluestein_spectrum(prog, N, M);
     const int64_t scr_os = (int64_t)M * S;
     prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * M * S));
@@ -1081,23 +1190,24 @@ static bool even_half_usable(const Program &prog, const RealAxisJob &job) {
 //   III: A[p] = conj W_4n^p                   (pre)
 //   IV, n even (L = n/2): A[p] = conj W_4n^2p (pre), B[p] = W_8n^(4p+1) (post)
 //   IV, n odd (L = 2n):   A[p] = W_4n^p (pre), B[p] = W_8n^(2p+1) (post), p < n
-static int table_r2r(Program &prog, int type, size_t n, size_t L) {
+int table_r2r(Program &prog, int type, size_t n, size_t L) {
     std::string key = "r2r" + std::to_string(type) + "_" + std::to_string(n) + "_" + std::to_string(L);
     auto it = prog.table_cache.find(key);
     if (it != prog.table_cache.end()) return it->second;
     HostTable t;
     t.c.assign(2 * L, std::complex<double>(0.0, 0.0));
+    if (prog.is_dd) t.lo.assign(2 * L, std::complex<double>(0.0, 0.0));
     for (size_t p = 0; p < L; p++) {
         if (type == 1) {
-            t.c[p] = root(p, 4 * n);
+            put_root(t, prog, p, p, 4 * n);
         } else if (type == 2) {
-            t.c[p] = std::conj(root(p, 4 * n));
+            put_root(t, prog, p, p, 4 * n, true);
         } else if (n % 2 == 0) {
-            t.c[p] = std::conj(root(2 * p, 4 * n));
-            t.c[L + p] = root(4 * p + 1, 8 * n);
+            put_root(t, prog, p, 2 * p, 4 * n, true);
+            put_root(t, prog, L + p, 4 * p + 1, 8 * n);
         } else if (p < n) {
-            t.c[p] = root(p, 4 * n);
-            t.c[L + p] = root(2 * p + 1, 8 * n);
+            put_root(t, prog, p, p, 4 * n);
+            put_root(t, prog, L + p, 2 * p + 1, 8 * n);
         }
     }
     return add_table(prog, key, std::move(t));
@@ -1108,7 +1218,7 @@ bool lower_r2r_axis_register(Program &prog, const R2rAxisJob &job) {
     if (!is_pow2(L) || !reg_kernels_enabled() || !job.alg || job.alg->kind != AlgorithmKind::Stockham) return false;
     if (job.n > (size_t)INT32_MAX / 4) return false;
     const bool strided = job.inner > 1;
-    const int rv = reg_variant_for(prog.is_double, L, REG_R2R, strided);
+    const int rv = reg_variant(prog, L, REG_R2R, strided);
     if (rv < 0) return false;
     PassPlan pp{};
     pp.kernel = KERNEL_REG;
@@ -1129,7 +1239,7 @@ bool lower_r2r_axis_register(Program &prog, const R2rAxisJob &job) {
     pp.label = "register dct/dst";
     // dense contiguous lines whose byte length is a multiple of 16: the persistent
     // variant fetches each CTA's next line group with one bulk copy
-    const size_t line_bytes = job.n * (prog.is_double ? 8 : 4);
+    const size_t line_bytes = job.n * (size_t)prog.rbytes();
     if (!strided && line_bytes % 16 == 0 && job.n <= 2 * L) {
         const int pv = reg_variant_persistent_twin(rv);
         if (pv >= 0) {
@@ -1146,7 +1256,7 @@ bool lower_r2r_axis_register(Program &prog, const R2rAxisJob &job) {
 static bool lower_real_axis_register(Program &prog, const RealAxisJob &job, bool r2c) {
     const size_t N = job.N, h = N / 2;
     if (N % 2 || !is_pow2(h) || !reg_kernels_enabled() || job.in_off || job.out_off) return false;
-    const int rv = reg_variant_for(prog.is_double, h, r2c ? REG_R2C_HALF : REG_C2R_HALF, false);
+    const int rv = reg_variant(prog, h, r2c ? REG_R2C_HALF : REG_C2R_HALF, false);
     if (rv < 0) return false;
     PassPlan pp{};
     pp.kernel = KERNEL_REG;
@@ -1182,8 +1292,8 @@ void lower_r2c_axis(Program &prog, const RealAxisJob &job) {
     if (!job.full_complex && N % 2 == 0 && N >= 2 && even_half_usable(prog, job)) {
         const size_t h = N / 2;
         const int wn = table_twiddle(prog, N);
-        const bool fused = job.alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.is_double, h, job.alg, false) &&
-                           line_capacity_ok(prog.is_double, h + 1);
+        const bool fused = job.alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.cbytes(), h, job.alg, false) &&
+                           line_capacity_ok(prog.cbytes(), h + 1);
         if (fused) {
             PassBuilder b(prog, (int)h, line_stages(h, job.alg), false, job.lines, 24);
             b.load((int)h, 0);
@@ -1195,7 +1305,7 @@ void lower_r2c_axis(Program &prog, const RealAxisJob &job) {
                                            job.in_off, job.out_buf, job.out_off, "r2c even-half"));
             return;
         }
-        if (!line_capacity_ok(prog.is_double, h + 1))
+        if (!line_capacity_ok(prog.cbytes(), h + 1))
             fail_unsupported("B200 engine: real axis post-processing exceeds on-chip capacity");
         prog.scratch_elems[2] = std::max(prog.scratch_elems[2], (size_t)job.lines * h);
         AxisJob a;
@@ -1258,8 +1368,8 @@ void lower_c2r_axis(Program &prog, const RealAxisJob &job) {
     if (!job.full_complex && N % 2 == 0 && N >= 2 && even_half_usable(prog, job)) {
         const size_t h = N / 2;
         const int wn = table_twiddle(prog, N);
-        const bool fused = job.alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.is_double, h, job.alg, false) &&
-                           line_capacity_ok(prog.is_double, h + 1);
+        const bool fused = job.alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.cbytes(), h, job.alg, false) &&
+                           line_capacity_ok(prog.cbytes(), h + 1);
         const int fsc = job.normalize ? F_SCALE : 0;
         if (fused) {
             PassBuilder b(prog, (int)h, line_stages(h, job.alg), false, job.lines, 24);
@@ -1272,7 +1382,7 @@ void lower_c2r_axis(Program &prog, const RealAxisJob &job) {
                                            job.out_buf, job.out_off, "c2r even-half"));
             return;
         }
-        if (!line_capacity_ok(prog.is_double, h + 1))
+        if (!line_capacity_ok(prog.cbytes(), h + 1))
             fail_unsupported("B200 engine: real axis pre-processing exceeds on-chip capacity");
         prog.scratch_elems[2] = std::max(prog.scratch_elems[2], (size_t)job.lines * h);
         {
@@ -1362,7 +1472,7 @@ void lower_convolution_axis0(Program &prog, size_t H, const AxisAlgorithm *alg, 
     const int mflags = (conj_sequence ? F_CONJ_IN : 0) | (cross_power ? F_NORMALIZE : 0) | F_CONJ_OUT;
     // power-of-two axis: forward FFT, multiply and inverse FFT in the register kernel
     if (alg->kind == AlgorithmKind::Stockham && is_pow2(H) && reg_kernels_enabled()) {
-        const int rv = reg_variant_for(prog.is_double, H, REG_CONV, true);
+        const int rv = reg_variant(prog, H, REG_CONV, true);
         if (rv >= 0) {
             PassPlan pp{};
             pp.kernel = KERNEL_REG;
@@ -1386,7 +1496,7 @@ void lower_convolution_axis0(Program &prog, size_t H, const AxisAlgorithm *alg, 
         }
     }
     const Side side = make_side((int64_t)H * inner, 0, 1, inner, false, (int64_t)H * inner, 1, (int)inner);
-    if (alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.is_double, H, alg, true)) {
+    if (alg->kind != AlgorithmKind::Bluestein && line_fits_on_chip(prog.cbytes(), H, alg, true)) {
         PassBuilder b(prog, (int)H, line_stages(H, alg), true, systems * inner, kMaxOps);
         b.load((int)H, 0);
         b.fft();

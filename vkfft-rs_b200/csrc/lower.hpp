@@ -57,7 +57,7 @@ int reg_variant_for(bool is_double, size_t n, int mode, bool strided);  // reg_k
 int reg_variant_radices(int v, int *out);
 int reg_variant_peer_twin(int v);  // REG_C2C -> REG_C2C_PEER variant (-1: none)
 int reg_variant_persistent_twin(int v);  // contiguous REG_C2C -> bulk-prefetch variant (-1: none)
-bool line_fits_on_chip(bool dbl, size_t L, const AxisAlgorithm *alg, bool strided);
+bool line_fits_on_chip(int complex_bytes, size_t L, const AxisAlgorithm *alg, bool strided);
 void lower_c2c_axis(Program &prog, const AxisJob &job);
 void lower_r2c_axis(Program &prog, const RealAxisJob &job);
 void lower_c2r_axis(Program &prog, const RealAxisJob &job);

@@ -98,6 +98,7 @@ struct alignas(16) Op {
     double scale;
     int64_t om;         // MUL: table index += (line's outer index o) * om
     int64_t lut_off;    // MUL: table index += lut_off
+    double scale_lo;    // double-double programs: low word of the scale (scale + scale_lo)
 };
 
 // Peer scatter of a pass's final store (the slab exchange fused into the last local FFT
@@ -170,10 +171,12 @@ struct ConvMultiply {
 // The tensor is [outer][N][inner]; the complex work array is [outer][L][inner], so a
 // thread index with `inner` fastest reads and writes coalesced lines for every axis.
 // kind: 0..3 DCT-I..IV, 4..7 DST-I..IV (the effective transform: II and III swap
-// for the inverse direction).
+// for the inverse direction).  tb: the reduction's twiddles by FFT position, [A | B]
+// (A the pre-processing, B the post-processing factor; lower.cpp table_r2r).
 struct R2rPass {
     const void *src;
     void *dst;
+    const void *tb;
     int64_t outer;  // batch x product of the slower dims
     int64_t inner;  // product of the faster dims
     int64_t n;      // logical length of the axis
@@ -182,6 +185,7 @@ struct R2rPass {
     int32_t kind;
     int32_t pre;    // 1: real tensor -> complex work array, 0: spectrum -> real tensor
     double scale;
+    double scale_lo;  // double-double programs: low word of the scale
 };
 
 // Boundary copy between a caller's buffer and a dense scratch tensor, with the

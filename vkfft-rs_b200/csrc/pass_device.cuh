@@ -11,6 +11,7 @@
 #endif
 
 #include "dft_codelets.cuh"
+#include "dd.cuh"
 #include "pass_desc.hpp"
 
 namespace b200fft {
@@ -41,6 +42,45 @@ template <typename T> __device__ __forceinline__ void st_data(void *base, int64_
     __stcs(reinterpret_cast<typename vec2<T>::type *>(base) + idx, w);
 }
 
+// Double-double complex elements are 32 bytes (re.hi, re.lo, im.hi, im.lo): two
+// 16-byte accesses each.
+template <> __device__ __forceinline__ cplx<dd> ld_ro<dd>(const void *base, int64_t idx) {
+    const double2 *q = reinterpret_cast<const double2 *>(base) + 2 * idx;
+    const double2 a = __ldg(q), b = __ldg(q + 1);
+    return {dd(a.x, a.y), dd(b.x, b.y)};
+}
+template <> __device__ __forceinline__ cplx<dd> ld_data<dd>(const void *base, int64_t idx) {
+    const double2 *q = reinterpret_cast<const double2 *>(base) + 2 * idx;
+    const double2 a = __ldcs(q), b = __ldcs(q + 1);
+    return {dd(a.x, a.y), dd(b.x, b.y)};
+}
+__device__ __forceinline__ double2 dd_words(dd v) {
+    double2 w;
+    w.x = v.hi;
+    w.y = v.lo;
+    return w;
+}
+template <> __device__ __forceinline__ void st_data<dd>(void *base, int64_t idx, cplx<dd> v) {
+    double2 *q = reinterpret_cast<double2 *>(base) + 2 * idx;
+    __stcs(q, dd_words(v.x));
+    __stcs(q + 1, dd_words(v.y));
+}
+
+// One real scalar of a real side.
+template <typename T> __device__ __forceinline__ T ld_real(const void *base, int64_t idx) {
+    return __ldcs(reinterpret_cast<const T *>(base) + idx);
+}
+template <> __device__ __forceinline__ dd ld_real<dd>(const void *base, int64_t idx) {
+    const double2 a = __ldcs(reinterpret_cast<const double2 *>(base) + idx);
+    return dd(a.x, a.y);
+}
+template <typename T> __device__ __forceinline__ void st_real(void *base, int64_t idx, T v) {
+    __stcs(reinterpret_cast<T *>(base) + idx, v);
+}
+template <> __device__ __forceinline__ void st_real<dd>(void *base, int64_t idx, dd v) {
+    __stcs(reinterpret_cast<double2 *>(base) + idx, dd_words(v));
+}
+
 __device__ __forceinline__ void raise_error(int *err, int code) {
     if (err && threadIdx.x == 0) atomicOr(err, code);
 }
@@ -56,8 +96,8 @@ __device__ __forceinline__ cplx<T> apply_mul(cplx<T> v, const Op &op, int c, int
         v = cmul(v, w);
     }
     if (op.flags & F_SCALE) {
-        v.x *= T(op.scale);
-        v.y *= T(op.scale);
+        v.x *= kc<T>(op.scale, op.scale_lo);
+        v.y *= kc<T>(op.scale, op.scale_lo);
     }
     if (op.flags & F_CONJ_OUT) v = cconj(v);
     return v;
@@ -113,7 +153,7 @@ __device__ __forceinline__ void op_load(const PassShape &p, const Op &op, cplx<T
                         mirrored = true;
                     }
                     if (s.real) {
-                        v[u].x = __ldcs(reinterpret_cast<const T *>(p.src) + a);
+                        v[u].x = ld_real<T>(p.src, a);
                     } else {
                         v[u] = ld_data<T>(p.src, a);
                         if (mirrored) v[u].y = -v[u].y;
@@ -158,7 +198,7 @@ __device__ __forceinline__ void op_store(const PassShape &p, const Op &op, const
                 a += p.peer.off - (int64_t)r * p.peer.sub;
             }
             if (s.real) {
-                __stcs(reinterpret_cast<T *>(dst) + a, v.x);
+                st_real<T>(dst, a, v.x);
             } else {
                 st_data<T>(dst, a, v);
             }
@@ -306,7 +346,7 @@ __device__ __forceinline__ void op_c2r_pre(const PassShape &p, const Op &op, cpl
     const int h = op.len;
     const int per = h / 2 + 1;
     const int total = p.G * per;
-    const T sc = (op.flags & F_SCALE) ? T(op.scale) : T(1);
+    const T sc = (op.flags & F_SCALE) ? kc<T>(op.scale, op.scale_lo) : T(1);
     const bool conj_out = op.flags & F_CONJ_OUT;
     for (int f = threadIdx.x; f < total; f += blockDim.x) {
         const int g = f / per;
@@ -481,8 +521,8 @@ __device__ __forceinline__ void op_permute_scatter(const Op &op, cplx<T> *sm) {
         }
         cplx<T> y = {x0.x + acc.x, x0.y + acc.y};
         if (op.flags & F_SCALE) {
-            y.x *= T(op.scale);
-            y.y *= T(op.scale);
+            y.x *= kc<T>(op.scale, op.scale_lo);
+            y.y *= kc<T>(op.scale, op.scale_lo);
         }
         if (op.flags & F_CONJ_OUT) y = cconj(y);
         sm[op.dst_base + g * op.sub_stride + spad(k)] = y;

@@ -5,6 +5,7 @@
 
 #include <complex>
 #include <cstdint>
+#include <cstring>
 #include <map>
 #include <string>
 #include <vector>
@@ -30,12 +31,14 @@ constexpr int kScratchBuffers = 6;
 struct HostTable {
     bool is_int = false;
     bool is_raw = false;  // already in the pass precision (user-supplied convolution spectra)
-    std::vector<std::complex<double>> c;
+    std::vector<std::complex<double>> c;   // values (double-double programs: the high words)
+    std::vector<std::complex<double>> lo;  // double-double programs: the low words (c + lo)
     std::vector<int32_t> i;
     std::vector<unsigned char> raw;
-    size_t bytes(bool dbl) const {
+    // bytes on the device for complex elements of `cbytes` bytes (8 f32, 16 f64, 32 dd)
+    size_t bytes(int cbytes) const {
         if (is_raw) return raw.size();
-        return is_int ? i.size() * 4 : c.size() * (dbl ? 16 : 8);
+        return is_int ? i.size() * 4 : c.size() * (size_t)cbytes;
     }
 };
 
@@ -66,7 +69,8 @@ struct PassPlan {
 };
 
 struct Program {
-    bool is_double = false;
+    bool is_double = false;  // compute in f64 (or in double-double when is_dd)
+    bool is_dd = false;      // compute in double-double (DoubleDouble precisions)
     std::vector<PassPlan> passes;
     std::vector<HostTable> tables;
     std::map<std::string, int> table_cache;
@@ -77,17 +81,48 @@ struct Program {
     int storage_scalar_bytes = 0;  // bytes of one stored scalar of the caller's buffers: 2 (f16),
                                    // 4, 8; 0 = the compute precision's
 
-    size_t io_scalar_bytes() const { return storage_scalar_bytes ? (size_t)storage_scalar_bytes : (is_double ? 8 : 4); }
+    int rbytes() const { return is_dd ? 16 : (is_double ? 8 : 4); }  // one compute scalar
+    int cbytes() const { return 2 * rbytes(); }                        // one compute complex
+    int scalar_kind() const { return is_dd ? 2 : (is_double ? 1 : 0); }  // kernel type: f32, f64, dd
+    size_t io_scalar_bytes() const { return storage_scalar_bytes ? (size_t)storage_scalar_bytes : (size_t)rbytes(); }
     size_t input_bytes() const { return input_elems * io_scalar_bytes() * (input_real ? 1 : 2); }
     size_t output_bytes() const { return output_elems * io_scalar_bytes() * (output_real ? 1 : 2); }
 
     size_t scratch_offset(int k) const {  // byte offset of scratch buffer k (256-byte aligned)
         size_t off = 0;
-        for (int i = 0; i < k; i++) off += (scratch_elems[i] * (is_double ? 16 : 8) + 255) & ~size_t(255);
+        for (int i = 0; i < k; i++) off += (scratch_elems[i] * (size_t)cbytes() + 255) & ~size_t(255);
         return off;
     }
     size_t scratch_bytes() const { return scratch_offset(kScratchBuffers); }
 };
+
+// Device image of a table in the program's precision: raw / int tables verbatim,
+// complex tables as f32 pairs, f64 pairs or double-double quadruples (re.hi, re.lo,
+// im.hi, im.lo, the reference's 32-byte DD complex layout).  `dst` holds t.bytes(cbytes).
+inline void pack_table(const HostTable &t, const Program &prog, unsigned char *dst) {
+    if (t.is_raw) {
+        std::memcpy(dst, t.raw.data(), t.raw.size());
+    } else if (t.is_int) {
+        std::memcpy(dst, t.i.data(), t.i.size() * 4);
+    } else if (prog.is_dd) {
+        double *d = reinterpret_cast<double *>(dst);
+        const bool has_lo = t.lo.size() == t.c.size();
+        for (size_t m = 0; m < t.c.size(); m++) {
+            d[4 * m] = t.c[m].real();
+            d[4 * m + 1] = has_lo ? t.lo[m].real() : 0.0;
+            d[4 * m + 2] = t.c[m].imag();
+            d[4 * m + 3] = has_lo ? t.lo[m].imag() : 0.0;
+        }
+    } else if (prog.is_double) {
+        std::memcpy(dst, t.c.data(), t.c.size() * 16);
+    } else {
+        float *f = reinterpret_cast<float *>(dst);
+        for (size_t m = 0; m < t.c.size(); m++) {
+            f[2 * m] = (float)t.c[m].real();
+            f[2 * m + 1] = (float)t.c[m].imag();
+        }
+    }
+}
 
 FastDiv make_fastdiv(uint32_t d);
 
@@ -96,6 +131,7 @@ int table_twiddle(Program &prog, size_t n);
 int table_reg_twiddles(Program &prog, size_t n, int variant);
 int table_bluestein_chirp(Program &prog, size_t n);
 int table_bluestein_spectrum(Program &prog, size_t n, size_t m);
+int table_r2r(Program &prog, int type, size_t n, size_t L);  // DCT/DST reduction twiddles [A | B]
 void host_fft_inplace(std::vector<std::complex<double>> &x, bool inverse);
 
 // Lowering of a whole transform (TransformIr families) into a Program.

@@ -11,14 +11,14 @@
 
 namespace b200fft {
 
-int kernel_variant_for(bool is_double);
+int kernel_variant_for(int scalar_kind);
 cudaError_t launch_pass(int variant, const PassParams &p, int64_t grid, int threads, size_t smem, cudaStream_t stream);
 void set_kernel_smem_limits();
 void set_reg_kernel_smem_limits();
 cudaError_t launch_reg(int variant, const RegParams &rp, cudaStream_t stream);
 cudaError_t launch_boundary_copy(const BoundaryCopy &b, cudaStream_t stream);
-cudaError_t launch_conv_multiply(const ConvMultiply &m, bool dbl, cudaStream_t stream);
-cudaError_t launch_r2r(const R2rPass &r, bool dbl, cudaStream_t stream);
+cudaError_t launch_conv_multiply(const ConvMultiply &m, int kind, cudaStream_t stream);
+cudaError_t launch_r2r(const R2rPass &r, int kind, cudaStream_t stream);
 
 // ---- host-side fault injection (no GPU fault is ever provoked) ------------------
 // B200FFT_FAULT=alloc:<n> or launch:<n> makes the n-th device allocation or kernel
@@ -163,26 +163,12 @@ static DeviceTables &ensure_tables(Context *ctx, uint64_t id, const Program &pro
     size_t total = 0;
     for (auto &t : prog.tables) {
         offs.push_back(total);
-        total += (t.bytes(prog.is_double) + 255) & ~size_t(255);
+        total += (t.bytes(prog.cbytes()) + 255) & ~size_t(255);
     }
     DeviceTables dt;
     std::vector<unsigned char> host(std::max<size_t>(total, 256));
     for (size_t k = 0; k < prog.tables.size(); k++) {
-        const HostTable &t = prog.tables[k];
-        unsigned char *dst = host.data() + offs[k];
-        if (t.is_raw) {
-            std::memcpy(dst, t.raw.data(), t.raw.size());
-        } else if (t.is_int) {
-            std::memcpy(dst, t.i.data(), t.i.size() * 4);
-        } else if (prog.is_double) {
-            std::memcpy(dst, t.c.data(), t.c.size() * 16);
-        } else {
-            float *f = reinterpret_cast<float *>(dst);
-            for (size_t m = 0; m < t.c.size(); m++) {
-                f[2 * m] = (float)t.c[m].real();
-                f[2 * m + 1] = (float)t.c[m].imag();
-            }
-        }
+        pack_table(prog.tables[k], prog, host.data() + offs[k]);
     }
     dt.base = device_alloc(host.size(), "table upload allocation");
     // A copy from pageable memory may return before its DMA has reached device memory, and
@@ -222,21 +208,22 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
     std::lock_guard<std::mutex> l(ctx->mu);
     if (!stream) stream = ctx->stream;
     DeviceTables &dt = ensure_tables(ctx, id, prog);
-    const size_t esz = prog.is_double ? 16 : 8;
+    const size_t esz = (size_t)prog.cbytes();
     unsigned char *scr = static_cast<unsigned char *>(workspace);
     if (!scr && prog.scratch_bytes() > 0)
         scr = static_cast<unsigned char *>(
             ensure_buffer(ctx->scratch, ctx->scratch_bytes, prog.scratch_bytes(), "scratch allocation"));
     void *bufs[2 + kScratchBuffers] = {const_cast<void *>(in), out};
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scr ? scr + prog.scratch_offset(k) : nullptr;
-    const int variant = kernel_variant_for(prog.is_double);
+    const int variant = kernel_variant_for(prog.scalar_kind());
     for (size_t pi = 0; pi < prog.passes.size(); pi++) {
         const PassPlan &pp = prog.passes[pi];
         if (pp.kernel == KERNEL_R2R) {
             R2rPass rr = pp.rr;
             rr.src = bufs[pp.src_buf];
             rr.dst = bufs[pp.dst_buf];
-            check(launch_r2r(rr, prog.is_double, stream), "kernel launch");
+            rr.tb = pp.reg_table2 >= 0 ? dt.ptrs[pp.reg_table2] : nullptr;
+            check(launch_r2r(rr, prog.scalar_kind(), stream), "kernel launch");
             continue;
         }
         if (pp.kernel == KERNEL_CMUL) {
@@ -244,7 +231,7 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
             cm.src = bufs[pp.src_buf];
             cm.dst = bufs[pp.dst_buf];
             cm.ker = dt.ptrs[pp.reg_table];
-            check(launch_conv_multiply(cm, prog.is_double, stream), "kernel launch");
+            check(launch_conv_multiply(cm, prog.scalar_kind(), stream), "kernel launch");
             continue;
         }
         if (pp.kernel == KERNEL_COPY) {
@@ -359,7 +346,7 @@ static bool same_algorithm(const Program &a, const Program &b) {
         }
     }
     for (size_t i = 0; i < a.tables.size(); i++)
-        if (a.tables[i].bytes(a.is_double) != b.tables[i].bytes(b.is_double)) return false;
+        if (a.tables[i].bytes(a.cbytes()) != b.tables[i].bytes(b.cbytes())) return false;
     return true;
 }
 
@@ -390,6 +377,10 @@ static void execute_mixed_host(Context *ctx, Transform &t, const void *in, size_
     const size_t n_in = prog.input_elems * (prog.input_real ? 1 : 2), n_out = prog.output_elems * (prog.output_real ? 1 : 2);
     if (in_bytes != n_in * api) fail_input_length(prog.input_elems, in_bytes / (api * (prog.input_real ? 1 : 2)));
     if (out_bytes != n_out * api) fail_input_length(prog.output_elems, out_bytes / (api * (prog.output_real ? 1 : 2)));
+    if (api == sb) {  // double-double with f64 storage: the host arrays are the storage type
+        execute_program_host(ctx, t.id, prog, in, in_bytes, out, out_bytes);
+        return;
+    }
     std::vector<unsigned char> si(n_in * sb), so(n_out * sb);
     for (size_t k = 0; k < n_in; k++) {
         const double v = api == 8 ? static_cast<const double *>(in)[k] : static_cast<const float *>(in)[k];

@@ -15,12 +15,12 @@
 
 namespace b200fft {
 
-int kernel_variant_for(bool is_double);
+int kernel_variant_for(int scalar_kind);
 cudaError_t launch_pass(int variant, const PassParams &p, int64_t grid, int threads, size_t smem, cudaStream_t stream);
 cudaError_t launch_reg(int variant, const RegParams &rp, cudaStream_t stream);
 cudaError_t launch_boundary_copy(const BoundaryCopy &b, cudaStream_t stream);
-cudaError_t launch_conv_multiply(const ConvMultiply &m, bool dbl, cudaStream_t stream);
-cudaError_t launch_r2r(const R2rPass &r, bool dbl, cudaStream_t stream);
+cudaError_t launch_conv_multiply(const ConvMultiply &m, int kind, cudaStream_t stream);
+cudaError_t launch_r2r(const R2rPass &r, int kind, cudaStream_t stream);
 
 constexpr size_t kStaticWorkspaceBytes = size_t(16) << 20;  // B200FFT_STATIC_WORKSPACE_BYTES
 constexpr int kMaxStaticDevices = 64;
@@ -53,7 +53,7 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
         throw FftError(B200FFT_RESOURCE_LIMIT_EXCEEDED, "static workspace execution supports at most " +
                                                             std::to_string(kMaxStaticTables) + " tables per transform");
     size_t table_bytes = 0;
-    for (auto &t : prog.tables) table_bytes += round256(t.bytes(prog.is_double));
+    for (auto &t : prog.tables) table_bytes += round256(t.bytes(prog.cbytes()));
     const size_t scratch_bytes = prog.scratch_bytes();
     if (table_bytes + scratch_bytes > kStaticWorkspaceBytes)
         throw FftError(B200FFT_RESOURCE_LIMIT_EXCEEDED,
@@ -74,7 +74,7 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
     size_t off = 0;
     for (size_t k = 0; k < prog.tables.size(); k++) {
         tables[k] = r.base + off;
-        off += round256(prog.tables[k].bytes(prog.is_double));
+        off += round256(prog.tables[k].bytes(prog.cbytes()));
     }
     if (r.owner != id && table_bytes > 0) {
         // Pack in the pass precision (as the context's table upload does), then one
@@ -82,21 +82,8 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
         // once the source was consumed, so the staging image can be reused at once.
         off = 0;
         for (const HostTable &t : prog.tables) {
-            unsigned char *dst = g_table_image + off;
-            if (t.is_raw) {
-                std::memcpy(dst, t.raw.data(), t.raw.size());
-            } else if (t.is_int) {
-                std::memcpy(dst, t.i.data(), t.i.size() * 4);
-            } else if (prog.is_double) {
-                std::memcpy(dst, t.c.data(), t.c.size() * 16);
-            } else {
-                float *f = reinterpret_cast<float *>(dst);
-                for (size_t m = 0; m < t.c.size(); m++) {
-                    f[2 * m] = (float)t.c[m].real();
-                    f[2 * m + 1] = (float)t.c[m].imag();
-                }
-            }
-            off += round256(t.bytes(prog.is_double));
+            pack_table(t, prog, g_table_image + off);
+            off += round256(t.bytes(prog.cbytes()));
         }
         r.owner = 0;
         check(cudaMemcpyAsync(r.base, g_table_image, table_bytes, cudaMemcpyHostToDevice, stream),
@@ -104,16 +91,17 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
     }
     r.owner = id;
     unsigned char *scr = r.base + table_bytes;
-    const size_t esz = prog.is_double ? 16 : 8;
+    const size_t esz = (size_t)prog.cbytes();
     void *bufs[2 + kScratchBuffers] = {const_cast<void *>(in), out};
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scr + prog.scratch_offset(k);
-    const int variant = kernel_variant_for(prog.is_double);
+    const int variant = kernel_variant_for(prog.scalar_kind());
     for (const PassPlan &pp : prog.passes) {
         if (pp.kernel == KERNEL_R2R) {
             R2rPass rr = pp.rr;
             rr.src = bufs[pp.src_buf];
             rr.dst = bufs[pp.dst_buf];
-            check(launch_r2r(rr, prog.is_double, stream), "kernel launch");
+            rr.tb = pp.reg_table2 >= 0 ? tables[pp.reg_table2] : nullptr;
+            check(launch_r2r(rr, prog.scalar_kind(), stream), "kernel launch");
             continue;
         }
         if (pp.kernel == KERNEL_CMUL) {
@@ -121,7 +109,7 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
             cm.src = bufs[pp.src_buf];
             cm.dst = bufs[pp.dst_buf];
             cm.ker = tables[pp.reg_table];
-            check(launch_conv_multiply(cm, prog.is_double, stream), "kernel launch");
+            check(launch_conv_multiply(cm, prog.scalar_kind(), stream), "kernel launch");
             continue;
         }
         if (pp.kernel == KERNEL_COPY) {

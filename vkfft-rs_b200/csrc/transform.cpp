@@ -3,6 +3,7 @@
 // builders do (nd_ir.rs:676-708, real_ir.rs:282-345, nd_real_ir.rs:88-225) and lower the
 // executed plans to the B200 launch program.
 #include <atomic>
+#include <cmath>
 #include <cstring>
 
 #include "transform.hpp"
@@ -30,15 +31,40 @@ static size_t product(const std::vector<size_t> &v, size_t from, size_t to) {
 }
 
 // Bytes of one compute / stored scalar of a precision (config.rs:107-161 layouts).
-static bool compute_is_f64(Precision p) { return p == Precision::F64 || p == Precision::F64ComputeF32Storage; }
+static bool compute_is_dd(Precision p) {
+    return p == Precision::DoubleDouble || p == Precision::DoubleDoubleF64Storage;
+}
+static bool compute_is_f64(Precision p) {
+    return p == Precision::F64 || p == Precision::F64ComputeF32Storage || compute_is_dd(p);
+}
 static int storage_scalar_bytes(Precision p) {
-    return p == Precision::F16StorageF32Compute ? 2 : (p == Precision::F64 ? 8 : 4);
+    switch (p) {
+        case Precision::F16StorageF32Compute: return 2;
+        case Precision::F64:
+        case Precision::DoubleDoubleF64Storage: return 8;
+        case Precision::DoubleDouble: return 16;
+        default: return 4;
+    }
 }
 
-static void check_executable(const FftConfig &c) {
-    if (!(c.precision == Precision::F32 || c.precision == Precision::F64 ||
-          c.precision == Precision::F16StorageF32Compute || c.precision == Precision::F64ComputeF32Storage))
-        fail_precision("B200 engine", precision_name(c.precision));
+static void check_executable(const FftConfig &) {}
+
+// Double-double programs: every scale of the lowering is the reciprocal of an integer
+// k (1/N, 1/M, 1/(2(N-1)), ...), passed as the nearest double; its low word is the
+// exact residual (1 - s k) / k, formed with one FMA.
+static double dd_scale_residual(double s) {
+    if (s == 0.0 || s == 1.0) return 0.0;
+    const double k = std::nearbyint(1.0 / s);
+    if (k < 1.0 || std::fabs(s * k - 1.0) > 1e-12) return 0.0;
+    return std::fma(-s, k, 1.0) / k;
+}
+
+static void finalize_dd_scales(Program &prog) {
+    if (!prog.is_dd) return;
+    for (PassPlan &pp : prog.passes) {
+        for (int k = 0; k < pp.p.nops; k++) pp.p.ops[k].scale_lo = dd_scale_residual(pp.p.ops[k].scale);
+        pp.rr.scale_lo = dd_scale_residual(pp.rr.scale);
+    }
 }
 
 static bool is_r2r(TransformKind k) {
@@ -124,13 +150,13 @@ static void add_boundaries(Transform &t) {
     t.formatted = fmt_in || fmt_out;
     // mixed precision (F16 storage / F32 compute, F64 compute / F32 storage): the caller's
     // buffers hold the storage type, converted at the boundary copies
-    const int sbytes = storage_scalar_bytes(c.precision), cbytes = prog.is_double ? 8 : 4;
+    const int sbytes = storage_scalar_bytes(c.precision), cbytes = prog.rbytes();
     const bool mixed = sbytes != cbytes;
     if (mixed) prog.storage_scalar_bytes = sbytes;
     if (!pad_in && !pad_out && !fmt_in && !fmt_out && !mixed) return;
     if (c.dimensions.size() > (size_t)kMaxCopyRank) fail_unsupported("boundary copies support rank <= 8");
     const size_t batch = c.kernel_preparation_system_count();
-    const size_t esz = prog.is_double ? 16 : 8;
+    const size_t esz = (size_t)prog.cbytes();
     auto copy = [&](const std::vector<size_t> &dims, bool input, bool pad, size_t elem_bytes, int src, int dst) {
         PassPlan pp{};
         pp.kernel = KERNEL_COPY;
@@ -192,6 +218,7 @@ static std::unique_ptr<Transform> build_transform_core(const FftConfig &config_i
 std::unique_ptr<Transform> build_transform(const FftConfig &config_in, int direction, const DeviceProfile &device) {
     auto t = build_transform_core(config_in, direction, device);
     add_boundaries(*t);
+    finalize_dd_scales(t->prog);
     return t;
 }
 
@@ -215,6 +242,7 @@ static std::unique_ptr<Transform> build_transform_core(const FftConfig &config_i
     t->children.assign(rank, std::nullopt);
     Program &prog = t->prog;
     prog.is_double = compute_is_f64(c.precision);
+    prog.is_dd = compute_is_dd(c.precision);
 
     if (c.transform == TransformKind::C2C) {
         const size_t tensor = product(c.dimensions, 0, rank);
@@ -333,6 +361,7 @@ static std::unique_ptr<Transform> build_transform_core(const FftConfig &config_i
                 r.kind = kind;
                 r.pre = pre ? 1 : 0;
                 r.scale = scale;
+                if ((kind & 3) != 0) pp.reg_table2 = table_r2r(prog, kind & 3, n, L);
                 pp.src_buf = pre ? (first ? BUF_IN : BUF_OUT) : BUF_SCRATCH1;
                 pp.dst_buf = pre ? BUF_SCRATCH1 : BUF_OUT;
                 pp.label = pre ? "r2r pre-process" : "r2r post-process";

@@ -627,7 +627,19 @@ _np_dtype = {
     (Precision.F64, True): np.float64, (Precision.F64, False): np.complex128,
     (Precision.F16_STORAGE_F32_COMPUTE, True): np.float32, (Precision.F16_STORAGE_F32_COMPUTE, False): np.complex64,
     (Precision.F64_COMPUTE_F32_STORAGE, True): np.float64, (Precision.F64_COMPUTE_F32_STORAGE, False): np.complex128,
+    # double-double: float64 words, (hi, lo) per real and (re.hi, re.lo, im.hi, im.lo) per
+    # complex element (the reference's DD buffer layout, double_double.rs encode_complex_double_double)
+    (Precision.DOUBLE_DOUBLE, True): np.float64, (Precision.DOUBLE_DOUBLE, False): np.float64,
+    (Precision.DOUBLE_DOUBLE_F64_STORAGE, True): np.float64,
+    (Precision.DOUBLE_DOUBLE_F64_STORAGE, False): np.complex128,
 }
+
+
+def _words(precision, real):
+    """Array items per logical element: 2 (real) / 4 (complex) for double-double, else 1."""
+    if precision == Precision.DOUBLE_DOUBLE:
+        return 2 if real else 4
+    return 1
 
 
 class TransformIr:
@@ -723,6 +735,15 @@ class TransformIr:
 
     def output_dtype(self):
         return _np_dtype[(self.config.precision, self.output_is_real)]
+
+    @property
+    def input_items(self):
+        """Host array items of the input (elements x words per element)."""
+        return self.input_elements * _words(self.config.precision, self.input_is_real)
+
+    @property
+    def output_items(self):
+        return self.output_elements * _words(self.config.precision, self.output_is_real)
 
 
 class ConvolutionConjugation(enum.IntEnum):
@@ -953,8 +974,8 @@ class CudaExecutionContext:
         `out` optionally supplies the (e.g. pinned) destination array."""
         x = np.ascontiguousarray(data, dtype=ir.input_dtype())
         if out is None:
-            out = np.empty(ir.output_elements, dtype=ir.output_dtype())
-        elif out.dtype != ir.output_dtype() or out.size != ir.output_elements or not out.flags.c_contiguous:
+            out = np.empty(ir.output_items, dtype=ir.output_dtype())
+        elif out.dtype != ir.output_dtype() or out.size != ir.output_items or not out.flags.c_contiguous:
             raise VkFftError(Status.InputLengthMismatch,
                              f"input contains {out.size} complex elements but kernel expects {ir.output_elements}")
         _check(library().b200fft_execute_host(self._h, ir._h, x.ctypes.data, x.nbytes,
@@ -966,7 +987,7 @@ class CudaExecutionContext:
         host execution and returns an AsyncTransformTicket at once."""
         x = np.ascontiguousarray(data, dtype=ir.input_dtype())
         if out is None:
-            out = np.empty(ir.output_elements, dtype=ir.output_dtype())
+            out = np.empty(ir.output_items, dtype=ir.output_dtype())
         h = ctypes.c_void_p()
         _check(library().b200fft_submit_host(self._h, ir._h, x.ctypes.data, x.nbytes, out.ctypes.data, out.nbytes,
                                              ctypes.byref(h)))
@@ -977,6 +998,16 @@ class CudaExecutionContext:
         return self.execute_transform(ir, data)
 
     def execute_transform_f64(self, ir, data):
+        return self.execute_transform(ir, data)
+
+    def execute_transform_double_double(self, ir, data):
+        """execute_transform_double_double (native_runtime.rs:971-987): float64 words,
+        (re.hi, re.lo, im.hi, im.lo) per complex element, (hi, lo) per real one."""
+        return self.execute_transform(ir, data)
+
+    def execute_transform_double_double_f64_storage(self, ir, data):
+        """execute_transform_double_double_f64_storage (native_runtime.rs:988-1004): f64
+        host arrays, double-double compute."""
         return self.execute_transform(ir, data)
 
     def execute_nd_real_convolution(self, ir, data, out=None):
