@@ -197,6 +197,8 @@ def test_fftw_golden_vectors_on_gpu(V, ctx, set_name, prec):
         cfg = V.FftConfig(shape).with_precision(V.Precision[prec])
         if kind == 1:
             cfg = cfg.with_transform(V.TransformKind.R2C)
+        elif kind == 2:  # ND DCT-II (FFTW REDFT10 on every axis)
+            cfg = cfg.with_transform(V.TransformKind.DCT2)
         if name == "c2c-bluestein-n103":
             t = V.PlannerTuning.portable()
             t.max_rader_fft_prime = 100
