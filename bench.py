@@ -327,6 +327,9 @@ WORKLOADS = {
     "dct2-4096-f64": dict(kind="r2r", r2r="DCT2", dims=[4096], batch=8192, prec="F64", config=0),
     "dct4-4096-f32": dict(kind="r2r", r2r="DCT4", dims=[4096], batch=16384, prec="F32", config=0),
     "dct2-512^2-f32": dict(kind="r2r", r2r="DCT2", dims=[512, 512], batch=256, prec="F32", config=0),
+    # double-double (not a headline config): C2C forward + normalised inverse
+    "c2c-4096-dd": dict(kind="c2c", dims=[4096], batch=2048, prec="DOUBLE_DOUBLE", config=0),
+    "c2c-1000-dd": dict(kind="c2c", dims=[1000], batch=8192, prec="DOUBLE_DOUBLE", config=0),
 }
 
 
@@ -437,9 +440,10 @@ def run_workload(args):
     kind, dims, batch, prec = wl["kind"], wl["dims"], wl["batch"], wl["prec"]
     if ws > 1 and wl.get("slab"):
         return run_slab_workload(args, wl, ctx, dev, dist, ws, rank, local)
-    dbl = prec == "F64"
+    dbl = prec in ("F64", "DOUBLE_DOUBLE")
     tdt = torch.float64 if dbl else torch.float32
-    rsz = 8 if dbl else 4
+    words = 2 if prec == "DOUBLE_DOUBLE" else 1  # float64 words per real value
+    rsz = (8 if dbl else 4) * words
     n = int(np.prod(dims))
     half = int(np.prod(dims[:-1])) * (dims[-1] // 2 + 1)
     gen = torch.Generator(device="cuda")
@@ -464,7 +468,9 @@ def run_workload(args):
         if kind == "c2c":
             fwd = V.TransformIr.build(cfg, V.Direction.FORWARD, dev)
             inv = V.TransformIr.build(cfg, V.Direction.INVERSE, dev)
-            a = torch.rand((batch * n * 2,), device="cuda", generator=gen, dtype=tdt) * 2 - 1
+            a = torch.rand((batch * n * 2 * words,), device="cuda", generator=gen, dtype=tdt) * 2 - 1
+            if words == 2:  # double-double words: a small canonical low word under each high word
+                a.view(-1, 2)[:, 1] *= 2.0 ** -60
             b = torch.empty_like(a)
             flop = 2 * 5.0 * n * math.log2(n) * batch
             alg_bytes = [2 * batch * n * 2 * rsz] * 2
@@ -520,7 +526,7 @@ def run_workload(args):
     line = {
         "metric": f"{args.workload} GFLOP/s (5N*log2N complex, 2.5N*log2N real and DCT/DST)", "value": value, "unit": "GFLOP/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": prec.lower(), "data": "synthetic (torch generator)",
+        "scaling": "weak", "vs_baseline": None, "dtype": "dd" if words == 2 else prec.lower(), "data": "synthetic (torch generator)",
         "config": {"workload": (f"BASELINE config {wl['config']}: " if wl["config"] else f"{wl.get('r2r')} ")
                                + f"{kind} {dims} x batch {batch}"
                                + (" recursive Rader tuning" if wl.get("tuning") else ""),
