@@ -34,6 +34,25 @@ template <> struct vec2<double> { using type = double2; };
 
 __device__ __forceinline__ int pad(int e) { return e + (e >> 4); }
 
+// Shared-memory stride between the G lines of a CTA (complex elements, >= pad(N-1) + 1).
+// A 128-byte wavefront holds W complex values (16 for f32, 8 for f64).  Within one
+// wavefront a warp touches L lines at D consecutive positions each: strided layouts put
+// the lines fastest (L = min(G, W), D = W / L), contiguous ones the positions (D = min(TT,
+// W), L = W / D).  Line g's slot for position t is g*LS + t (+ the same pad), so the
+// wavefront is conflict-free when LS = D (mod W): the lines then start D slots apart and
+// their D positions fill the gaps.  (LS = N + N/16 + 1 = 1 (mod W) made a strided
+// 8-line CTA 2-way conflicted.)
+template <typename T>
+__host__ __device__ constexpr int reg_ls(int N, int E, int G, bool strided) {
+    const int W = sizeof(T) == 4 ? 16 : 8;
+    const int TT = N / E;
+    int ls = N + N / 16 + 1;
+    if (!strided && TT >= W) return ls;  // a wavefront stays inside one line
+    const int D = strided ? (G >= W ? 1 : W / G) : TT;
+    while (ls % W != D % W) ls++;
+    return ls;
+}
+
 template <typename T> __device__ __forceinline__ cplx<T> mul(cplx<T> a, cplx<T> b) {
     return {a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x};
 }
@@ -296,7 +315,7 @@ __device__ __forceinline__ void stages(cplx<T> (&v)[E], int t, cplx<T> *sline, c
 template <typename T, int N, int E, int G, int MODE, bool STRIDED, int... Rs>
 __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_constant__ RegParams rp) {
     constexpr int TT = N / E;
-    constexpr int LS = N + N / 16 + 1;  // padded line stride in shared memory
+    constexpr int LS = reg_ls<T>(N, E, G, STRIDED);  // line stride in shared memory
     extern __shared__ __align__(16) unsigned char smem_raw[];
     int g, t;
     if (STRIDED) {
@@ -448,7 +467,7 @@ __device__ __forceinline__ bool bar_wait(uint64_t *bar, unsigned parity) {
 template <typename T, int N, int E, int G, int MINB, int MODE, int... Rs>
 __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __grid_constant__ RegParams rp) {
     constexpr int TT = N / E;
-    constexpr int LS = N + N / 16 + 1;
+    constexpr int LS = reg_ls<T>(N, E, G, false);
     // bytes of one line in the input: N complex, or r2r_n reals (at most 2N of them)
     const unsigned LINE_BYTES = MODE == REG_R2R ? (unsigned)(rp.r2r_n * sizeof(T)) : (unsigned)(N * sizeof(cplx<T>));
     const unsigned GROUP_BYTES = G * LINE_BYTES;
@@ -529,12 +548,12 @@ struct RegVariant {
 };
 
 #define RV(T, MODE, STR, N, E, G, ...)                                                                      \
-    {sizeof(T) == 8, N, MODE, STR, G *(N / E), G, (size_t)G *(N + N / 16 + 1) * sizeof(T) * 2,             \
+    {sizeof(T) == 8, N, MODE, STR, G *(N / E), G, (size_t)G * regk::reg_ls<T>(N, E, G, STR) * sizeof(T) * 2,  \
      (const void *)regk::reg_fft_kernel<T, N, E, G, MODE, STR, __VA_ARGS__>, {__VA_ARGS__}, 0}
 // persistent contiguous lines: barrier slot + one group buffer + the exchange buffer
 #define RVP(T, MODE, N, E, G, MINB, ...)                                                                    \
     {sizeof(T) == 8, N, MODE, 0, G *(N / E), G,                                                             \
-     128 + (size_t)G * N * sizeof(T) * 2 + (size_t)G *(N + N / 16 + 1) * sizeof(T) * 2,                     \
+     128 + (size_t)G * N * sizeof(T) * 2 + (size_t)G * regk::reg_ls<T>(N, E, G, false) * sizeof(T) * 2,     \
      (const void *)regk::reg_fft_persistent<T, N, E, G, MINB, MODE, __VA_ARGS__>, {__VA_ARGS__}, 1}
 #define RVP_ALL(T, MODE)                                                                                    \
     RVP(T, MODE, 256, 16, 16, 3, 16, 16), RVP(T, MODE, 512, 16, 8, 3, 16, 16, 2),                           \
