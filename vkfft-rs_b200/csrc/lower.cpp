@@ -1275,6 +1275,22 @@ static bool lower_real_axis_register(Program &prog, const RealAxisJob &job, bool
     pp.src_buf = job.in_buf;
     pp.dst_buf = job.out_buf;
     pp.label = r2c ? "register r2c even-half" : "register c2r even-half";
+    // dense C2R lines: the persistent variant fetches each CTA's next group of bins with
+    // one bulk copy when every group (the last, partial one included) is a multiple of 16
+    // bytes (its loads gather X[p] and X[h-p]; R2C measured faster without it)
+    if (!r2c) {
+        const int pv = reg_variant_persistent_twin(rv);
+        if (pv >= 0) {
+            const size_t G = (size_t)reg_variant_lines_per_cta(pv);
+            const size_t line_bytes = (r2c ? h : h + 1) * (size_t)prog.cbytes();
+            const size_t tail = (size_t)job.lines % G;
+            if ((G * line_bytes) % 16 == 0 && (tail * line_bytes) % 16 == 0) {
+                pp.reg_variant_plain = rv;
+                pp.reg_variant = pv;
+                pp.label = "register c2r even-half (bulk prefetch)";
+            }
+        }
+    }
     for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
     prog.passes.push_back(pp);
     return true;

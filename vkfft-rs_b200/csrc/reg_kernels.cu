@@ -312,6 +312,49 @@ __device__ __forceinline__ void stages(cplx<T> (&v)[E], int t, cplx<T> *sline, c
     if constexpr (!LAST) stages<T, N, E, MODE, P * R, NEXT_OFF, false, Rest...>(v, t, sline, tw, rp, io);
 }
 
+// REG_C2R_HALF pre-processing of position p from the h+1 bins X (accessor at(j)):
+// Z[p] = s (X[p] + conj X[h-p] + i conj(W_2h^p) (X[p] - conj X[h-p])), conjugated for
+// the inverse-by-forward trick.
+template <typename T, int N, typename At>
+__device__ __forceinline__ cplx<T> c2r_half_point(const RegParams &rp, At at, int p) {
+    cplx<T> x = at(p);
+    cplx<T> mc = at(N - p);
+    if (p == 0 && rp.real_ends) x.y = mc.y = T(0);  // X[0], X[h]
+    const cplx<T> wv = tw_load(reinterpret_cast<const cplx<T> *>(rp.tw2), p);
+    const cplx<T> mm = {mc.x, -mc.y};
+    const cplx<T> d = {x.x - mm.x, x.y - mm.y};
+    const cplx<T> r = mul(cplx<T>{wv.x, -wv.y}, d);
+    const T sc = T(rp.scale2);
+    return {sc * (x.x + mm.x - r.y), -(sc * (x.y + mm.y + r.x))};
+}
+
+// REG_R2C_HALF post-processing: X[k] = 1/2 ((Z[k] + conj Z[h-k]) - i W_2h^k (Z[k] -
+// conj Z[h-k])), k = 0..h.  Z[h-k] belongs to another thread, so Z goes through the
+// line's shared-memory slot once.
+template <typename T, int N, int E>
+__device__ __forceinline__ void r2c_half_epilogue(const RegParams &rp, const cplx<T> (&v)[E], int t,
+                                                  cplx<T> *sline, int64_t out_base, bool valid) {
+    constexpr int TT = N / E;
+    __syncthreads();  // the last stage's shared-memory reads are done
+#pragma unroll
+    for (int m = 0; m < E; m++) sline[pad(t + m * TT)] = v[m];
+    __syncthreads();
+    if (!valid) return;
+    const cplx<T> *w2 = reinterpret_cast<const cplx<T> *>(rp.tw2);
+    auto post = [&](cplx<T> a, cplx<T> bc, int kk) {
+        const cplx<T> b = {bc.x, -bc.y};
+        const cplx<T> r = mul(tw_load(w2, kk), cplx<T>{a.x - b.x, a.y - b.y});
+        return cplx<T>{T(0.5) * (a.x + b.x + r.y), T(0.5) * (a.y + b.y - r.x)};
+    };
+#pragma unroll
+    for (int m = 0; m < E; m++) {
+        const int p = t + m * TT;
+        const cplx<T> zk2 = sline[pad((N - p) & (N - 1))];
+        st_c<T>(rp.out, out_base + p, post(v[m], zk2, p));
+        if (p == 0) st_c<T>(rp.out, out_base + N, post(v[m], v[m], N));
+    }
+}
+
 template <typename T, int N, int E, int G, int MODE, bool STRIDED, int... Rs>
 __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_constant__ RegParams rp) {
     constexpr int TT = N / E;
@@ -351,17 +394,7 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
                 const cplx<T> w = ld_c<T>(rp.in, io.in_base + (int64_t)p * rp.src.es);
                 v[m] = {w.x, rp.conj ? -w.y : w.y};
             } else if (MODE == REG_C2R_HALF) {
-                // Z[p] = s (X[p] + conj X[h-p] + i conj(W_2h^p) (X[p] - conj X[h-p])), then
-                // conjugated for the inverse-by-forward trick
-                cplx<T> x = ld_c<T>(rp.in, io.in_base + p);
-                cplx<T> mc = ld_c<T>(rp.in, io.in_base + (N - p));
-                if (p == 0 && rp.real_ends) x.y = mc.y = T(0);  // X[0], X[h]
-                const cplx<T> wv = tw_load(reinterpret_cast<const cplx<T> *>(rp.tw2), p);
-                const cplx<T> mm = {mc.x, -mc.y};
-                const cplx<T> d = {x.x - mm.x, x.y - mm.y};
-                const cplx<T> r = mul(cplx<T>{wv.x, -wv.y}, d);
-                const T sc = T(rp.scale2);
-                v[m] = {sc * (x.x + mm.x - r.y), -(sc * (x.y + mm.y + r.x))};
+                v[m] = c2r_half_point<T, N>(rp, [&](int j) { return ld_c<T>(rp.in, io.in_base + j); }, p);
             } else if (MODE == REG_R2C_FULL) {
                 v[m] = {__ldcs(reinterpret_cast<const T *>(rp.in) + io.in_base + (int64_t)p * rp.src.es), T(0)};
             } else {
@@ -407,34 +440,13 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
     if (MODE == REG_R2R && io.valid) r2r_store_all<T, N, E, !STRIDED>(rp, reinterpret_cast<T *>(rp.out) + io.out_base, t, v);
     // peer stores are visible system-wide before the rank's exchange signal
     if (MODE == REG_C2C_PEER) __threadfence_system();
-    if (MODE == REG_R2C_HALF) {
-        // X[k] = 1/2 ((Z[k] + conj Z[h-k]) - i W_2h^k (Z[k] - conj Z[h-k])), k = 0..h:
-        // Z[h-k] belongs to another thread, so Z goes through shared memory once
-        __syncthreads();  // the last stage's shared-memory reads are done
-#pragma unroll
-        for (int m = 0; m < E; m++) sline[pad(t + m * TT)] = v[m];
-        __syncthreads();
-        if (io.valid) {
-            const cplx<T> *w2 = reinterpret_cast<const cplx<T> *>(rp.tw2);
-            auto post = [&](cplx<T> a, cplx<T> bc, int kk) {
-                const cplx<T> b = {bc.x, -bc.y};
-                const cplx<T> r = mul(tw_load(w2, kk), cplx<T>{a.x - b.x, a.y - b.y});
-                return cplx<T>{T(0.5) * (a.x + b.x + r.y), T(0.5) * (a.y + b.y - r.x)};
-            };
-#pragma unroll
-            for (int m = 0; m < E; m++) {
-                const int p = t + m * TT;
-                const cplx<T> zk2 = sline[pad((N - p) & (N - 1))];
-                st_c<T>(rp.out, io.out_base + p, post(v[m], zk2, p));
-                if (p == 0) st_c<T>(rp.out, io.out_base + N, post(v[m], v[m], N));
-            }
-        }
-    }
+    if (MODE == REG_R2C_HALF) r2c_half_epilogue<T, N, E>(rp, v, t, sline, io.out_base, io.valid);
 }
 
 // ---- persistent variant: bulk-copy prefetch of the next line group -------------------
-// Dense contiguous lines (REG_C2C: N complex points; REG_R2R: the real line of rp.r2r_n
-// values, whose byte length is a multiple of 16): each CTA loops over groups of G lines.  One thread fetches the group with cp.async.bulk into a shared
+// Dense contiguous lines (REG_C2C: N complex points; REG_C2R_HALF: N+1 bins; REG_R2R:
+// the real line of rp.r2r_n values), every group's bytes a multiple of 16:
+// each CTA loops over groups of G lines.  One thread fetches the group with cp.async.bulk into a shared
 // buffer, tracked by an mbarrier; as soon as every thread has taken its points from the
 // buffer it fetches the CTA's next group, so the next load overlaps the radix stages and
 // the stores of the current one.  Waits are bounded: on expiry the kernel records error
@@ -468,13 +480,16 @@ template <typename T, int N, int E, int G, int MINB, int MODE, int... Rs>
 __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __grid_constant__ RegParams rp) {
     constexpr int TT = N / E;
     constexpr int LS = reg_ls<T>(N, E, G, false);
-    // bytes of one line in the input: N complex, or r2r_n reals (at most 2N of them)
-    const unsigned LINE_BYTES = MODE == REG_R2R ? (unsigned)(rp.r2r_n * sizeof(T)) : (unsigned)(N * sizeof(cplx<T>));
+    // bytes of one line in the input: N complex (C2C, R2C_HALF), N+1 bins (C2R_HALF), or
+    // r2r_n reals (R2R, at most 2N of them)
+    const unsigned LINE_BYTES = MODE == REG_R2R        ? (unsigned)(rp.r2r_n * sizeof(T))
+                                : MODE == REG_C2R_HALF ? (unsigned)((N + 1) * sizeof(cplx<T>))
+                                                       : (unsigned)(N * sizeof(cplx<T>));
     const unsigned GROUP_BYTES = G * LINE_BYTES;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem_raw);
     cplx<T> *buf = reinterpret_cast<cplx<T> *>(smem_raw + 128);
-    cplx<T> *xch = buf + G * N;
+    cplx<T> *xch = buf + G * (N + 1);
     const int g = threadIdx.x / TT, t = threadIdx.x - g * TT;
     cplx<T> *sline = xch + g * LS;
     const cplx<T> *tw = reinterpret_cast<const cplx<T> *>(rp.tw);
@@ -514,6 +529,10 @@ __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __g
         if (MODE == REG_R2R) {
             const T *xs = reinterpret_cast<const T *>(buf) + g * rp.r2r_n;
             r2r_load_all<T, N, E>(rp, [&](int j) { return xs[j]; }, t, v);
+        } else if (MODE == REG_C2R_HALF) {
+            const cplx<T> *xs = buf + g * (N + 1);
+#pragma unroll
+            for (int m = 0; m < E; m++) v[m] = c2r_half_point<T, N>(rp, [&](int j) { return xs[j]; }, t + m * TT);
         } else {
 #pragma unroll
             for (int m = 0; m < E; m++) {
@@ -530,6 +549,7 @@ __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __g
         }
         stages<T, N, E, MODE, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
         if (MODE == REG_R2R && io.valid) r2r_store_all<T, N, E, true>(rp, reinterpret_cast<T *>(rp.out) + io.out_base, t, v);
+        if (MODE == REG_R2C_HALF) r2c_half_epilogue<T, N, E>(rp, v, t, sline, io.out_base, io.valid);
     }
     // never leave with a bulk copy still writing this CTA's shared memory
     if (threadIdx.x == 0 && in_flight && !bar_wait(bar, parity)) atomicOr(rp.err, 64);
@@ -553,7 +573,7 @@ struct RegVariant {
 // persistent contiguous lines: barrier slot + one group buffer + the exchange buffer
 #define RVP(T, MODE, N, E, G, MINB, ...)                                                                    \
     {sizeof(T) == 8, N, MODE, 0, G *(N / E), G,                                                             \
-     128 + (size_t)G * N * sizeof(T) * 2 + (size_t)G * regk::reg_ls<T>(N, E, G, false) * sizeof(T) * 2,     \
+     128 + (size_t)G * (N + 1) * sizeof(T) * 2 + (size_t)G * regk::reg_ls<T>(N, E, G, false) * sizeof(T) * 2, \
      (const void *)regk::reg_fft_persistent<T, N, E, G, MINB, MODE, __VA_ARGS__>, {__VA_ARGS__}, 1}
 #define RVP_ALL(T, MODE)                                                                                    \
     RVP(T, MODE, 256, 16, 16, 3, 16, 16), RVP(T, MODE, 512, 16, 8, 3, 16, 16, 2),                           \
@@ -615,6 +635,7 @@ static const RegVariant kRegVariants[] = {
     // (blocks per SM asked of the register allocator: the shared-memory limit)
     RVP_ALL(float, REG_C2C),
     RVP_ALL(float, REG_R2R),
+    RVP_ALL(float, REG_C2R_HALF),
     // (f64 groups need twice the buffer and registers: one CTA per SM, slower than the
     // ordinary kernel's two, so f64 keeps the ordinary variants)
 };
@@ -638,7 +659,7 @@ int reg_variant_for(bool is_double, size_t n, int mode, bool strided) {
 // radices and lines per CTA), or -1.
 int reg_variant_persistent_twin(int v) {
     const RegVariant &a = kRegVariants[v];
-    if ((a.mode != REG_C2C && a.mode != REG_R2R) || a.strided || a.persistent) return -1;
+    if ((a.mode != REG_C2C && a.mode != REG_R2R && a.mode != REG_C2R_HALF) || a.strided || a.persistent) return -1;
     for (int i = 0; i < (int)(sizeof(kRegVariants) / sizeof(kRegVariants[0])); i++) {
         const RegVariant &b = kRegVariants[i];
         if (b.persistent && b.mode == a.mode && b.is_double == a.is_double && b.n == a.n && b.g == a.g &&
