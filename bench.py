@@ -251,7 +251,7 @@ def run_ours(args):
         host_spec_t, spec = pinned()
         host_back_t, back = pinned()
         host_in_t.copy_(a.reshape(-1).cpu())
-        e2e_steps = max(1, min(args.steps, 3))
+        e2e_steps = max(1, min(args.steps, 10))  # host-side timing: enough steps to average PCIe noise
         ctx.execute_transform(fwd, x_host, out=spec)  # warm the staging buffers
         torch.cuda.synchronize()
         if dist:

@@ -427,7 +427,14 @@ void execute_transform_host(Context *ctx, Transform &t_in, const void *in, size_
     }
     const size_t in_need = prog.input_bytes(), out_need = prog.output_bytes();
     const size_t batch = t.plan.config.kernel_preparation_system_count();
-    constexpr size_t kChunkBytes = size_t(128) << 20;  // input bytes per sub-batch
+    // input bytes per sub-batch: small enough that the unoverlapped first upload and last
+    // download of a call stay short, large enough that each copy runs at full PCIe rate
+    // (B200FFT_HOST_CHUNK_MB overrides the 32 MiB default)
+    static const size_t kChunkBytes = [] {
+        const char *e = std::getenv("B200FFT_HOST_CHUNK_MB");
+        const long mb = e ? std::atol(e) : 32;
+        return size_t(mb > 0 ? mb : 32) << 20;
+    }();
     const size_t in_per = batch ? in_need / batch : 0, out_per = batch ? out_need / batch : 0;
     const size_t chunk = in_per ? std::max<size_t>(1, kChunkBytes / in_per) : 0;
     Transform *ct = nullptr, *rt = nullptr;

@@ -49,7 +49,7 @@ struct Context {
     std::thread worker;
     bool stopping = false;
     // pipelined host execution: streams and per-slot staging (input, output, scratch)
-    static constexpr int kPipeSlots = 3;
+    static constexpr int kPipeSlots = 4;
     cudaStream_t pipe[kPipeSlots] = {};
     void *pipe_buf = nullptr;
     size_t pipe_bytes = 0;
