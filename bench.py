@@ -322,6 +322,8 @@ WORKLOADS = {
     "c2c-65537-f32": dict(kind="c2c", dims=[65537], batch=2048, prec="F32", config=4),
     "c2c-65537-f64": dict(kind="c2c", dims=[65537], batch=2048, prec="F64", config=4),
     "conv-2048": dict(kind="conv", dims=[2048, 2048], batch=64, prec="F32", config=5),
+    # small 2D case (512 MB): one contiguous and one strided 1024-point axis (profiling)
+    "c2c-1024^2x64": dict(kind="c2c", dims=[1024, 1024], batch=64, prec="F32", config=3),
     # DCT / DST (not a headline config): forward DCT-II + normalised inverse (DCT-III)
     "dct2-4096-f32": dict(kind="r2r", r2r="DCT2", dims=[4096], batch=16384, prec="F32", config=0),
     "dct2-4096-f64": dict(kind="r2r", r2r="DCT2", dims=[4096], batch=8192, prec="F64", config=0),
