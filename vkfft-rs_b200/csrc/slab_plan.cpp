@@ -27,9 +27,12 @@ void mark_exchange_pass(Program &prog, size_t first, int out_buf) {
     if (pp.dst_buf != out_buf || pp.dst_off != 0) fail_runtime("slab exchange pass does not write the axis output");
     pp.peer_scatter = true;
     if (pp.kernel == KERNEL_REG) {
-        const int twin = reg_variant_peer_twin(pp.reg_variant);
+        // from the ordinary variant: a persistent twin has no peer-scatter form, and its
+        // misaligned-input fallback must not be the non-scattering kernel
+        const int twin = reg_variant_peer_twin(pp.reg_variant_plain >= 0 ? pp.reg_variant_plain : pp.reg_variant);
         if (twin < 0) fail_runtime("slab exchange pass has no peer-scatter register kernel");
         pp.reg_variant = twin;
+        pp.reg_variant_plain = -1;
         pp.peer_es = pp.rp.dst.es;
         return;
     }
