@@ -53,7 +53,7 @@ bool stage_radix_supported(int r) { return (r >= 2 && r <= 13) || r == 16; }
 std::string jit_pass_source(const PassPlan &pp, int scalar_kind) {
     const PassParams &p = pp.p;
     std::ostringstream o;
-    o << "#include \"pass_device.cuh\"\nusing namespace b200fft;\n"
+    o << "#define B200FFT_NT " << pp.threads << "\n#include \"pass_device.cuh\"\nusing namespace b200fft;\n"
       << "extern \"C\" __global__ void __launch_bounds__(" << pp.threads
       << ") b200fft_pass(const __grid_constant__ PassParams p) {\n"
       << "  typedef " << (scalar_kind == 2 ? "b200fft::dd" : scalar_kind == 1 ? "double" : "float") << " T;\n"

@@ -14,6 +14,17 @@
 #include "dd.cuh"
 #include "pass_desc.hpp"
 
+// Threads of the CTA: the run-time specialised kernels define it as the pass's literal
+// thread count, so every op loop below has a compile-time stride and trip count (the
+// compiler unrolls the rounds and overlaps their loads); the precompiled interpreter
+// reads blockDim.x.
+#ifndef B200FFT_NT
+#define B200FFT_NT blockDim.x
+#define B200FFT_STAGE_UNROLL
+#else
+#define B200FFT_STAGE_UNROLL _Pragma("unroll")
+#endif
+
 namespace b200fft {
 
 template <typename T> struct vec2;
@@ -121,12 +132,12 @@ __device__ __forceinline__ void op_load(const PassShape &p, const Op &op, cplx<T
     const int total = G * len;
     const Side &s = p.in;
     const bool efast = s.es == 1;
-    for (int f0 = 0; f0 < total; f0 += kLoadUnroll * blockDim.x) {
+    for (int f0 = 0; f0 < total; f0 += kLoadUnroll * B200FFT_NT) {
         cplx<T> v[kLoadUnroll];
         int dst[kLoadUnroll];
 #pragma unroll
         for (int u = 0; u < kLoadUnroll; u++) {
-            const int f = f0 + threadIdx.x + u * blockDim.x;
+            const int f = f0 + threadIdx.x + u * B200FFT_NT;
             dst[u] = -1;
             v[u] = {T(0), T(0)};
             if (f < total) {
@@ -176,7 +187,7 @@ __device__ __forceinline__ void op_store(const PassShape &p, const Op &op, const
     const int total = G * len;
     const Side &s = p.out;
     const bool efast = s.es == 1;
-    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+    for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         int g, e;
         if (efast) {
             g = fdiv(f, op.div_a);
@@ -216,7 +227,8 @@ __device__ __forceinline__ void op_stage(const Op &op, cplx<T> *sm) {
     const int NBL = op.len / R;
     const int NB = op.nsub * NBL;
     const int P = op.P;
-    for (int b = threadIdx.x; b < NB; b += blockDim.x) {
+    B200FFT_STAGE_UNROLL
+    for (int b = threadIdx.x; b < NB; b += B200FFT_NT) {
         const int s = fdiv(b, op.div_a);
         const int bb = b - s * NBL;
         const int j = bb - (int)fdiv(bb, op.div_b) * P;
@@ -262,7 +274,7 @@ __device__ __forceinline__ void op_mul(const Op &op, cplx<T> *sm, const LineMeta
     const int len = op.len;
     const int total = op.nsub * len;
     const bool line_fast = op.flags & F_LINE_FAST;
-    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+    for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         int s, e;
         if (line_fast) {
             e = fdiv(f, op.div_b);
@@ -312,7 +324,7 @@ __device__ __forceinline__ void op_r2c_post(const PassShape &p, const Op &op, cp
     const int h = op.len;
     const int per = h / 2 + 1;
     const int total = p.G * per;
-    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+    for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         const int g = f / per;
         const int k = f - g * per;
         cplx<T> *z = sm + op.src_base + g * op.sub_stride;
@@ -348,7 +360,7 @@ __device__ __forceinline__ void op_c2r_pre(const PassShape &p, const Op &op, cpl
     const int total = p.G * per;
     const T sc = (op.flags & F_SCALE) ? kc<T>(op.scale, op.scale_lo) : T(1);
     const bool conj_out = op.flags & F_CONJ_OUT;
-    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+    for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         const int g = f / per;
         const int k = f - g * per;
         cplx<T> *z = sm + op.src_base + g * op.sub_stride;
@@ -386,7 +398,7 @@ __device__ __forceinline__ void op_rader_gather(const Op &op, cplx<T> *sm) {
     const int tstep = op.len / (P * pr);
     const int *perm = reinterpret_cast<const int *>(op.lut2);
     const int total = NB * pr;
-    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+    for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         const int b = fdiv(f, op.div_c);
         const int m = f - b * pr;
         const int s = fdiv(b, op.div_a);
@@ -416,7 +428,7 @@ __device__ __forceinline__ void op_rader_scatter(const Op &op, cplx<T> *sm) {
     const int total = NB * pr;
     const bool direct = op.flags & F_DIRECT;
     const bool conj_in = op.flags & F_CONJ_IN;
-    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+    for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         const int b = fdiv(f, op.div_c);
         const int m = f - b * pr;
         const int s = fdiv(b, op.div_a);
@@ -467,7 +479,7 @@ __device__ __forceinline__ void op_herm_expand(const PassShape &p, const Op &op,
     const int per = n - lo;
     if (per <= 0) return;
     const int total = p.G * per;
-    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+    for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         const int g = f / per;
         const int k = lo + (f - g * per);
         cplx<T> *z = sm + op.src_base + g * op.sub_stride;
@@ -482,7 +494,7 @@ __device__ __forceinline__ void op_permute_gather(const Op &op, cplx<T> *sm) {
     const int pr = op.radix;
     const int *perm = reinterpret_cast<const int *>(op.lut2);
     const int total = op.nsub * pr;
-    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+    for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         const int g = fdiv(f, op.div_c);
         const int m = f - g * pr;
         const int q = m < pr - 1 ? __ldg(perm + m) : 0;
@@ -493,7 +505,7 @@ __device__ __forceinline__ void op_permute_gather(const Op &op, cplx<T> *sm) {
 // line[slot] = line[0] for every line of the src region.
 template <typename T>
 __device__ __forceinline__ void op_save_dc(const Op &op, cplx<T> *sm) {
-    for (int g = threadIdx.x; g < op.nsub; g += blockDim.x)
+    for (int g = threadIdx.x; g < op.nsub; g += B200FFT_NT)
         sm[op.src_base + g * op.sub_stride + spad(op.nfull)] = sm[op.src_base + g * op.sub_stride];
 }
 
@@ -504,7 +516,7 @@ __device__ __forceinline__ void op_permute_scatter(const Op &op, cplx<T> *sm) {
     const int pr = op.radix;
     const int *ginv = reinterpret_cast<const int *>(op.lut3);
     const int total = op.nsub * pr;
-    for (int f = threadIdx.x; f < total; f += blockDim.x) {
+    for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         const int g = fdiv(f, op.div_c);
         const int m = f - g * pr;
         const cplx<T> *src = sm + op.src_base + g * op.sub_stride;
@@ -541,7 +553,7 @@ __device__ __forceinline__ LineMeta pass_prologue(const PassShape &p, unsigned c
     const int64_t l0 = (int64_t)blockIdx.x * p.G;
     const int64_t rem = p.nlines - l0;
     LineMeta lm{ib, ob, col, oidx, (int)(rem < p.G ? rem : p.G)};
-    for (int g = threadIdx.x; g < p.G; g += blockDim.x) {
+    for (int g = threadIdx.x; g < p.G; g += B200FFT_NT) {
         int64_t l = l0 + g;
         if (g >= lm.nl) l = l0;  // padding lines: any valid address, never read or written
         const int64_t i = l % p.ni;
