@@ -1213,7 +1213,65 @@ int table_r2r(Program &prog, int type, size_t n, size_t L) {
     return add_table(prog, key, std::move(t));
 }
 
+// [W_n^k | W_4n^k], k = 0..n/2: the even-half and rotation twiddles of REG_R2R_HALF.
+static int table_r2r_half(Program &prog, size_t n) {
+    std::string key = "r2rh" + std::to_string(n);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    const size_t h = n / 2;
+    HostTable t;
+    t.c.resize(2 * (h + 1));
+    for (size_t k = 0; k <= h; k++) {
+        put_root(t, prog, k, k, n);
+        put_root(t, prog, h + 1 + k, k, 4 * n);
+    }
+    return add_table(prog, key, std::move(t));
+}
+
+// DCT/DST-II/III of contiguous even-length lines: the reduction's real length-n sequence
+// through the even-half algebra, one register pass with an FFT of length n/2.
+static bool lower_r2r_half_register(Program &prog, const R2rAxisJob &job) {
+    const int type = job.kind & 3;
+    const size_t n = job.n, h = n / 2;
+    // f32 only: the f64 even-half variants need ~145 registers and measured slower than the
+    // full-length REG_R2R pass
+    if ((type != 1 && type != 2) || job.inner != 1 || n % 2 || !is_pow2(h) || !reg_kernels_enabled() || !job.alg ||
+        job.alg->kind != AlgorithmKind::Stockham || prog.is_double)
+        return false;
+    const int rv = reg_variant(prog, h, REG_R2R_HALF, false);
+    if (rv < 0) return false;
+    PassPlan pp{};
+    pp.kernel = KERNEL_REG;
+    pp.reg_variant = rv;
+    pp.reg_table = table_reg_twiddles(prog, h, rv);
+    pp.reg_table2 = table_r2r_half(prog, n);
+    pp.rp.nlines = job.outer;
+    pp.rp.ni = 1;
+    pp.rp.src = pp.rp.dst = RegSide{(int64_t)n, 0, 1};
+    pp.rp.scale = job.scale;
+    pp.rp.conj = type == 2 ? 1 : 0;
+    pp.rp.n = (int32_t)h;
+    pp.rp.r2r_kind = job.kind;
+    pp.rp.r2r_n = (int32_t)n;
+    pp.reg_in_real = pp.reg_out_real = true;
+    pp.src_buf = job.in_buf;
+    pp.dst_buf = job.out_buf;
+    pp.label = "register dct/dst even-half";
+    if ((n * (size_t)prog.rbytes()) % 16 == 0) {
+        const int pv = reg_variant_persistent_twin(rv);
+        if (pv >= 0) {
+            pp.reg_variant_plain = rv;
+            pp.reg_variant = pv;
+            pp.label = "register dct/dst even-half (bulk prefetch)";
+        }
+    }
+    for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
+    prog.passes.push_back(pp);
+    return true;
+}
+
 bool lower_r2r_axis_register(Program &prog, const R2rAxisJob &job) {
+    if (lower_r2r_half_register(prog, job)) return true;
     const size_t L = job.L;
     if (!is_pow2(L) || !reg_kernels_enabled() || !job.alg || job.alg->kind != AlgorithmKind::Stockham) return false;
     if (job.n > (size_t)INT32_MAX / 4) return false;

@@ -221,6 +221,106 @@ __device__ __forceinline__ void r2r_store_all(const RegParams &rp, T *out, int t
     }
 }
 
+// REG_R2R_HALF (N = h, the line holds n = 2h reals).  The II/III reductions of
+// r2r_ir.rs:1282-1500 run a real length-n sequence through a complex FFT; here that
+// sequence goes through the even-half algebra of the real FFT (real_ir.rs:1002-1013,
+// 1087-1100) so the FFT has length h.  With A = W_n^k and B = W_4n^k (k = 0..h):
+//   II:  z[p] = (v[2p], v[2p+1]) of the even-odd reorder v (odd sources negated for DST);
+//        after FFT_h, V[p] = 1/2((Z[p] + conj Z[h-p]) - i A[p] (Z[p] - conj Z[h-p])) and
+//        u = B[p] V[p] give X[p] = 2 Re u, X[n-p] = -2 Im u (DST: X at n-1-k).
+//   III: V[k] = (a_k - i b_k) conj B[k] (a, b = x[k], x[n-k]; DST x[n-1-k], x[k-1]);
+//        Z[p] = (V[p] + conj V[h-p]) + i conj A[p] (V[p] - conj V[h-p]); the inverse FFT_h
+//        gives v[2p] + i v[2p+1], stored unreordered (odd outputs negated for DST).
+template <typename T, int N, int E, typename At>
+__device__ __forceinline__ void r2r_half_load_all(const RegParams &rp, At at, int t, cplx<T> (&v)[E]) {
+    constexpr int TT = N / E;
+    constexpr int n = 2 * N;
+    const bool dst = rp.r2r_kind >= 4;
+    const cplx<T> *A = reinterpret_cast<const cplx<T> *>(rp.tw2);
+    const cplx<T> *B = A + (N + 1);
+    if ((rp.r2r_kind & 3) == 1) {
+        auto src = [&](int mm) { return mm < N ? 2 * mm : 2 * (n - mm) - 1; };
+#pragma unroll
+        for (int m = 0; m < E; m++) {
+            const int p = t + m * TT;
+            const int s0 = src(2 * p), s1 = src(2 * p + 1);
+            T a = at(s0), b = at(s1);
+            if (dst) {
+                if (s0 & 1) a = -a;
+                if (s1 & 1) b = -b;
+            }
+            v[m] = {a, b};
+        }
+    } else {
+        auto Vk = [&](int k) {
+            const T a = dst ? at(n - 1 - k) : at(k);
+            const T b = k == 0 ? T(0) : (dst ? at(k - 1) : at(n - k));
+            const cplx<T> w = tw_load(B, k);
+            return mul(cplx<T>{a, -b}, cplx<T>{w.x, -w.y});
+        };
+#pragma unroll
+        for (int m = 0; m < E; m++) {
+            const int p = t + m * TT;
+            const cplx<T> vp = Vk(p), vq = Vk(N - p);
+            const cplx<T> sm = {vp.x + vq.x, vp.y - vq.y}, df = {vp.x - vq.x, vp.y + vq.y};
+            const cplx<T> wa = tw_load(A, p);
+            const cplx<T> r = mul(cplx<T>{wa.x, -wa.y}, df);
+            v[m] = {sm.x - r.y, sm.y + r.x};
+        }
+    }
+    if (rp.conj) {
+#pragma unroll
+        for (int m = 0; m < E; m++) v[m].y = -v[m].y;
+    }
+}
+
+template <typename T, int N, int E>
+__device__ __forceinline__ void r2r_half_epilogue(const RegParams &rp, cplx<T> (&v)[E], int t, cplx<T> *sline,
+                                                  T *out, bool valid) {
+    constexpr int TT = N / E;
+    constexpr int n = 2 * N;
+    const bool dst = rp.r2r_kind >= 4;
+    const T s = T(rp.scale);
+    const cplx<T> *A = reinterpret_cast<const cplx<T> *>(rp.tw2);
+    const cplx<T> *B = A + (N + 1);
+    if ((rp.r2r_kind & 3) == 1) {
+        __syncthreads();  // the last stage's shared-memory reads are done
+#pragma unroll
+        for (int m = 0; m < E; m++) sline[pad(t + m * TT)] = v[m];
+        __syncthreads();
+        if (!valid) return;
+        auto put = [&](int k, T x) { __stcs(out + (dst ? n - 1 - k : k), x * s); };
+        auto post = [&](cplx<T> a, cplx<T> bc, int kk) {
+            const cplx<T> b = {bc.x, -bc.y};
+            const cplx<T> r = mul(tw_load(A, kk), cplx<T>{a.x - b.x, a.y - b.y});
+            return cplx<T>{T(0.5) * (a.x + b.x + r.y), T(0.5) * (a.y + b.y - r.x)};
+        };
+#pragma unroll
+        for (int m = 0; m < E; m++) {
+            const int p = t + m * TT;
+            const cplx<T> zq = sline[pad((N - p) & (N - 1))];
+            const cplx<T> u = mul(tw_load(B, p), post(v[m], zq, p));
+            put(p, T(2) * u.x);
+            if (p != 0) put(n - p, T(-2) * u.y);
+            if (p == 0) put(N, T(2) * mul(tw_load(B, N), post(v[m], v[m], N)).x);
+        }
+    } else {
+        if (!valid) return;
+        auto put = [&](int mm, T x) {
+            const int k = mm < N ? 2 * mm : 2 * n - 2 * mm - 1;
+            __stcs(out + k, ((dst && (k & 1)) ? -x : x) * s);
+        };
+#pragma unroll
+        for (int m = 0; m < E; m++) {
+            const int p = t + m * TT;
+            cplx<T> z = v[m];
+            if (rp.conj) z.y = -z.y;
+            put(2 * p, z.x);
+            put(2 * p + 1, z.y);
+        }
+    }
+}
+
 // Store of one output point at line position p (last stage), per data mode.
 template <typename T, int N, int MODE>
 __device__ __forceinline__ void store_point(const RegParams &rp, const LineIO &io, int p, cplx<T> y) {
@@ -284,7 +384,7 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
             for (int q = 1; q < R; q++) x[q] = mul(x[q], w[q]);
         }
         dft<R, T>(x);
-        if (LAST && (MODE == REG_R2C_HALF || MODE == REG_CONV || MODE == REG_R2R)) {
+        if (LAST && (MODE == REG_R2C_HALF || MODE == REG_CONV || MODE == REG_R2R || MODE == REG_R2R_HALF)) {
             // output q of butterfly k sits at position t + (k + q NB) TT: back into v for
             // the post-processing epilogue
 #pragma unroll
@@ -384,7 +484,10 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
         const T *x = reinterpret_cast<const T *>(rp.in) + io.in_base;
         const int64_t es = STRIDED ? rp.src.es : 1;
         r2r_load_all<T, N, E>(rp, [&](int j) { return __ldcs(x + (int64_t)j * es); }, t, v);
-    } else if (MODE != REG_R2R && io.valid) {
+    } else if (MODE == REG_R2R_HALF && io.valid) {
+        const T *x = reinterpret_cast<const T *>(rp.in) + io.in_base;
+        r2r_half_load_all<T, N, E>(rp, [&](int j) { return __ldcs(x + j); }, t, v);
+    } else if (MODE != REG_R2R && MODE != REG_R2R_HALF && io.valid) {
 #pragma unroll
         for (int m = 0; m < E; m++) {
             const int p = t + m * TT;
@@ -441,6 +544,8 @@ __global__ void __launch_bounds__(G *(N / E)) reg_fft_kernel(const __grid_consta
     // peer stores are visible system-wide before the rank's exchange signal
     if (MODE == REG_C2C_PEER) __threadfence_system();
     if (MODE == REG_R2C_HALF) r2c_half_epilogue<T, N, E>(rp, v, t, sline, io.out_base, io.valid);
+    if (MODE == REG_R2R_HALF)
+        r2r_half_epilogue<T, N, E>(rp, v, t, sline, reinterpret_cast<T *>(rp.out) + io.out_base, io.valid);
 }
 
 // ---- persistent variant: bulk-copy prefetch of the next line group -------------------
@@ -482,7 +587,7 @@ __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __g
     constexpr int LS = reg_ls<T>(N, E, G, false);
     // bytes of one line in the input: N complex (C2C, R2C_HALF), N+1 bins (C2R_HALF), or
     // r2r_n reals (R2R, at most 2N of them)
-    const unsigned LINE_BYTES = MODE == REG_R2R        ? (unsigned)(rp.r2r_n * sizeof(T))
+    const unsigned LINE_BYTES = (MODE == REG_R2R || MODE == REG_R2R_HALF) ? (unsigned)(rp.r2r_n * sizeof(T))
                                 : MODE == REG_C2R_HALF ? (unsigned)((N + 1) * sizeof(cplx<T>))
                                                        : (unsigned)(N * sizeof(cplx<T>));
     const unsigned GROUP_BYTES = G * LINE_BYTES;
@@ -529,6 +634,9 @@ __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __g
         if (MODE == REG_R2R) {
             const T *xs = reinterpret_cast<const T *>(buf) + g * rp.r2r_n;
             r2r_load_all<T, N, E>(rp, [&](int j) { return xs[j]; }, t, v);
+        } else if (MODE == REG_R2R_HALF) {
+            const T *xs = reinterpret_cast<const T *>(buf) + g * rp.r2r_n;
+            r2r_half_load_all<T, N, E>(rp, [&](int j) { return xs[j]; }, t, v);
         } else if (MODE == REG_C2R_HALF) {
             const cplx<T> *xs = buf + g * (N + 1);
 #pragma unroll
@@ -550,6 +658,8 @@ __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __g
         stages<T, N, E, MODE, 1, 0, true, Rs...>(v, t, sline, tw, rp, io);
         if (MODE == REG_R2R && io.valid) r2r_store_all<T, N, E, true>(rp, reinterpret_cast<T *>(rp.out) + io.out_base, t, v);
         if (MODE == REG_R2C_HALF) r2c_half_epilogue<T, N, E>(rp, v, t, sline, io.out_base, io.valid);
+        if (MODE == REG_R2R_HALF)
+            r2r_half_epilogue<T, N, E>(rp, v, t, sline, reinterpret_cast<T *>(rp.out) + io.out_base, io.valid);
     }
     // never leave with a bulk copy still writing this CTA's shared memory
     if (threadIdx.x == 0 && in_flight && !bar_wait(bar, parity)) atomicOr(rp.err, 64);
@@ -631,11 +741,13 @@ static const RegVariant kRegVariants[] = {
     RV_CONTIG(double, REG_R2R),
     RV_STRIDED(float, REG_R2R),
     RV_STRIDED(double, REG_R2R),
+    RV_CONTIG(float, REG_R2R_HALF),
     // persistent twins of the contiguous C2C variants (bulk-copy prefetch)
     // (blocks per SM asked of the register allocator: the shared-memory limit)
     RVP_ALL(float, REG_C2C),
     RVP_ALL(float, REG_R2R),
     RVP_ALL(float, REG_C2R_HALF),
+    RVP_ALL(float, REG_R2R_HALF),
     // (f64 groups need twice the buffer and registers: one CTA per SM, slower than the
     // ordinary kernel's two, so f64 keeps the ordinary variants)
 };
@@ -659,7 +771,9 @@ int reg_variant_for(bool is_double, size_t n, int mode, bool strided) {
 // radices and lines per CTA), or -1.
 int reg_variant_persistent_twin(int v) {
     const RegVariant &a = kRegVariants[v];
-    if ((a.mode != REG_C2C && a.mode != REG_R2R && a.mode != REG_C2R_HALF) || a.strided || a.persistent) return -1;
+    if ((a.mode != REG_C2C && a.mode != REG_R2R && a.mode != REG_R2R_HALF && a.mode != REG_C2R_HALF) || a.strided ||
+        a.persistent)
+        return -1;
     for (int i = 0; i < (int)(sizeof(kRegVariants) / sizeof(kRegVariants[0])); i++) {
         const RegVariant &b = kRegVariants[i];
         if (b.persistent && b.mode == a.mode && b.is_double == a.is_double && b.n == a.n && b.g == a.g &&

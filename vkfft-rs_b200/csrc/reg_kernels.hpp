@@ -21,6 +21,9 @@ enum RegMode : int32_t {
     REG_R2R = 7,      // DCT/DST of one axis: the FFT reduction's pre-processing on load (reads the
                       // real line), the FFT of length N = L, the post-processing on store (writes
                       // the real line); tw2 holds the reduction's twiddles by FFT position
+    REG_R2R_HALF = 8, // DCT/DST-II/III of a contiguous line of n = 2N reals: the reduction's real
+                      // length-n sequence through the even-half algebra, FFT of length N;
+                      // tw2 = [W_n^k | W_4n^k], k = 0..N
 };
 
 // Line l = o * ni + i; element p of the line is at o*os + i*is + p*es (units of the
