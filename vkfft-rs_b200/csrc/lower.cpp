@@ -1257,7 +1257,9 @@ static bool lower_r2r_half_register(Program &prog, const R2rAxisJob &job) {
     pp.src_buf = job.in_buf;
     pp.dst_buf = job.out_buf;
     pp.label = "register dct/dst even-half";
-    if ((n * (size_t)prog.rbytes()) % 16 == 0) {
+    // type III (four reals per point) runs faster from the bulk-copied line; type II
+    // measured faster on the plain kernel
+    if (type == 2 && (n * (size_t)prog.rbytes()) % 16 == 0) {
         const int pv = reg_variant_persistent_twin(rv);
         if (pv >= 0) {
             pp.reg_variant_plain = rv;
