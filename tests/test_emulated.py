@@ -103,6 +103,13 @@ CASES = [
     dict(kind="kprep", dims=[64], batch=2, prec="F64", coords=3),
     dict(kind="kprep", dims=[60], batch=1, prec="F32", coords=2, real=True),
     dict(kind="kprep", dims=[16, 10], batch=2, prec="F64", coords=2, real=True),
+    # three-pass Bluestein on a contiguous axis (row-ordered spectrum / twiddle tables) and
+    # on a strided one
+    dict(kind="c2c", dims=[4099], batch=2, prec="F64"),
+    dict(kind="c2c", dims=[4099], batch=1, prec="F64", inverse=True, normalize=True),
+    dict(kind="c2c", dims=[65537], batch=1, prec="F32"),
+    dict(kind="c2c", dims=[3, 4099], batch=1, prec="F64"),
+    dict(kind="c2c", dims=[4099, 3], batch=1, prec="F64"),
     # DCT / DST (r2r_ir.rs): every kind, odd/even lengths, ND, inverse pairs, padding
     *[dict(kind="r2r", r2r=k, dims=[n], batch=3, prec=p) for k in
       ("DCT1", "DCT2", "DCT3", "DCT4", "DST1", "DST2", "DST3", "DST4") for n in (2, 17, 64) for p in ("F32", "F64")],

@@ -237,6 +237,24 @@ int table_bluestein_spectrum(Program &prog, size_t n, size_t m) {
     return add_table(prog, key, std::move(t));
 }
 
+// The Bluestein spectrum in the row order of a three-pass convolution: entry k1 M2 + k2
+// holds spectrum[k1 + M1 k2] (the rows of the middle pass are then read contiguously).
+int table_bluestein_spectrum_rows(Program &prog, size_t n, size_t m, size_t m1, size_t m2) {
+    std::string key = "bspecrows" + std::to_string(n) + "_" + std::to_string(m) + "_" + std::to_string(m1);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    const HostTable &src = prog.tables[table_bluestein_spectrum(prog, n, m)];
+    HostTable t;
+    t.c.resize(m);
+    if (!src.lo.empty()) t.lo.resize(m);
+    for (size_t k1 = 0; k1 < m1; k1++)
+        for (size_t k2 = 0; k2 < m2; k2++) {
+            t.c[k1 * m2 + k2] = src.c[k1 + m1 * k2];
+            if (!src.lo.empty()) t.lo[k1 * m2 + k2] = src.lo[k1 + m1 * k2];
+        }
+    return add_table(prog, key, std::move(t));
+}
+
 // Accurate host mixed-radix FFT (Stockham, twiddles from long double), used only to
 // build kernel spectra.  O(n * sum of prime factors).
 void host_fft_inplace(std::vector<std::complex<double>> &x, bool inverse) {
@@ -1124,6 +1142,9 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     const int spec = table_bluestein_spectrum(prog, N, M);
     const int64_t scr_os = (int64_t)M * S;
     prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * M * S));
+    // contiguous axis (S = 1): the rows of pass B are contiguous in scratch and its threads
+    // walk elements, so its spectrum and twiddle tables are laid out row by row
+    const bool rows_contig = S == 1;
     // pass A: columns n2: x[n2 + M2 n1] * chirp (n < N, else 0), FFT over n1, * W_M^{n2 k1}
     {
         PassBuilder b(prog, (int)M1, line_stages(M1, nullptr), true, no * S * M2, kMaxOps);
@@ -1141,10 +1162,17 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
         PassBuilder b(prog, (int)M2, line_stages(M2, nullptr), true, no * S * M1, kMaxOps);
         b.load((int)M2, 0);
         b.fft();
-        b.mul_region(spec, F_CONJ_OUT, 1, (int)M1);
+        if (rows_contig)
+            b.mul_region(table_bluestein_spectrum_rows(prog, N, M, M1, M2), F_CONJ_OUT, (int)M2, 1);
+        else
+            b.mul_region(spec, F_CONJ_OUT, 1, (int)M1);
         b.fft();
-        b.store((int)M2, F_CONJ_IN | F_CONJ_LUT, MUL_TWIDDLE_CE, table_twiddle_transposed(prog, M1, M2, M), 1.0,
-                (int)M1, 1);
+        if (rows_contig)  // W_M^{k1 n2} at k1 M2 + n2
+            b.store((int)M2, F_CONJ_IN | F_CONJ_LUT, MUL_TWIDDLE_CE, table_twiddle_transposed(prog, M2, M1, M), 1.0,
+                    1, (int)M2);
+        else
+            b.store((int)M2, F_CONJ_IN | F_CONJ_LUT, MUL_TWIDDLE_CE, table_twiddle_transposed(prog, M1, M2, M), 1.0,
+                    (int)M1, 1);
         prog.passes.push_back(b.finish(no, S, (int64_t)M1,
                                        make_side(scr_os, 1, (int64_t)M2 * S, S, false, M, (int)M2, 1),
                                        make_side(scr_os, 1, (int64_t)M2 * S, S, false, M, (int)M2, 1), BUF_SCRATCH0,

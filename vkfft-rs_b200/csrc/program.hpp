@@ -131,6 +131,7 @@ int table_twiddle(Program &prog, size_t n);
 int table_reg_twiddles(Program &prog, size_t n, int variant);
 int table_bluestein_chirp(Program &prog, size_t n);
 int table_bluestein_spectrum(Program &prog, size_t n, size_t m);
+int table_bluestein_spectrum_rows(Program &prog, size_t n, size_t m, size_t m1, size_t m2);
 int table_r2r(Program &prog, int type, size_t n, size_t L);  // DCT/DST reduction twiddles [A | B]
 void host_fft_inplace(std::vector<std::complex<double>> &x, bool inverse);
 
