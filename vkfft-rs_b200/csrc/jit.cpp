@@ -78,7 +78,7 @@ std::string jit_pass_source(const PassPlan &pp, int scalar_kind) {
           << "; op.sub_stride = " << op.sub_stride << "; op.mul = " << op.mul << "; op.cm = " << op.cm
           << "; op.em = " << op.em << ";\n"
           << "    op.w_base = " << op.w_base << "; op.w_stride = " << op.w_stride << "; op.x0_base = " << op.x0_base
-          << "; op.nfull = " << op.nfull << ";\n"
+          << "; op.nfull = " << op.nfull << "; op.pad_shift = " << op.pad_shift << ";\n"
           << "    op.div_a = " << fastdiv_literal(op.div_a) << "; op.div_b = " << fastdiv_literal(op.div_b)
           << "; op.div_c = " << fastdiv_literal(op.div_c) << ";\n";
         std::snprintf(num, sizeof num, "%a", op.scale);

@@ -534,6 +534,85 @@ bool line_fits_on_chip(int ce, size_t L, const AxisAlgorithm *alg, bool strided)
     return shape_pass(ce, (int)L, line_stages(L, alg), strided, 1 << 20, kMaxOps, sh);
 }
 
+// ---- shared-memory layout choice ------------------------------------------------------
+// Wavefronts of one warp access to 8-byte (complex f32) or 16-byte slots: the largest
+// number of distinct 4-byte rows any bank is asked for.
+static int bank_wavefronts(const int *slot, int n, int words) {
+    int rows[32][16];
+    int cnt[32] = {};
+    int worst = 0;
+    for (int i = 0; i < n; i++)
+        for (int w = 0; w < words; w++) {
+            const int word = slot[i] * words + w, bank = word & 31, row = word >> 5;
+            bool seen = false;
+            for (int k = 0; k < cnt[bank]; k++) seen |= rows[bank][k] == row;
+            if (!seen && cnt[bank] < 16) rows[bank][cnt[bank]++] = row;
+            worst = std::max(worst, cnt[bank]);
+        }
+    return worst;
+}
+
+// Modelled shared-memory wavefronts of a Stockham-only pass (radix stages between the
+// two line buffers, an element-fast and a line-fast load/store) for a padding shift and
+// line stride: the same index arithmetic as op_stage / op_load / op_store, over the first
+// warps of every access pattern.
+static long smem_cost(const std::vector<StageSpec> &stages, int L, int G, int threads, int shift, int ls, int words) {
+    auto spad = [&](int e) { return e + (e >> shift); };
+    long cost = 0;
+    int slot[32];
+    int P = 1;
+    const int kWarps = 24;
+    for (const StageSpec &st : stages) {
+        const int R = st.radix, NBL = L / R, NB = G * NBL;
+        for (int w = 0; w < kWarps && w * 32 < NB; w++)
+            for (int q = 0; q < R; q++) {
+                int n = 0, m = 0, wslot[32];
+                for (int l = 0; l < 32 && w * 32 + l < NB; l++, n++) {
+                    const int b = w * 32 + l, s = b / NBL, bb = b - s * NBL, j = bb % P;
+                    slot[n] = s * ls + spad(bb + q * NBL);
+                    wslot[m++] = G * ls + s * ls + spad((bb - j) * R + j + q * P);
+                }
+                cost += bank_wavefronts(slot, n, words) + bank_wavefronts(wslot, m, words);
+            }
+        P *= R;
+    }
+    for (int pattern = 0; pattern < 2; pattern++)
+        for (int w = 0; w < kWarps && w * 32 < G * L; w++) {
+            int n = 0;
+            for (int l = 0; l < 32 && w * 32 + l < G * L; l++, n++) {
+                const int f = w * 32 + l;
+                const int g = pattern ? f % G : f / L, e = pattern ? f / G : f % L;
+                slot[n] = g * ls + spad(e);
+            }
+            cost += 2 * bank_wavefronts(slot, n, words);
+        }
+    (void)threads;
+    return cost;
+}
+
+// Padding shift (4 or unpadded) and line stride of a pass: the current layout unless the
+// model finds an unpadded one with fewer wavefronts that fits in the same stride budget.
+// Passes with Rader stages keep the padded layout their region sizes assume.
+static void choose_smem_layout(const std::vector<StageSpec> &stages, int L, int G, int threads, int words,
+                               int &shift, int &ls) {
+    shift = 4;
+    for (const StageSpec &st : stages)
+        if (st.rader || st.radix < 2 || L % st.radix) return;
+    if (stages.empty()) return;
+    const int ls0 = ls;
+    long best = smem_cost(stages, L, G, threads, 4, ls0, words);
+    // unpadded strides from L + 2 (ops address elements L and L + 1: the even-half post /
+    // pre-processing and the saved DC slot) within the padded stride, 65 candidates at most
+    for (int cand = L + 2; cand <= std::min(ls0, L + 66); cand++) {
+        const long c = smem_cost(stages, L, G, threads, 31, cand, words);
+        if (c < best) {
+            best = c;
+            shift = 31;
+            ls = cand;
+        }
+    }
+}
+
 // Builds the op program of one pass.
 class PassBuilder {
    public:
@@ -541,6 +620,7 @@ class PassBuilder {
         : prog_(prog), L_(L), stages_(std::move(stages)) {
         if (!shape_pass(prog.cbytes(), L, stages_, strided, nlines, std::max(nops_hint, (int)kMaxOps), sh_))
             fail_resource("B200 FFT pass shared memory", (size_t)L * 2 * prog.cbytes(), budget_bytes());
+        choose_smem_layout(stages_, L, sh_.G, sh_.threads, prog.cbytes() / 4, pad_shift_, sh_.ls);
         A_ = 0;
         B_ = sh_.G * sh_.ls;
         extra_base_ = 2 * sh_.G * sh_.ls;
@@ -555,6 +635,7 @@ class PassBuilder {
         Op &o = plan_.p.ops[nops_++];
         std::memset(&o, 0, sizeof(Op));
         o.type = type;
+        o.pad_shift = pad_shift_;
         return o;
     }
     void set_tables(int a, int b = -1, int c = -1) {
@@ -814,6 +895,7 @@ class PassBuilder {
     int L_;
     std::vector<StageSpec> stages_;
     CtaShape sh_;
+    int pad_shift_ = 4;  // shared-memory padding of the pass (choose_smem_layout)
     PassPlan plan_{};
     int nops_ = 0;
     int A_, B_, cur_, other_;

@@ -89,6 +89,8 @@ struct alignas(16) Op {
     int32_t w_stride;   // RADER: W sub-line stride
     int32_t x0_base;    // RADER / MUL(F_SAVE_DC): X0 region base, two slots per butterfly
     int32_t nfull;      // R2C/C2R/HERM_EXPAND: full real length N; MUL: only n < nfull (0: all)
+    int32_t pad_shift;  // shared-memory slot of element e: e + (e >> pad_shift) (31: unpadded);
+                        // one value for every op of a pass
     FastDiv div_a;      // STAGE: len/radix; RADER: len/p; LOAD/STORE/MUL: len
     FastDiv div_b;      // STAGE/RADER: P
     FastDiv div_c;      // RADER: p

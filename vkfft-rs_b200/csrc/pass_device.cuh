@@ -32,7 +32,9 @@ template <> struct vec2<float> { using type = float2; };
 template <> struct vec2<double> { using type = double2; };
 
 __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) { return (__umulhi(n, f.m) + n) >> f.s; }
-__device__ __forceinline__ int spad(int e) { return e + (e >> 4); }
+// Padded shared-memory slot of line element e (Op::pad_shift: one spare slot every
+// 2^shift elements, or none for shift 31).
+__device__ __forceinline__ int spad(int e, int shift) { return e + (e >> shift); }
 
 template <typename T> __device__ __forceinline__ cplx<T> cmul(cplx<T> a, cplx<T> b) {
     return {a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x};
@@ -149,7 +151,7 @@ __device__ __forceinline__ void op_load(const PassShape &p, const Op &op, cplx<T
                     e = fdiv(f, p.div_g);
                     g = f - e * G;
                 }
-                dst[u] = op.dst_base + g * op.sub_stride + spad(e);
+                dst[u] = op.dst_base + g * op.sub_stride + spad(e, op.pad_shift);
                 const int c = lm.col[g];
                 const int n = c * s.cm + e * s.em;
                 if (g < lm.nl && n < s.count) {
@@ -199,7 +201,7 @@ __device__ __forceinline__ void op_store(const PassShape &p, const Op &op, const
         const int c = lm.col[g];
         const int n = c * s.cm + e * s.em;
         if (g < lm.nl && n < s.count) {
-            cplx<T> v = sm[op.src_base + g * op.sub_stride + spad(e)];
+            cplx<T> v = sm[op.src_base + g * op.sub_stride + spad(e, op.pad_shift)];
             v = apply_mul(v, op, c, e, n);
             int64_t a = lm.ob[g] + (int64_t)e * s.es;
             void *dst = p.dst;
@@ -236,7 +238,7 @@ __device__ __forceinline__ void op_stage(const Op &op, cplx<T> *sm) {
         cplx<T> *dst = sm + op.dst_base + s * op.sub_stride;
         cplx<T> v[R];
 #pragma unroll
-        for (int q = 0; q < R; q++) v[q] = src[spad(bb + q * NBL)];
+        for (int q = 0; q < R; q++) v[q] = src[spad(bb + q * NBL, op.pad_shift)];
         if (P > 1) {
 #pragma unroll
             for (int q = 1; q < R; q++) v[q] = cmul(v[q], ld_ro<T>(op.lut, (q - 1) * P + j));
@@ -244,7 +246,7 @@ __device__ __forceinline__ void op_stage(const Op &op, cplx<T> *sm) {
         dft<R, T>(v);
         const int e0 = (bb - j) * R + j;
 #pragma unroll
-        for (int q = 0; q < R; q++) dst[spad(e0 + q * P)] = v[q];
+        for (int q = 0; q < R; q++) dst[spad(e0 + q * P, op.pad_shift)] = v[q];
     }
 }
 
@@ -283,7 +285,7 @@ __device__ __forceinline__ void op_mul(const Op &op, cplx<T> *sm, const LineMeta
             s = fdiv(f, op.div_a);
             e = f - s * len;
         }
-        cplx<T> *ptr = sm + op.src_base + s * op.sub_stride + spad(e);
+        cplx<T> *ptr = sm + op.src_base + s * op.sub_stride + spad(e, op.pad_shift);
         const cplx<T> v = *ptr;
         if ((op.flags & F_SAVE_DC) && e == 0) sm[op.x0_base + 2 * s + 1] = v;
         const int c = op.cm ? lm.col[s] : 0;
@@ -329,7 +331,7 @@ __device__ __forceinline__ void op_r2c_post(const PassShape &p, const Op &op, cp
         const int k = f - g * per;
         cplx<T> *z = sm + op.src_base + g * op.sub_stride;
         const int k2 = (h - k) % h;
-        const cplx<T> zk = z[spad(k % h)], zk2 = z[spad(k2)];
+        const cplx<T> zk = z[spad(k % h, op.pad_shift)], zk2 = z[spad(k2, op.pad_shift)];
         auto post = [&](cplx<T> a, cplx<T> bc, int kk) {
             const cplx<T> b = cconj(bc);
             const cplx<T> w = ld_ro<T>(op.lut2, kk);
@@ -339,14 +341,14 @@ __device__ __forceinline__ void op_r2c_post(const PassShape &p, const Op &op, cp
         };
         const cplx<T> xk = post(zk, zk2, k);
         if (k == 0) {
-            z[spad(0)] = xk;
-            z[spad(h)] = post(zk, zk, h);
+            z[spad(0, op.pad_shift)] = xk;
+            z[spad(h, op.pad_shift)] = post(zk, zk, h);
         } else if (k != h - k) {
             const cplx<T> xk2 = post(zk2, zk, h - k);
-            z[spad(k)] = xk;
-            z[spad(h - k)] = xk2;
+            z[spad(k, op.pad_shift)] = xk;
+            z[spad(h - k, op.pad_shift)] = xk2;
         } else {
-            z[spad(k)] = xk;
+            z[spad(k, op.pad_shift)] = xk;
         }
     }
 }
@@ -364,7 +366,7 @@ __device__ __forceinline__ void op_c2r_pre(const PassShape &p, const Op &op, cpl
         const int g = f / per;
         const int k = f - g * per;
         cplx<T> *z = sm + op.src_base + g * op.sub_stride;
-        const cplx<T> xa = z[spad(k)], xb = z[spad(h - k)];
+        const cplx<T> xa = z[spad(k, op.pad_shift)], xb = z[spad(h - k, op.pad_shift)];
         auto pre = [&](cplx<T> x, cplx<T> mc, int kk) {
             const cplx<T> m = cconj(mc);
             const cplx<T> w = cconj(ld_ro<T>(op.lut2, kk));
@@ -376,13 +378,13 @@ __device__ __forceinline__ void op_c2r_pre(const PassShape &p, const Op &op, cpl
         };
         const cplx<T> za = pre(xa, xb, k);
         if (k == 0) {
-            z[spad(0)] = za;
+            z[spad(0, op.pad_shift)] = za;
         } else if (k != h - k) {
             const cplx<T> zb = pre(xb, xa, h - k);
-            z[spad(k)] = za;
-            z[spad(h - k)] = zb;
+            z[spad(k, op.pad_shift)] = za;
+            z[spad(h - k, op.pad_shift)] = zb;
         } else {
-            z[spad(k)] = za;
+            z[spad(k, op.pad_shift)] = za;
         }
     }
 }
@@ -405,10 +407,10 @@ __device__ __forceinline__ void op_rader_gather(const Op &op, cplx<T> *sm) {
         const int bb = b - s * NBL;
         const int j = bb - (int)fdiv(bb, op.div_b) * P;
         const int q = m < pr - 1 ? __ldg(perm + m) : 0;
-        cplx<T> v = sm[op.src_base + s * op.sub_stride + spad(bb + q * NBL)];
+        cplx<T> v = sm[op.src_base + s * op.sub_stride + spad(bb + q * NBL, op.pad_shift)];
         if (P > 1 && q > 0) v = cmul(v, ld_ro<T>(op.lut, j * q * tstep));
         if (m < pr - 1)
-            sm[op.w_base + b * op.w_stride + spad(m)] = v;
+            sm[op.w_base + b * op.w_stride + spad(m, op.pad_shift)] = v;
         else
             sm[op.x0_base + 2 * b] = v;
     }
@@ -442,7 +444,7 @@ __device__ __forceinline__ void op_rader_scatter(const Op &op, cplx<T> *sm) {
             k = 0;
             if (direct) {
                 for (int q = 0; q < pr - 1; q++) {
-                    const cplx<T> a = w[spad(q)];
+                    const cplx<T> a = w[spad(q, op.pad_shift)];
                     acc.x += a.x;
                     acc.y += a.y;
                 }
@@ -455,18 +457,18 @@ __device__ __forceinline__ void op_rader_scatter(const Op &op, cplx<T> *sm) {
                 const int L1 = pr - 1;
                 int idx = m;
                 for (int q = 0; q < L1; q++) {
-                    const cplx<T> a = w[spad(q)];
+                    const cplx<T> a = w[spad(q, op.pad_shift)];
                     const cplx<T> bt = ld_ro<T>(op.lut, idx);
                     acc.x += a.x * bt.x - a.y * bt.y;
                     acc.y += a.x * bt.y + a.y * bt.x;
                     idx = idx == 0 ? L1 - 1 : idx - 1;
                 }
             } else {
-                acc = w[spad(m)];
+                acc = w[spad(m, op.pad_shift)];
                 if (conj_in) acc = cconj(acc);
             }
         }
-        sm[op.dst_base + s * op.sub_stride + spad((bb - j) * pr + j + k * P)] = {x0.x + acc.x, x0.y + acc.y};
+        sm[op.dst_base + s * op.sub_stride + spad((bb - j) * pr + j + k * P, op.pad_shift)] = {x0.x + acc.x, x0.y + acc.y};
     }
 }
 
@@ -483,7 +485,7 @@ __device__ __forceinline__ void op_herm_expand(const PassShape &p, const Op &op,
         const int g = f / per;
         const int k = lo + (f - g * per);
         cplx<T> *z = sm + op.src_base + g * op.sub_stride;
-        z[spad(k)] = cconj(z[spad(n - k)]);
+        z[spad(k, op.pad_shift)] = cconj(z[spad(n - k, op.pad_shift)]);
     }
 }
 
@@ -498,7 +500,7 @@ __device__ __forceinline__ void op_permute_gather(const Op &op, cplx<T> *sm) {
         const int g = fdiv(f, op.div_c);
         const int m = f - g * pr;
         const int q = m < pr - 1 ? __ldg(perm + m) : 0;
-        sm[op.dst_base + g * op.sub_stride + spad(m)] = sm[op.src_base + g * op.sub_stride + spad(q)];
+        sm[op.dst_base + g * op.sub_stride + spad(m, op.pad_shift)] = sm[op.src_base + g * op.sub_stride + spad(q, op.pad_shift)];
     }
 }
 
@@ -506,7 +508,7 @@ __device__ __forceinline__ void op_permute_gather(const Op &op, cplx<T> *sm) {
 template <typename T>
 __device__ __forceinline__ void op_save_dc(const Op &op, cplx<T> *sm) {
     for (int g = threadIdx.x; g < op.nsub; g += B200FFT_NT)
-        sm[op.src_base + g * op.sub_stride + spad(op.nfull)] = sm[op.src_base + g * op.sub_stride];
+        sm[op.src_base + g * op.sub_stride + spad(op.nfull, op.pad_shift)] = sm[op.src_base + g * op.sub_stride];
 }
 
 // Pass-level Rader scatter: from [c_0 .. c_{p-2}, x0, A0] (c conjugated when F_CONJ_IN),
@@ -520,15 +522,15 @@ __device__ __forceinline__ void op_permute_scatter(const Op &op, cplx<T> *sm) {
         const int g = fdiv(f, op.div_c);
         const int m = f - g * pr;
         const cplx<T> *src = sm + op.src_base + g * op.sub_stride;
-        const cplx<T> x0 = src[spad(pr - 1)];
+        const cplx<T> x0 = src[spad(pr - 1, op.pad_shift)];
         cplx<T> acc;
         int k;
         if (m < pr - 1) {
-            acc = src[spad(m)];
+            acc = src[spad(m, op.pad_shift)];
             if (op.flags & F_CONJ_IN) acc = cconj(acc);
             k = __ldg(ginv + m);
         } else {
-            acc = src[spad(pr)];
+            acc = src[spad(pr, op.pad_shift)];
             k = 0;
         }
         cplx<T> y = {x0.x + acc.x, x0.y + acc.y};
@@ -537,7 +539,7 @@ __device__ __forceinline__ void op_permute_scatter(const Op &op, cplx<T> *sm) {
             y.y *= kc<T>(op.scale, op.scale_lo);
         }
         if (op.flags & F_CONJ_OUT) y = cconj(y);
-        sm[op.dst_base + g * op.sub_stride + spad(k)] = y;
+        sm[op.dst_base + g * op.sub_stride + spad(k, op.pad_shift)] = y;
     }
 }
 
