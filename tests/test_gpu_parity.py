@@ -54,8 +54,9 @@ def test_c2c_1d_inverse_normalized(V, ctx, n, batch, prec):
 
 @pytest.mark.parametrize("prec", ["F32", "F64"])
 def test_c2c_large_four_step_and_bluestein_multipass(V, ctx, prec):
-    # 2^17 (four-step) and the BASELINE Bluestein N=65537 (device M=131220, three passes)
-    for n, batch in ((131072, 3), (65537, 2)):
+    # 2^17 and 2^19 (four-step; 2^19 is the reference's published large case) and the
+    # BASELINE Bluestein N=65537 (device M=131220, three passes)
+    for n, batch in ((131072, 3), (524288, 2), (65537, 2)):
         ir, err = run_c2c(V, ctx, [n], batch, prec, V.Direction.FORWARD, seed=7)
         assert err <= TOL[prec], (n, ir.axis_child(0), err)
 
