@@ -240,8 +240,28 @@ __device__ __forceinline__ void op_stage(const Op &op, cplx<T> *sm) {
 #pragma unroll
         for (int q = 0; q < R; q++) v[q] = src[spad(bb + q * NBL, op.pad_shift)];
         if (P > 1) {
+            // Large stage tables (and every f64 table) miss L1 next to the line buffers:
+            // only their power-of-two rows are read and w_q = w_{q - lowbit(q)} w_{lowbit(q)}
+            // forms the rest (at most three products deep).  Small f32 tables stay L1-resident
+            // and are read whole, which costs fewer issue slots than the products.
+            // Double-double reads every row (its products cost more than the loads).
+            if (sizeof(T) <= 8 && (sizeof(T) == 8 || (R - 1) * P >= 512)) {
+                cplx<T> w[R];
 #pragma unroll
-            for (int q = 1; q < R; q++) v[q] = cmul(v[q], ld_ro<T>(op.lut, (q - 1) * P + j));
+                for (int q = 1; q < R; q++) {
+                    if ((q & (q - 1)) == 0) {
+                        w[q] = ld_ro<T>(op.lut, (q - 1) * P + j);
+                    } else {
+                        const int lb = q & (-q);
+                        w[q] = cmul(w[q - lb], w[lb]);
+                    }
+                }
+#pragma unroll
+                for (int q = 1; q < R; q++) v[q] = cmul(v[q], w[q]);
+            } else {
+#pragma unroll
+                for (int q = 1; q < R; q++) v[q] = cmul(v[q], ld_ro<T>(op.lut, (q - 1) * P + j));
+            }
         }
         dft<R, T>(v);
         const int e0 = (bb - j) * R + j;
