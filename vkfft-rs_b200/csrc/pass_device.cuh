@@ -32,9 +32,10 @@ template <> struct vec2<float> { using type = float2; };
 template <> struct vec2<double> { using type = double2; };
 
 __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) { return (__umulhi(n, f.m) + n) >> f.s; }
-// Padded shared-memory slot of line element e (Op::pad_shift: one spare slot every
-// 2^shift elements, or none for shift 31).
-__device__ __forceinline__ int spad(int e, int shift) { return e + (e >> shift); }
+// Shared-memory slot of line element e >= 0 (Op::pad_shift: one spare slot every
+// 2^shift elements, or none for shift 31 -- the unpadded layout; pad_shift is a literal
+// in the specialised kernels, so the branch folds away there).
+__device__ __forceinline__ int spad(int e, int shift) { return shift >= 31 ? e : e + (e >> shift); }
 
 template <typename T> __device__ __forceinline__ cplx<T> cmul(cplx<T> a, cplx<T> b) {
     return {a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x};
@@ -231,7 +232,7 @@ __device__ __forceinline__ void op_stage(const Op &op, cplx<T> *sm) {
     const int P = op.P;
     B200FFT_STAGE_UNROLL
     for (int b = threadIdx.x; b < NB; b += B200FFT_NT) {
-        const int s = fdiv(b, op.div_a);
+        const int s = op.nsub == 1 ? 0 : (int)fdiv(b, op.div_a);
         const int bb = b - s * NBL;
         const int j = bb - (int)fdiv(bb, op.div_b) * P;
         const cplx<T> *src = sm + op.src_base + s * op.sub_stride;
@@ -423,7 +424,7 @@ __device__ __forceinline__ void op_rader_gather(const Op &op, cplx<T> *sm) {
     for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         const int b = fdiv(f, op.div_c);
         const int m = f - b * pr;
-        const int s = fdiv(b, op.div_a);
+        const int s = op.nsub == 1 ? 0 : (int)fdiv(b, op.div_a);
         const int bb = b - s * NBL;
         const int j = bb - (int)fdiv(bb, op.div_b) * P;
         const int q = m < pr - 1 ? __ldg(perm + m) : 0;
@@ -453,7 +454,7 @@ __device__ __forceinline__ void op_rader_scatter(const Op &op, cplx<T> *sm) {
     for (int f = threadIdx.x; f < total; f += B200FFT_NT) {
         const int b = fdiv(f, op.div_c);
         const int m = f - b * pr;
-        const int s = fdiv(b, op.div_a);
+        const int s = op.nsub == 1 ? 0 : (int)fdiv(b, op.div_a);
         const int bb = b - s * NBL;
         const int j = bb - (int)fdiv(bb, op.div_b) * P;
         const cplx<T> x0 = sm[op.x0_base + 2 * b];
