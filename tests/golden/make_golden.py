@@ -107,4 +107,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {os.path.relpath(__file__)} <vkfft-rs checkout>")
+    main(sys.argv[1])
