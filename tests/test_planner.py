@@ -16,6 +16,12 @@ def test_lib_rs_doc_example(V):
 
 def test_factorization_helpers(V):
     # planner.rs:748-752, 1098-1123
+    # prime_factorization(360) = [2, 2, 2, 3, 3, 5] (ascending, with multiplicity), seen
+    # through the Stockham axis plan; 47 is its own single factor (a Rader prime)
+    a = V.FftPlan.build(V.FftConfig([360])).axes[0]
+    assert a.kind == V.AlgorithmKind.STOCKHAM and a.radix.prime_factors == [2, 2, 2, 3, 3, 5]
+    p = V.FftPlan.build(V.FftConfig([47])).axes[0]
+    assert p.kind == V.AlgorithmKind.RADER and [r.prime for r in p.primes] == [47]
     assert V.next_smooth_at_least(2061) >= 2061
     v = V.next_smooth_at_least(2061)
     for c in range(2061, v):
