@@ -290,3 +290,30 @@ def test_validation_errors_match_reference(V):
     with pytest.raises(V.VkFftError) as e:
         V.FftPlan.build(V.FftConfig([8]).with_convolution(True))
     assert e.value.variant == "UnsupportedKernelPath"
+
+
+def test_bluestein_auto_padding_matches_fixed_upstream_boundaries(V):
+    """Bluestein convolution lengths chosen for device plans (scheduler.rs:11436-11500):
+    the fixed upstream benchmark table where it applies, otherwise the smooth-length
+    search (our entry point combines both, as upstream_bluestein_auto_padding does)."""
+    P = V.Precision
+    nvidia = V.DeviceProfile.generic(V.Backend.VULKAN, V.GpuVendor.NVIDIA).replace(
+        shared_memory_bytes=48 * 1024, shared_memory_pow2_bytes=32 * 1024, coalesced_memory_bytes=32)
+    amd = V.DeviceProfile.generic(V.Backend.VULKAN, V.GpuVendor.AMD)
+    unknown = V.DeviceProfile.generic(V.Backend.VULKAN, V.GpuVendor.OTHER, 0x1234)
+    pad = V.upstream_bluestein_auto_padding
+    table_hits = [(41, P.F32, nvidia, 96), (41, P.F64, nvidia, 90), (206, P.F32, nvidia, 512),
+                  (256, P.F32, nvidia, 512), (257, P.F32, nvidia, 567), (4096, P.F32, nvidia, 8192),
+                  (19, P.F32, amd, 42), (19, P.F64, amd, 40), (3438, P.F64, amd, 6875),
+                  (3439, P.F64, amd, 8192)]
+    for n, prec, dev, m in table_hits:
+        assert pad(n, 1, prec, dev) == m, (n, prec, m)
+    # table misses fall through to the search, which never goes below 2N - 1; a vendor
+    # without a fixed upstream scheduler profile has neither (scheduler.rs:291)
+    for n, prec, dev in ((66, P.DOUBLE_DOUBLE, nvidia), (4097, P.F32, nvidia)):
+        assert pad(n, 1, prec, dev) >= 2 * n - 1, (n, prec)
+    with pytest.raises(V.VkFftError) as e:
+        pad(206, 1, P.F32, unknown)
+    assert e.value.variant == "UnsupportedKernelPath" and "known GPU scheduler profile" in str(e.value)
+    for prec in (P.F32, P.DOUBLE_DOUBLE, P.DOUBLE_DOUBLE_F64_STORAGE):
+        assert pad(4106, 1, prec, nvidia) == 8232, prec
