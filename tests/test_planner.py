@@ -317,3 +317,21 @@ def test_bluestein_auto_padding_matches_fixed_upstream_boundaries(V):
     assert e.value.variant == "UnsupportedKernelPath" and "known GPU scheduler profile" in str(e.value)
     for prec in (P.F32, P.DOUBLE_DOUBLE, P.DOUBLE_DOUBLE_F64_STORAGE):
         assert pad(4106, 1, prec, nvidia) == 8232, prec
+
+
+@pytest.mark.parametrize("vendor,other,precision,expected", [
+    ("NVIDIA", 0, "F32", (17, 89, 17, 16384)),
+    ("AMD", 0, "F64", (17, 89, 29, 16384)),
+    ("AMD", 0, "DOUBLE_DOUBLE", (11, 29, 19, 16384)),
+    ("NVIDIA", 0, "DOUBLE_DOUBLE", (11, 29, 17, 16384)),
+    ("INTEL", 0, "F32", (17, 17, 17, 16384)),
+    ("APPLE", 0, "F64", (17, 17, 17, 16384)),
+    ("OTHER", 0x1234, "F32", (17, 17, 17, 16384)),
+])
+def test_device_rader_thresholds_match_fixed_upstream_initialization(V, vendor, other, precision, expected):
+    # config.rs device_rader_thresholds_match_fixed_upstream_initialization: the Rader
+    # prime windows (min/max direct, min/max FFT convolution) a device profile resolves to
+    device = V.DeviceProfile.generic(V.Backend.VULKAN, V.GpuVendor[vendor], other)
+    t = V.PlannerTuning.for_device(device, V.Precision[precision])
+    got = (t.min_rader_direct_prime, t.max_rader_direct_prime, t.min_rader_fft_prime, t.max_rader_fft_prime)
+    assert got == expected
