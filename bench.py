@@ -54,24 +54,47 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi sampling during the timed region (the pool's clocks line)."""
+    """nvidia-smi sampling of this rank's GPU (the pool's clocks line).
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    The sampler starts before the warm-up and waits for its first row, so a timed region
+    shorter than the sampling period still has samples around it: the summary keeps the
+    rows read inside the timed window (`mark_start` / `mark_end`) widened by one period on
+    each side, all of them taken with the GPU under this benchmark's load.  The GPU is
+    matched by PCI bus id, which holds under CUDA_VISIBLE_DEVICES and torchrun (the
+    nvidia-smi index of a rank's GPU need not equal its CUDA ordinal)."""
+
+    QUERY = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 50
 
-    def __init__(self, index):
-        self.index = index
-        self.rows = []
+    def __init__(self, device_ordinal):
+        self.bus_id = None
+        try:
+            import torch
+            pci = torch.cuda.get_device_properties(device_ordinal).pci_bus_id  # e.g. 0000:1B:00.0
+            self.bus_id = pci.upper()
+        except Exception:
+            pass
+        self.rows = []  # (wall time, fields)
         self.proc = None
+        self.t_start = self.t_end = None
+
+    @staticmethod
+    def _same_bus(a, b):
+        # nvidia-smi prints an 8-digit domain (00000000:1B:00.0), torch a 4-digit one
+        return a.split(":", 1)[-1].upper() == b.split(":", 1)[-1].upper()
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", str(self.PERIOD_MS)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
         return self
@@ -79,8 +102,19 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+            if len(parts) >= 9 and (self.bus_id is None or self._same_bus(parts[0], self.bus_id)):
+                self.rows.append((time.time(), parts))
+
+    def mark_start(self):
+        self.t_start = time.time()
+
+    def mark_end(self):
+        self.t_end = time.time()
+        # at least one row after the window closes
+        n = len(self.rows)
+        t0 = time.time()
+        while len(self.rows) == n and time.time() - t0 < 1.0 and self.proc and self.proc.poll() is None:
+            time.sleep(0.005)
 
     def __exit__(self, *exc):
         if self.proc:
@@ -91,14 +125,19 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        rows = [r for _, r in self.rows]
+        if self.t_start is not None and self.t_end is not None:
+            pad = 1.5 * self.PERIOD_MS * 1e-3
+            rows = [r for t, r in self.rows if self.t_start - pad <= t <= self.t_end + pad]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i] == "Active"})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(rows),
+                "window": "timed region +- one sampling period (50 ms), GPU matched by PCI bus id"}
 
 
 def cpu_baseline(steps_hint=1, budget_s=12.0):
@@ -150,29 +189,91 @@ def dist_env():
     return ws, rank, local
 
 
+def headline_config(ws):
+    """`config` of the headline line, shared by both arms."""
+    return {"workload": "BASELINE config 2: C2C N=4096 x batch 65536 per rank, forward + normalised inverse",
+            "global_batch": BATCH * ws, "seq_len": N, "parallelism": f"batch-sharded x{ws}",
+            "l2": "inputs (2 GiB per rank) larger than L2; no flush"}
+
+
 def run_reference(args):
+    """The reference's CPU algorithm (the C port of src/reference.rs in oracle/) on all host
+    cores, on the headline's metric and config.  A step is one forward + normalised inverse
+    pass over a fixed sample of the 65536 lines, sized in the warm-up so that a step takes
+    about a second; `ms_per_step` is the time of that step as run, and the time the whole
+    batch would take at the same rate is reported beside it."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return 0
-    steps = []
+    import oracle
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1)
+
+    def pair(xd, y):
+        lines = xd.shape[0]
+        oracle.lib().oracle_fft_batch(oracle._dp(xd), oracle._dp(y), N, lines, 0, 0, threads)
+        oracle.lib().oracle_fft_batch(oracle._dp(y), oracle._dp(xd), N, lines, 1, 1, threads)
+
+    probe = max(2 * threads, 16)
+    xd = (rng.uniform(-1, 1, (probe, N)) + 1j * rng.uniform(-1, 1, (probe, N))).astype(np.complex64).astype(np.complex128)
+    y = np.empty_like(xd)
+    t0 = time.perf_counter()
+    pair(xd, y)
+    dt = time.perf_counter() - t0
+    lines = int(min(BATCH, max(threads, round(probe * 1.0 / max(dt, 1e-6)))))
+    lines = max(threads, lines - lines % threads) if lines >= threads else lines
+    xd = (rng.uniform(-1, 1, (lines, N)) + 1j * rng.uniform(-1, 1, (lines, N))).astype(np.complex64).astype(np.complex128)
+    y = np.empty_like(xd)
     for _ in range(args.warmup):
-        cpu_baseline(1, budget_s=1.0)
+        pair(xd, y)
+    times = []
     for _ in range(args.steps):
-        steps.append(cpu_baseline(1, budget_s=max(4.0, 30.0 / max(args.steps, 1))))
-    value = statistics.mean(s["value"] for s in steps)
-    cb = dict(steps[-1])
-    cb["value"] = value
+        t0 = time.perf_counter()
+        pair(xd, y)
+        times.append(time.perf_counter() - t0)
+    step_s = statistics.mean(times)
+    value = 2 * FLOP_PER_TRANSFORM * lines / step_s / 1e9
+    cfg = headline_config(ws)
+    cfg["sampled_fraction"] = lines / (BATCH * ws)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GFLOP/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 2 * FLOP_PER_TRANSFORM * BATCH / value / 1e6,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+        "ms_per_step_full_batch": step_s * 1e3 * BATCH * ws / lines,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "C2C N=4096 x batch 65536 (per rank), forward + normalised inverse",
-                   "global_batch": BATCH, "parallelism": "host cores"},
-        "cpu_baseline": cb,
+        "config": cfg,
+        "cpu_baseline": {"value": value, "unit": "GFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{lines} of the {BATCH * ws} lines per step (forward + normalised inverse, "
+                                   f"f64 oracle), {args.steps} steps of {step_s:.2f} s"},
         "e2e": {"value": value, "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
     return 0
+
+
+def headline_parity(ctx, fwd, a, b, sp, rank, dist, lines=16):
+    """After the timed region: one more forward transform of the current data, and 16
+    sampled lines of it (first, last and random ones, spread over every line group of the
+    persistent kernel) against the CPU oracle; the max relative L2 over the ranks."""
+    import torch
+    import oracle
+    ctx.execute_resident(fwd, a.data_ptr(), b.data_ptr(), stream=sp)
+    ctx.synchronize(sp)
+    rng = np.random.default_rng(100 + rank)
+    idx = sorted({0, BATCH - 1} | set(int(v) for v in rng.choice(BATCH, lines - 2, replace=False)))[:lines]
+    it = torch.tensor(idx, device="cuda")
+    xa = a.view(BATCH, 2 * N)[it].double().cpu().numpy()
+    ya = b.view(BATCH, 2 * N)[it].double().cpu().numpy()
+    xs = xa[:, 0::2] + 1j * xa[:, 1::2]
+    ys = ya[:, 0::2] + 1j * ya[:, 1::2]
+    ref = oracle.fft_nd(xs, 1)
+    err = float(np.linalg.norm(ys - ref) / np.linalg.norm(ref))
+    if dist:
+        t = torch.tensor([err], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        err = float(t[0])
+    return {"relL2": err, "lines": len(idx), "tol": 2e-6, "ok": err <= 2e-6,
+            "check": "forward transform of the data after the timed steps; sampled lines against the CPU "
+                     "oracle (f64 restatement of reference.rs), max over ranks"}
 
 
 def run_ours(args):
@@ -204,16 +305,17 @@ def run_ours(args):
         ctx.execute_resident(fwd, a.data_ptr(), b.data_ptr(), stream=sp)
         ctx.execute_resident(inv, b.data_ptr(), a.data_ptr(), stream=sp)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # per-launch timing of the dominant kernel (forward pass) on the same stream
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(local) as clk:
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clk.mark_start()
         ev0.record(stream)
         for k in range(args.steps):
             evs[k][0].record(stream)
@@ -222,6 +324,8 @@ def run_ours(args):
             ctx.execute_resident(inv, b.data_ptr(), a.data_ptr(), stream=sp)
         ev1.record(stream)
         torch.cuda.synchronize()
+        clk.mark_end()
+    ctx.synchronize(sp)  # raises if a kernel recorded an error
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -238,6 +342,7 @@ def run_ours(args):
     ms_per_step = elapsed_ms / args.steps
     total_transforms = 2 * BATCH * ws
     value = total_transforms * FLOP_PER_TRANSFORM / (ms_per_step * 1e-3) / 1e9
+    parity = headline_parity(ctx, fwd, a, b, sp, rank, dist)
 
     if args.skip_e2e:
         e2e_value = None
@@ -277,9 +382,7 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": "GFLOP/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (uniform [-1,1], torch generator seed 1+rank)",
-        "config": {"workload": "BASELINE config 2: C2C N=4096 x batch 65536 per rank, forward + normalised inverse",
-                   "global_batch": BATCH * ws, "seq_len": N, "parallelism": f"batch-sharded x{ws}",
-                   "l2": "inputs (2 GiB per rank) larger than L2; no flush"},
+        "config": headline_config(ws),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": peak_kind, "this_gpu_copy_gbs": box_copy,
                      "kernel": "reg_fft_persistent<float,4096> (register-resident Stockham with bulk-copy prefetch, one launch per transform direction)"},
@@ -288,6 +391,7 @@ def run_ours(args):
         "gpu_launches": args.steps * (fwd.launch_count + inv.launch_count),
         "clocks": clk.summary(),
         "rank_ms_per_step": rank_ms,
+        "parity": parity,
     }
     if rank == 0:
         line["cpu_baseline"] = cpu_baseline(1, budget_s=12.0) if (ws == 1 and not args.skip_cpu) else None
@@ -386,12 +490,14 @@ def run_slab_workload(args, wl, ctx, dev, dist, ws, rank, local):
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in launches]
            for _ in range(args.steps)]
     with ClockSampler(local) as clk:
+        clk.mark_start()
         for k in range(args.steps):
             for j, f in enumerate(launches):
                 evs[k][j][0].record(stream)
                 f()
                 evs[k][j][1].record(stream)
         torch.cuda.synchronize()
+        clk.mark_end()
     ctx.synchronize(sp)
     part_ms = [statistics.mean(evs[k][j][0].elapsed_time(evs[k][j][1]) for k in range(args.steps))
                for j in range(len(launches))]
@@ -517,6 +623,7 @@ def run_workload(args):
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in launches]
            for _ in range(args.steps)]
     with ClockSampler(local) as clk:
+        clk.mark_start()
         for k in range(args.steps):
             for j, f in enumerate(launches):
                 if flush is not None:
@@ -525,6 +632,7 @@ def run_workload(args):
                 f(sp)
                 evs[k][j][1].record(stream)
         torch.cuda.synchronize()
+        clk.mark_end()
     part_ms = [statistics.mean(evs[k][j][0].elapsed_time(evs[k][j][1]) for k in range(args.steps))
                for j in range(len(launches))]
     ms = sum(part_ms)

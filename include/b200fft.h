@@ -306,9 +306,10 @@ b200fft_status b200fft_execute(b200fft_context *context, b200fft_transform *tran
  * on each device.  A transform whose tables plus scratch
  * (b200fft_transform_workspace_bytes covers the scratch part) exceed the region is
  * rejected with B200FFT_RESOURCE_LIMIT_EXCEEDED and a message giving both sizes.
- * Nothing in the region has to start at zero.  The first call on a device, and the
- * first call after another transform used the region, copy the tables in from host
- * memory; make the first call before any stream capture.  Calls whose GPU work can
+ * Nothing in the region has to start at zero.  Every call copies its transform's
+ * tables in from host memory (a packed image the transform keeps from its first call)
+ * ahead of its kernels, on the same stream.  The first call on a device also looks up
+ * the region's address: make it before any stream capture.  Calls whose GPU work can
  * overlap -- on different streams, contexts or threads of one process -- share the
  * region and race: order them on one stream.  in and out as for b200fft_execute;
  * stream: a cudaStream_t, or NULL for the context's stream. */

@@ -13,6 +13,7 @@
 // through an explicit multiply pass.  The reference requires K C copies of the kernel
 // spectrum; a single copy is accepted too and broadcast to every coordinate.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 
@@ -95,7 +96,7 @@ static std::unique_ptr<Convolution> build_c2c_convolution(const FftConfig &c, co
         if (!std::isfinite(v)) fail_invalid_ir("convolution kernel spectrum contains non-finite values");
     }
     auto conv = std::make_unique<Convolution>();
-    static uint64_t next_id = 1ull << 42;
+    static std::atomic<uint64_t> next_id{1ull << 42};
     conv->id = next_id++;
     conv->config = c;
     conv->device = device;
@@ -175,7 +176,7 @@ std::unique_ptr<Convolution> build_convolution(const FftConfig &config_in, const
     if (config_in.has_formatted_strides()) fail_unsupported("B200 engine: formatted buffer strides are not implemented yet");
     const FftConfig c = config_in.resolve_tuning_for_device(device);
     auto conv = std::make_unique<Convolution>();
-    static uint64_t next_id = 1ull << 40;
+    static std::atomic<uint64_t> next_id{1ull << 40};
     conv->id = next_id++;
     conv->config = c;
     conv->device = device;

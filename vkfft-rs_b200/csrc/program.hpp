@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -80,6 +81,10 @@ struct Program {
     double algorithmic_flops = 0;  // 5 N log2 N per complex transform (for reports)
     int storage_scalar_bytes = 0;  // bytes of one stored scalar of the caller's buffers: 2 (f16),
                                    // 4, 8; 0 = the compute precision's
+    // Packed device image of `tables` (256-byte aligned entries), built on the first
+    // static-workspace execution and kept for the program's lifetime: the source of that
+    // entry point's per-call table upload (static_workspace.cu).
+    mutable std::shared_ptr<const std::vector<unsigned char>> static_table_image;
 
     int rbytes() const { return is_dd ? 16 : (is_double ? 8 : 4); }  // one compute scalar
     int cbytes() const { return 2 * rbytes(); }                        // one compute complex

@@ -1,5 +1,7 @@
 // Slab decomposition plans (host only): the per-rank launch programs of a slab transform
 // (see slab.cu for the data flow and the exchange).
+#include <atomic>
+
 #include "slab.hpp"
 
 namespace b200fft {
@@ -12,11 +14,9 @@ size_t prod(const std::vector<size_t> &v, size_t a, size_t b) {
     return r;
 }
 
-uint64_t next_slab_id() {
-    static uint64_t next = 1ull << 41;
-    const uint64_t id = next;
-    next += 2;
-    return id;
+uint64_t next_slab_id() {  // ids id and id + 1 (the two directions' programs)
+    static std::atomic<uint64_t> next{1ull << 41};
+    return next.fetch_add(2);
 }
 
 // Marks the last pass a lowering appended (it must write the axis output) as the

@@ -3,11 +3,13 @@
 //
 // The region is one file-scope __device__ array.  Its address is looked up once per
 // device with cudaGetSymbolAddress (with that device current) and cached.  A call lays
-// the region out as [packed tables | scratch buffers], uploads the transform's tables
-// when the region last held another transform's tables, and launches the same passes
-// as execute_program.  Nothing in the region has to start at zero: every pass writes
-// each scratch element before a later pass reads it, and the tables are copied in
-// before the first launch that reads them.  The kernels' error word is the context's.
+// the region out as [packed tables | scratch buffers], copies the transform's tables in
+// from the packed host image the transform keeps (built on its first call here), and
+// launches the same passes as execute_program.  Every call uploads its own tables, so a
+// call's result never depends on which transform used the region before it.  Nothing
+// in the region has to start at zero: every pass writes each scratch element before a
+// later pass reads it, and the tables are copied in before the first launch that reads
+// them.  The kernels' error word is the context's.
 #include <cstring>
 #include <mutex>
 
@@ -29,13 +31,8 @@ constexpr size_t kMaxStaticTables = 512;
 static __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
 
 namespace {
-struct StaticRegion {
-    unsigned char *base = nullptr;  // device address of g_static_workspace on this device
-    uint64_t owner = 0;             // program whose tables the region holds (0: none)
-};
 std::mutex g_static_mu;
-StaticRegion g_static[kMaxStaticDevices];
-unsigned char g_table_image[kStaticWorkspaceBytes];  // host staging of the packed tables
+unsigned char *g_static_base[kMaxStaticDevices];  // device address of g_static_workspace per device
 }  // namespace
 
 static void check(cudaError_t e, const char *what) {
@@ -44,7 +41,7 @@ static void check(cudaError_t e, const char *what) {
 
 static size_t round256(size_t v) { return (v + 255) & ~size_t(255); }
 
-void execute_program_static(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out,
+void execute_program_static(Context *ctx, uint64_t /*id*/, const Program &prog, const void *in, void *out,
                             cudaStream_t stream) {
     if (ctx->device < 0 || ctx->device >= kMaxStaticDevices)
         throw FftError(B200FFT_RESOURCE_LIMIT_EXCEEDED, "static workspace supports CUDA device ordinals below " +
@@ -61,36 +58,43 @@ void execute_program_static(Context *ctx, uint64_t id, const Program &prog, cons
                            " bytes but this transform needs " + std::to_string(table_bytes + scratch_bytes) +
                            " (tables " + std::to_string(table_bytes) + ", scratch " + std::to_string(scratch_bytes) +
                            "); execute it with b200fft_execute and a workspace instead");
+    for (const PassPlan &pp : prog.passes)
+        if (pp.peer_scatter)
+            throw FftError(B200FFT_UNSUPPORTED_KERNEL_PATH,
+                           "static workspace execution does not run slab exchange passes (they store into other "
+                           "ranks' buffers); execute slab transforms with b200fft_execute_slab");
     check(cudaSetDevice(ctx->device), "cudaSetDevice");
     if (!stream) stream = ctx->stream;
     std::lock_guard<std::mutex> g(g_static_mu);
-    StaticRegion &r = g_static[ctx->device];
-    if (!r.base) {
+    unsigned char *&base = g_static_base[ctx->device];
+    if (!base) {
         void *p = nullptr;
         check(cudaGetSymbolAddress(&p, g_static_workspace), "cudaGetSymbolAddress of the static workspace");
-        r.base = static_cast<unsigned char *>(p);
+        base = static_cast<unsigned char *>(p);
     }
     const void *tables[kMaxStaticTables];
     size_t off = 0;
     for (size_t k = 0; k < prog.tables.size(); k++) {
-        tables[k] = r.base + off;
+        tables[k] = base + off;
         off += round256(prog.tables[k].bytes(prog.cbytes()));
     }
-    if (r.owner != id && table_bytes > 0) {
-        // Pack in the pass precision (as the context's table upload does), then one
-        // stream-ordered copy.  The copy is from pageable memory: it has returned only
-        // once the source was consumed, so the staging image can be reused at once.
-        off = 0;
-        for (const HostTable &t : prog.tables) {
-            pack_table(t, prog, g_table_image + off);
-            off += round256(t.bytes(prog.cbytes()));
+    if (table_bytes > 0) {
+        // The packed image (pass precision, as the context's table upload packs it) is
+        // built once per program and lives as long as the program; the copy is
+        // stream-ordered before the passes that read the tables.
+        if (!prog.static_table_image) {
+            auto img = std::make_shared<std::vector<unsigned char>>(table_bytes, 0);
+            off = 0;
+            for (const HostTable &t : prog.tables) {
+                pack_table(t, prog, img->data() + off);
+                off += round256(t.bytes(prog.cbytes()));
+            }
+            prog.static_table_image = img;
         }
-        r.owner = 0;
-        check(cudaMemcpyAsync(r.base, g_table_image, table_bytes, cudaMemcpyHostToDevice, stream),
+        check(cudaMemcpyAsync(base, prog.static_table_image->data(), table_bytes, cudaMemcpyHostToDevice, stream),
               "static workspace table upload");
     }
-    r.owner = id;
-    unsigned char *scr = r.base + table_bytes;
+    unsigned char *scr = base + table_bytes;
     const size_t esz = (size_t)prog.cbytes();
     void *bufs[2 + kScratchBuffers] = {const_cast<void *>(in), out};
     for (int k = 0; k < kScratchBuffers; k++) bufs[2 + k] = scr + prog.scratch_offset(k);
