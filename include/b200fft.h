@@ -267,11 +267,13 @@ int32_t b200fft_transform_input_is_real(const b200fft_transform *transform);
 int32_t b200fft_transform_output_is_real(const b200fft_transform *transform);
 /* Bytes of device scratch one execution needs (0 when every pass runs in place on chip). */
 uint64_t b200fft_transform_workspace_bytes(const b200fft_transform *transform);
-/* Compiles (NVRTC, no GPU needed, nothing loaded) the run-time specialised kernel of
- * every generic pass of the transform: returns the number compiled, or -1 with the
- * compiler log in `log`.  A build check for the specialisation; execution compiles and
- * loads the same kernels on first use. */
-int32_t b200fft_transform_compile_check(const b200fft_transform *transform, char *log, size_t capacity);
+/* Generic (op-program) passes of the transform that run an ahead-of-time specialised
+ * sm_100a kernel from the library's catalogue: returns their number (-1 for a null
+ * transform) and stores the number of generic passes in *generic_passes; the others run
+ * the precompiled interpreter kernel.  No counterpart in the reference (whose kernels
+ * are generated and compiled at run time, backend/cuda/runtime.rs:300-368); nothing is
+ * compiled at run time here.  Needs no GPU. */
+int32_t b200fft_transform_specialised_passes(const b200fft_transform *transform, int32_t *generic_passes);
 /* Number of kernel launches one execution issues. */
 uint32_t b200fft_transform_launch_count(const b200fft_transform *transform);
 
@@ -345,6 +347,9 @@ b200fft_status b200fft_convolution_build(const b200fft_config *config,
                                          b200fft_convolution **convolution);
 void b200fft_convolution_destroy(b200fft_convolution *convolution);
 uint64_t b200fft_convolution_workspace_bytes(const b200fft_convolution *convolution);
+/* As b200fft_transform_specialised_passes, for a convolution's launch list (no
+ * counterpart in the reference). */
+int32_t b200fft_convolution_specialised_passes(const b200fft_convolution *convolution, int32_t *generic_passes);
 /* Element counts of the input / output arrays (real for the ND real convolution, complex
  * for ConvolutionIr / NdConvolutionIr). */
 uint64_t b200fft_convolution_input_elements(const b200fft_convolution *convolution);

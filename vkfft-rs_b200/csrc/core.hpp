@@ -84,6 +84,9 @@ struct DeviceProfile {
     static DeviceProfile generic(Backend b, Vendor v, uint32_t other = 0);  // config.rs:267-282
 };
 
+// DeviceProfile of a CUDA device from its attributes (backend/cuda/runtime.rs:1204-1225)
+DeviceProfile cuda_device_profile(size_t shared_per_block, size_t max_threads, size_t dim_x, size_t dim_y,
+                                  size_t dim_z, bool supports_f64);
 PlannerTuning tuning_for_device(const DeviceProfile &d, Precision p);  // config.rs:396-420
 bool has_fixed_upstream_gpu_scheduler_profile(const DeviceProfile &d); // config.rs:287-299
 size_t upstream_coalesced_memory_bytes_for_precision(const DeviceProfile &d, Precision p);

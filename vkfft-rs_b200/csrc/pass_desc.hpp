@@ -6,14 +6,7 @@
 // processing) and stored back.  Plain POD so it can be a __grid_constant__
 // kernel parameter.
 #pragma once
-#ifdef __CUDACC_RTC__
-typedef int int32_t;
-typedef unsigned int uint32_t;
-typedef long long int64_t;
-typedef unsigned long long uint64_t;
-#else
 #include <cstdint>
-#endif
 
 namespace b200fft {
 

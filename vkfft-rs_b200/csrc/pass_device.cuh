@@ -1,23 +1,20 @@
 // Device side of the B200 FFT pass kernel: the per-CTA prologue and the op functions
 // (load, radix stages, multiplies, Rader, real pre/post processing, store).  Included
 // by kernels.cu (the precompiled op-program interpreter, and the CPU emulator) and by
-// the run-time specialised pass kernels (jit.cpp), which call the same functions with
-// the pass's sizes and strides as compile-time constants.
+// the ahead-of-time specialised pass kernels the build generates (aot.hpp), which call
+// the same functions with the pass's structure as compile-time constants.
 #pragma once
 
-#ifndef __CUDACC_RTC__
 #include <cmath>
 #include <cstdint>
-#endif
 
 #include "dft_codelets.cuh"
 #include "dd.cuh"
 #include "pass_desc.hpp"
 
-// Threads of the CTA: the run-time specialised kernels define it as the pass's literal
-// thread count, so every op loop below has a compile-time stride and trip count (the
-// compiler unrolls the rounds and overlaps their loads); the precompiled interpreter
-// reads blockDim.x.
+// Threads of the CTA: each unit of specialised kernels defines it as their literal
+// thread count, so every op loop below has a compile-time stride (the compiler unrolls
+// the rounds of a radix stage and overlaps their loads); the interpreter reads blockDim.x.
 #ifndef B200FFT_NT
 #define B200FFT_NT blockDim.x
 #define B200FFT_STAGE_UNROLL

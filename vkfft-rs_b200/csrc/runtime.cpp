@@ -58,12 +58,6 @@ int probe_devices() {
     return n;
 }
 
-static size_t floor_pow2(size_t v) {
-    size_t p = 1;
-    while (p * 2 <= v) p *= 2;
-    return v ? p : 0;
-}
-
 Context *context_create(int device) {
     int n = probe_devices();
     if (device < 0 || device >= n) fail_unavailable("CUDA device ordinal " + std::to_string(device) + " is out of range");
@@ -83,19 +77,9 @@ Context *context_create(int device) {
         ctx->sm_count = prop.multiProcessorCount;
         // The profile the reference derives from the same attributes
         // (backend/cuda/runtime.rs:1204-1225).
-        DeviceProfile d = DeviceProfile::generic(Backend::Cuda, Vendor::Nvidia);
-        d.shared_memory_bytes = prop.sharedMemPerBlock;
-        d.shared_memory_pow2_bytes = floor_pow2(prop.sharedMemPerBlock);
-        d.max_threads_per_block = prop.maxThreadsPerBlock;
-        d.max_workgroup_size[0] = prop.maxThreadsDim[0];
-        d.max_workgroup_size[1] = prop.maxThreadsDim[1];
-        d.max_workgroup_size[2] = prop.maxThreadsDim[2];
-        d.coalesced_memory_bytes = 32;
-        d.shared_banks = 32;
-        d.supports_f64 = prop.major > 1 || (prop.major == 1 && prop.minor >= 3);
-        d.subgroup.size = d.subgroup.min_size = d.subgroup.max_size = 32;
-        d.subgroup.compute_supported = d.subgroup.basic_supported = d.subgroup.shuffle_supported = true;
-        d.subgroup.shuffle_relative_supported = d.subgroup.compute_full_subgroups = true;
+        DeviceProfile d = cuda_device_profile(prop.sharedMemPerBlock, prop.maxThreadsPerBlock, prop.maxThreadsDim[0],
+                                              prop.maxThreadsDim[1], prop.maxThreadsDim[2],
+                                              prop.major > 1 || (prop.major == 1 && prop.minor >= 3));
         ctx->profile = d;
         set_kernel_smem_limits();
         set_reg_kernel_smem_limits();
@@ -183,7 +167,7 @@ static DeviceTables &ensure_tables(Context *ctx, uint64_t id, const Program &pro
     for (size_t k = 0; k < prog.tables.size(); k++)
         dt.ptrs.push_back(static_cast<unsigned char *>(dt.base) + offs[k]);
     try {
-        dt.jit = jit_kernels_for(prog, ctx->device);
+        dt.spec = aot_kernels_for(prog, ctx->device);
     } catch (...) {
         cudaFree(dt.base);
         throw;
@@ -274,9 +258,9 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
             p.peer.sub = peer->chunk * pp.peer_es;
         }
         if (injected("launch", g_launch_count)) fail_runtime("kernel launch failed: injected launch fault");
-        if (pi < dt.jit.size() && dt.jit[pi]) {
+        if (pi < dt.spec.size() && dt.spec[pi]) {
             void *args[] = {&p};
-            check(cudaLaunchKernel(dt.jit[pi], dim3((unsigned)pp.grid), dim3(pp.threads), args, pp.smem, stream),
+            check(cudaLaunchKernel(dt.spec[pi], dim3((unsigned)pp.grid), dim3(pp.threads), args, pp.smem, stream),
                   "kernel launch");
         } else {
             check(launch_pass(variant, p, pp.grid, pp.threads, pp.smem, stream), "kernel launch");

@@ -14,6 +14,7 @@
 #include <thread>
 #include <unordered_map>
 
+#include "aot.hpp"
 #include "transform.hpp"
 
 namespace b200fft {
@@ -21,12 +22,8 @@ namespace b200fft {
 struct DeviceTables {
     void *base = nullptr;
     std::vector<const void *> ptrs;
-    std::vector<const void *> jit;  // per pass: specialised kernel (jit.cpp) or null
+    std::vector<const void *> spec;  // per pass: ahead-of-time specialised kernel (aot.hpp) or null
 };
-
-bool jit_enabled();
-std::vector<const void *> jit_kernels_for(const Program &prog, int device);
-int jit_compile_check(const Program &prog, std::string &log);
 
 struct Context {
     int device = 0;

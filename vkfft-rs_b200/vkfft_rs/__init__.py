@@ -252,7 +252,7 @@ def library():
         "b200fft_transform_output_is_real": ([vp], i32),
         "b200fft_transform_workspace_bytes": ([vp], u64),
         "b200fft_transform_launch_count": ([vp], u32),
-        "b200fft_transform_compile_check": ([vp, ctypes.c_char_p, ctypes.c_size_t], i32),
+        "b200fft_transform_specialised_passes": ([vp, P(i32)], i32),
         "b200fft_probe": ([P(i32)], i32),
         "b200fft_context_create": ([i32, P(vp)], i32),
         "b200fft_context_destroy": ([vp], None),
@@ -264,6 +264,7 @@ def library():
         "b200fft_convolution_build": ([P(_Config), P(_Device), vp, u64, P(vp)], i32),
         "b200fft_convolution_destroy": ([vp], None),
         "b200fft_convolution_workspace_bytes": ([vp], u64),
+        "b200fft_convolution_specialised_passes": ([vp, P(i32)], i32),
         "b200fft_convolution_input_elements": ([vp], u64),
         "b200fft_convolution_output_elements": ([vp], u64),
         "b200fft_convolution_input_is_real": ([vp], i32),
@@ -662,14 +663,12 @@ class TransformIr:
             _lib.b200fft_transform_destroy(h)
             self._h = None
 
-    def compile_check(self):
-        """NVRTC-compiles the specialised kernel of every generic pass (no GPU needed);
-        returns how many, raises RuntimeError with the compiler log on failure."""
-        buf = ctypes.create_string_buffer(16384)
-        n = library().b200fft_transform_compile_check(self._h, buf, len(buf))
-        if n < 0:
-            raise RuntimeError(buf.value.decode(errors="replace"))
-        return n
+    @property
+    def specialised_passes(self):
+        """(generic passes with an ahead-of-time specialised kernel, generic passes)."""
+        total = ctypes.c_int32()
+        covered = library().b200fft_transform_specialised_passes(self._h, ctypes.byref(total))
+        return int(covered), int(total.value)
 
     @property
     def family(self):
@@ -787,6 +786,13 @@ class _ConvolutionApplication:
     @property
     def workspace_bytes(self):
         return int(library().b200fft_convolution_workspace_bytes(self._h))
+
+    @property
+    def specialised_passes(self):
+        """(generic passes with an ahead-of-time specialised kernel, generic passes)."""
+        total = ctypes.c_int32()
+        covered = library().b200fft_convolution_specialised_passes(self._h, ctypes.byref(total))
+        return int(covered), int(total.value)
 
     def real_dtype(self):
         return np.float32 if self.precision == Precision.F32 else np.float64
