@@ -4,9 +4,9 @@ Collected last (file name) so that it also runs after every other GPU test has u
 context's own scratch and tables.  Each case compares two calls in a row of the static
 entry point with the ordinary resident entry point (b200fft_execute) on the same input.
 The two calls agree bit for bit; against b200fft_execute they agree to the parity
-tolerance, because b200fft_execute runs generic passes as run-time specialised kernels
-(compiled and loaded on first use, which allocates) while the static entry point keeps
-the precompiled ones."""
+tolerance, because b200fft_execute runs catalogued generic passes on their ahead-of-time
+specialised kernels while the static entry point runs every generic pass on the
+precompiled interpreter kernel (the same arithmetic, compiled differently)."""
 import numpy as np
 import pytest
 
