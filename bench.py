@@ -54,31 +54,48 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of this rank's GPU (the pool's clocks line).
+    """Clocks and throttle reasons of this rank's GPU during the timed region.
 
-    The sampler starts before the warm-up and waits for its first row, so a timed region
-    shorter than the sampling period still has samples around it: the summary keeps the
-    rows read inside the timed window (`mark_start` / `mark_end`) widened by one period on
-    each side, all of them taken with the GPU under this benchmark's load.  The GPU is
-    matched by PCI bus id, which holds under CUDA_VISIBLE_DEVICES and torchrun (the
-    nvidia-smi index of a rank's GPU need not equal its CUDA ordinal)."""
+    Two readers: NVML, polled every millisecond between `mark_start` and `mark_end` (a
+    timed region of a few tens of milliseconds still gets tens of samples, all taken with
+    the GPU under this benchmark's load), and the pool's nvidia-smi clocks line, started
+    before the warm-up, whose rows inside the window widened by one period are the
+    fallback when NVML is unavailable.  The GPU is matched by PCI bus id, which holds
+    under CUDA_VISIBLE_DEVICES and torchrun.  Only reads; no setting is changed."""
 
     QUERY = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     PERIOD_MS = 50
+    # NVML clocks-event reason bits (nvml.h: HwSlowdown, HwThermalSlowdown,
+    # SwThermalSlowdown, SwPowerCap)
+    REASON_BITS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+                   "sw_power_cap": 0x4}
 
     def __init__(self, device_ordinal):
         self.bus_id = None
         try:
             import torch
-            pci = torch.cuda.get_device_properties(device_ordinal).pci_bus_id  # e.g. 0000:1B:00.0
-            self.bus_id = pci.upper()
+            self.bus_id = torch.cuda.get_device_properties(device_ordinal).pci_bus_id.upper()  # 0000:1B:00.0
         except Exception:
             pass
-        self.rows = []  # (wall time, fields)
+        self.rows = []  # nvidia-smi: (wall time, fields)
+        self.nv = []    # NVML: (sm MHz, reasons bitmask)
+        self.nv_max = None
         self.proc = None
         self.t_start = self.t_end = None
+        self.active = False
+        self.stop = False
+        self.handle = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            dom, rest = self.bus_id.split(":", 1)
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(f"{int(dom, 16):08X}:{rest}")
+            self.nvml = pynvml
+            self.nv_max = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.handle = None
 
     @staticmethod
     def _same_bus(a, b):
@@ -97,6 +114,9 @@ class ClockSampler:
                 time.sleep(0.01)
         except OSError:
             self.proc = None
+        if self.handle is not None:
+            self.poller = threading.Thread(target=self._poll, daemon=True)
+            self.poller.start()
         return self
 
     def _read(self):
@@ -105,18 +125,36 @@ class ClockSampler:
             if len(parts) >= 9 and (self.bus_id is None or self._same_bus(parts[0], self.bus_id)):
                 self.rows.append((time.time(), parts))
 
+    def _poll(self):
+        nv = self.nvml
+        while not self.stop:
+            if self.active:
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                    self.nv.append((sm, rs))
+                except Exception:
+                    pass
+                time.sleep(0.001)
+            else:
+                time.sleep(0.002)
+
     def mark_start(self):
         self.t_start = time.time()
+        self.active = True
 
     def mark_end(self):
+        self.active = False
         self.t_end = time.time()
-        # at least one row after the window closes
+        # at least one nvidia-smi row after the window closes
         n = len(self.rows)
         t0 = time.time()
         while len(self.rows) == n and time.time() - t0 < 1.0 and self.proc and self.proc.poll() is None:
             time.sleep(0.005)
 
     def __exit__(self, *exc):
+        self.stop = True
+        self.active = False
         if self.proc:
             self.proc.terminate()
             try:
@@ -125,6 +163,12 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self.nv:
+            sm = [v for v, _ in self.nv]
+            reasons = sorted({k for _, r in self.nv for k, bit in self.REASON_BITS.items() if r & bit})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.nv_max, "reasons": reasons,
+                    "samples": len(sm), "sm_mhz_min": min(sm),
+                    "window": "NVML polled every 1 ms inside the timed region (GPU matched by PCI bus id)"}
         rows = [r for _, r in self.rows]
         if self.t_start is not None and self.t_end is not None:
             pad = 1.5 * self.PERIOD_MS * 1e-3
@@ -137,7 +181,7 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows),
-                "window": "timed region +- one sampling period (50 ms), GPU matched by PCI bus id"}
+                "window": "nvidia-smi rows in the timed region +- one sampling period (50 ms)"}
 
 
 def cpu_baseline(steps_hint=1, budget_s=12.0):
@@ -276,6 +320,161 @@ def headline_parity(ctx, fwd, a, b, sp, rank, dist, lines=16):
                      "oracle (f64 restatement of reference.rs), max over ranks"}
 
 
+def timed_steps(steps, warmup, stream, calls, dist):
+    """Warm-up, then `steps` steps of `calls` bracketed by barriers and synchronisation;
+    returns the device milliseconds of one step (CUDA events on `stream`), max over ranks."""
+    import torch
+    for _ in range(max(warmup, 3)):
+        for f in calls:
+            f()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        for f in calls:
+            f()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if dist:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    return ms
+
+
+def slab_section(args, ctx, dev, stream, ws, rank, dist):
+    """BASELINE config 3 (C2C 512^3 f32, N(0,1) input) as the strong-scaling companion of the
+    headline: on one GPU the local 3D transform, on N GPUs the slab decomposition (rank g
+    owns planes g*512/N.., the all-to-all is fused into the axis-1 pass's stores over
+    NVLink).  A step is one forward + one normalised inverse transform; GFLOP/s counts
+    5 n log2 n per transform (n = 512^3) for the whole job.  Phase times are of one more
+    forward call (max over ranks); nvlink_gbs = bytes one GPU stores into the others /
+    the exchange pass's time.  Parity (N > 1): the gathered slab output against the
+    single-GPU transform of the gathered input on rank 0 -- the path the full-size test
+    pins to the CPU oracle at this size."""
+    import torch
+    import vkfft_rs as V
+    D = 512
+    n = D ** 3
+    flop = 2 * 5.0 * n * math.log2(n)
+    sp = stream.cuda_stream
+    cfg = V.FftConfig([D, D, D]).with_inverse_normalization(True)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2 + rank)
+    out = {"workload": "BASELINE config 3: C2C 512^3 f32, forward + normalised inverse",
+           "scaling": "strong (one tensor over all GPUs)"}
+    if ws == 1:
+        fwd = V.TransformIr.build(cfg, V.Direction.FORWARD, dev)
+        inv = V.TransformIr.build(cfg, V.Direction.INVERSE, dev)
+        x = torch.randn((n * 2,), device="cuda", generator=gen)
+        y = torch.empty_like(x)
+        wsb = torch.empty((max(fwd.workspace_bytes, inv.workspace_bytes, 1),), dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        ms = timed_steps(args.steps, args.warmup, stream,
+                         [lambda: ctx.execute_resident(fwd, x.data_ptr(), y.data_ptr(), wsb.data_ptr(), sp),
+                          lambda: ctx.execute_resident(inv, y.data_ptr(), x.data_ptr(), wsb.data_ptr(), sp)], None)
+        ctx.synchronize(sp)
+        out.update({"ms_per_step": ms, "gflops": flop / (ms * 1e-3) / 1e9, "parallelism": "1 GPU (local 3D transform)",
+                    "gpu_launches_per_step": fwd.launch_count + inv.launch_count})
+        return out
+    fwd = V.SlabTransform.build(cfg, V.Direction.FORWARD, ws, rank, dev)
+    inv = V.SlabTransform.build(cfg, V.Direction.INVERSE, ws, rank, dev)
+    fwd.setup(ctx)
+    inv.setup(ctx)
+    fwd.set_phase_timing(True)
+    x = torch.randn((fwd.input_elements * 2,), device="cuda", generator=gen)
+    x0 = x.clone()
+    y = torch.empty((fwd.output_elements * 2,), device="cuda")
+    torch.cuda.synchronize()
+    ms = timed_steps(args.steps, args.warmup, stream,
+                     [lambda: ctx.execute_slab(fwd, x.data_ptr(), y.data_ptr(), stream=sp),
+                      lambda: ctx.execute_slab(inv, y.data_ptr(), x.data_ptr(), stream=sp)], dist)
+    ctx.synchronize(sp)
+    # phases of the forward transform (from the original input), median of 3 calls
+    phases = []
+    for _ in range(3):
+        dist.barrier()
+        ctx.execute_slab(fwd, x0.data_ptr(), y.data_ptr(), stream=sp)
+        phases.append(fwd.phase_times())
+    ctx.synchronize(sp)
+    ph = [statistics.median(p[k] for p in phases) for k in range(4)]
+    t = torch.tensor(ph, device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ph = [float(v) for v in t]
+    remote = fwd.output_elements * 8 * (ws - 1) / ws
+    # parity: y holds the forward transform of x0
+    xin = torch.empty((ws * x0.numel(),), device="cuda")
+    dist.all_gather_into_tensor(xin, x0)
+    yall = torch.empty((ws * y.numel(),), device="cuda")
+    dist.all_gather_into_tensor(yall, y)
+    err = None
+    if rank == 0:
+        full = V.TransformIr.build(cfg, V.Direction.FORWARD, dev)
+        yref = torch.empty_like(xin)
+        ctx.execute_resident(full, xin.data_ptr(), yref.data_ptr(), stream=sp)
+        ctx.synchronize(sp)
+        # [P, D0, D1/P, D2, 2] -> [D0, P, D1/P, D2, 2]
+        yslab = yall.view(ws, D, D // ws, D, 2).permute(1, 0, 2, 3, 4).reshape(-1)
+        err = float(torch.linalg.vector_norm((yslab - yref).double()) / torch.linalg.vector_norm(yref.double()))
+        del yref, yslab
+    del xin, yall
+    fwd.destroy()
+    inv.destroy()
+    out.update({
+        "ms_per_step": ms, "gflops": flop / (ms * 1e-3) / 1e9, "parallelism": f"slab x{ws}",
+        "forward_phases_ms": {"local_passes": ph[0], "exchange_pass": ph[1], "barrier": ph[2], "after_exchange": ph[3]},
+        "nvlink": {"bytes_per_gpu_per_direction": remote, "exchange_pass_gbs": remote / (ph[1] * 1e-3) / 1e9,
+                   "whole_forward_gbs": remote / (sum(ph) * 1e-3) / 1e9, "peak_gbs": 770.0,
+                   "peak_source": "measured peer copy of this pool (nominal 900)"},
+        "parity": None if err is None else {"relL2_vs_single_gpu": err, "tol": 2e-6, "ok": err <= 2e-6},
+    })
+    return out
+
+
+def conv_section(args, ctx, dev, stream, ws, rank, dist):
+    """BASELINE config 5 (64 images 2048^2 f32, U[0,1], convolved with one sigma = 8
+    Gaussian) sharded by image: 64/N images per rank, no collective on the data path.  A
+    step is one convolution (R2C -> spectrum multiply -> normalised C2R) of the rank's
+    images; GFLOP/s counts 2 x 2.5 n log2 n per image (n = 2048^2) for the whole job.
+    Parity: one image of rank 0 against the CPU oracle."""
+    import torch
+    import vkfft_rs as V
+    dims, total = [2048, 2048], 64
+    n = dims[0] * dims[1]
+    per = total // ws
+    sp = stream.cuda_stream
+    cfg = (V.FftConfig(dims).with_transform(V.TransformKind.R2C).with_convolution(True)
+           .with_coordinate_features(per))
+    spec = gaussian_spectrum(dims)
+    conv = V.NdRealConvolutionIr.build_from_spectrum(cfg, spec, dev)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4 + rank)
+    x = torch.rand((per * n,), device="cuda", generator=gen)
+    y = torch.empty_like(x)
+    wsb = torch.empty((max(conv.workspace_bytes, 1),), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    ms = timed_steps(args.steps, args.warmup, stream,
+                     [lambda: ctx.execute_nd_real_convolution_resident(conv, x.data_ptr(), y.data_ptr(),
+                                                                       wsb.data_ptr(), sp)], dist)
+    ctx.synchronize(sp)
+    err = None
+    if rank == 0:
+        import oracle
+        xi = x[:n].double().cpu().numpy().reshape(dims)
+        ref = oracle.convolve_nd(xi, spec, dims, 1)
+        yi = y[:n].double().cpu().numpy().reshape(dims)
+        err = float(np.linalg.norm(yi - ref) / np.linalg.norm(ref))
+    flop = total * 2 * 2.5 * n * math.log2(n)
+    return {"workload": "BASELINE config 5: 64 images 2048^2 f32 convolved with a sigma=8 Gaussian",
+            "images_per_rank": per, "parallelism": f"images sharded x{ws}", "scaling": "strong (64 images in total)",
+            "ms_per_step": ms, "gflops": flop / (ms * 1e-3) / 1e9,
+            "parity": None if err is None else {"relL2_image0": err, "tol": 2e-6, "ok": err <= 2e-6}}
+
+
 def run_ours(args):
     import torch
     import vkfft_rs as V
@@ -372,6 +571,16 @@ def run_ours(args):
             e2e_s = float(t[0])
         e2e_value = total_transforms * FLOP_PER_TRANSFORM / e2e_s / 1e9
     bytes_one = BATCH * N * 8
+    if not args.skip_e2e:
+        del host_in_t, host_spec_t, host_back_t, x_host, spec, back
+    del a, b
+    torch.cuda.empty_cache()
+    sections = {}
+    if not args.headline_only:
+        sections["slab_512^3"] = slab_section(args, ctx, dev, stream, ws, rank, dist)
+        torch.cuda.empty_cache()
+        sections["conv_2048_sharded"] = conv_section(args, ctx, dev, stream, ws, rank, dist)
+        torch.cuda.empty_cache()
 
     peak, peak_kind = load_peaks()
     box_copy = live_copy_gbs(stream)
@@ -393,6 +602,7 @@ def run_ours(args):
         "rank_ms_per_step": rank_ms,
         "parity": parity,
     }
+    line.update(sections)
     if rank == 0:
         line["cpu_baseline"] = cpu_baseline(1, budget_s=12.0) if (ws == 1 and not args.skip_cpu) else None
         print(json.dumps(line))
@@ -685,6 +895,8 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH, help="transforms per rank (profiling runs use fewer)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: resident timing only")
     ap.add_argument("--skip-cpu", action="store_true", help="profiling runs: no CPU baseline")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="profiling runs: no config-3 slab / config-5 sharded sections")
     ap.add_argument("--workload", default="c2c-4096", choices=["c2c-4096"] + sorted(WORKLOADS),
                     help="c2c-4096 is the headline (config 2); the others measure the remaining configs")
     args = ap.parse_args()

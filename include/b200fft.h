@@ -403,6 +403,13 @@ b200fft_status b200fft_slab_set_timeout(b200fft_slab *slab, uint64_t timeout_ns)
 b200fft_status b200fft_slab_attach(b200fft_context *context, b200fft_slab *slab, void *handle);
 /* handles: nranks consecutive handles, rank order.  Fails if two ranks share a GPU. */
 b200fft_status b200fft_slab_connect(b200fft_context *context, b200fft_slab *slab, const void *handles);
+/* Phase timing (profiling; no counterpart in the reference): once enabled (after
+ * attach), every execution records CUDA events around its phases, and
+ * b200fft_slab_phase_times waits for the last execution and writes ms[4] = the local
+ * passes before the exchange, the exchange pass (the FFT pass whose stores land in the
+ * ranks' buffers), the barrier, and the passes after it. */
+b200fft_status b200fft_slab_set_phase_timing(b200fft_slab *slab, int32_t enabled);
+b200fft_status b200fft_slab_phase_times(b200fft_slab *slab, float *ms);
 /* Stream ordered, device pointers; input and output must not overlap.  workspace as for
  * b200fft_execute (NULL: context-owned scratch). */
 b200fft_status b200fft_execute_slab(b200fft_context *context, b200fft_slab *slab, const void *input,

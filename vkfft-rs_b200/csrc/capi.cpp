@@ -452,6 +452,21 @@ b200fft_status b200fft_slab_set_timeout(b200fft_slab *slab, uint64_t timeout_ns)
     });
 }
 
+b200fft_status b200fft_slab_set_phase_timing(b200fft_slab *slab, int32_t enabled) {
+    return guarded([&] {
+        need(slab, "slab");
+        slab_set_phase_timing(slab->s.get(), enabled != 0);
+    });
+}
+
+b200fft_status b200fft_slab_phase_times(b200fft_slab *slab, float *ms) {
+    return guarded([&] {
+        need(slab, "slab");
+        need(ms, "ms");
+        slab_phase_times(slab->s.get(), ms);
+    });
+}
+
 b200fft_status b200fft_slab_attach(b200fft_context *context, b200fft_slab *slab, void *handle) {
     return guarded([&] {
         need(context, "context");

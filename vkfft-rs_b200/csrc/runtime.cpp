@@ -187,7 +187,7 @@ static void *ensure_buffer(void *&buf, size_t &have, size_t need, const char *wh
 }
 
 void execute_program(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out, void *workspace,
-                     cudaStream_t stream, const PeerStore *peer) {
+                     cudaStream_t stream, const PeerStore *peer, cudaEvent_t before_last) {
     check(cudaSetDevice(ctx->device), "cudaSetDevice");
     std::lock_guard<std::mutex> l(ctx->mu);
     if (!stream) stream = ctx->stream;
@@ -202,6 +202,7 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
     const int variant = kernel_variant_for(prog.scalar_kind());
     for (size_t pi = 0; pi < prog.passes.size(); pi++) {
         const PassPlan &pp = prog.passes[pi];
+        if (before_last && pi + 1 == prog.passes.size()) check(cudaEventRecord(before_last, stream), "cudaEventRecord");
         if (pp.kernel == KERNEL_R2R) {
             R2rPass rr = pp.rr;
             rr.src = bufs[pp.src_buf];

@@ -59,8 +59,10 @@ void forget_program(uint64_t id);  // drop uploaded tables of a destroyed transf
 
 // Stream-ordered execution of a program on device pointers.  peer: the exchange
 // buffers of the ranks for passes marked peer_scatter (slab transforms only).
+// before_last: an event recorded on the stream just before the last pass is launched
+// (the slab's phase timing), or null.
 void execute_program(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out, void *workspace,
-                     cudaStream_t stream, const PeerStore *peer = nullptr);
+                     cudaStream_t stream, const PeerStore *peer = nullptr, cudaEvent_t before_last = nullptr);
 // Stream-ordered execution out of the library's static device region (allocates nothing).
 void execute_program_static(Context *ctx, uint64_t id, const Program &prog, const void *in, void *out,
                             cudaStream_t stream);

@@ -83,6 +83,12 @@ void release_slab_device(Slab *s) {
     if (s->ctx) {
         cudaSetDevice(s->ctx->device);
         cudaStreamSynchronize(s->ctx->stream);
+        for (void *&e : s->events)
+            if (e) {
+                cudaEventSynchronize(static_cast<cudaEvent_t>(e));
+                cudaEventDestroy(static_cast<cudaEvent_t>(e));
+                e = nullptr;
+            }
         for (int r = 0; r < s->nranks; r++)
             if (r != s->rank && s->peer_ptr[r]) cudaIpcCloseMemHandle(s->peer_ptr[r]);
         if (s->local) cudaFree(s->local);
@@ -146,6 +152,29 @@ void slab_connect(Context *ctx, Slab *s, const unsigned char *handles) {
     s->connected = true;
 }
 
+void slab_set_phase_timing(Slab *s, bool enabled) {
+    if (enabled && !s->ctx) fail_unsupported("attach the slab transform to a context before enabling phase timing");
+    if (enabled && !s->events[0]) {
+        check(cudaSetDevice(s->ctx->device), "cudaSetDevice");
+        for (void *&e : s->events) {
+            cudaEvent_t ev;
+            check(cudaEventCreate(&ev), "cudaEventCreate");
+            e = ev;
+        }
+    }
+    s->timing = enabled;
+}
+
+void slab_phase_times(Slab *s, float ms[4]) {
+    if (!s->timing || !s->events[0]) fail_unsupported("phase timing is not enabled on this slab transform");
+    check(cudaSetDevice(s->ctx->device), "cudaSetDevice");
+    check(cudaEventSynchronize(static_cast<cudaEvent_t>(s->events[4])), "cudaEventSynchronize");
+    for (int k = 0; k < 4; k++)
+        check(cudaEventElapsedTime(&ms[k], static_cast<cudaEvent_t>(s->events[k]),
+                                   static_cast<cudaEvent_t>(s->events[k + 1])),
+              "cudaEventElapsedTime");
+}
+
 void execute_slab(Context *ctx, Slab *s, const void *in, void *out, void *workspace, CUstream_st *stream) {
     if (s->ctx != ctx || !s->connected) fail_unsupported("slab transform is not connected on this context");
     check(cudaSetDevice(ctx->device), "cudaSetDevice");
@@ -154,7 +183,10 @@ void execute_slab(Context *ctx, Slab *s, const void *in, void *out, void *worksp
     const size_t buf_off = kFlagBytes + (epoch & 1) * s->buffer_bytes();
     PeerStore ps = s->peer;
     for (int r = 0; r < s->nranks; r++) ps.ptr[r] = static_cast<unsigned char *>(s->peer_ptr[r]) + buf_off;
-    execute_program(ctx, s->id_pre, s->pre, in, out, workspace, stream, &ps);
+    auto ev = [&](int k) { return s->timing ? static_cast<cudaEvent_t>(s->events[k]) : nullptr; };
+    if (s->timing) check(cudaEventRecord(ev(0), stream), "cudaEventRecord");
+    execute_program(ctx, s->id_pre, s->pre, in, out, workspace, stream, &ps, ev(1));
+    if (s->timing) check(cudaEventRecord(ev(2), stream), "cudaEventRecord");
     BarrierParams bp{};
     for (int r = 0; r < s->nranks; r++) bp.flags[r] = static_cast<unsigned *>(s->peer_ptr[r]);
     bp.rank = s->rank;
@@ -164,7 +196,9 @@ void execute_slab(Context *ctx, Slab *s, const void *in, void *out, void *worksp
     bp.timeout_ns = s->timeout_ns;
     slab_barrier_kernel<<<1, 32, 0, stream>>>(bp);
     check(cudaGetLastError(), "slab barrier launch");
+    if (s->timing) check(cudaEventRecord(ev(3), stream), "cudaEventRecord");
     execute_program(ctx, s->id_post, s->post, static_cast<unsigned char *>(s->local) + buf_off, out, workspace, stream);
+    if (s->timing) check(cudaEventRecord(ev(4), stream), "cudaEventRecord");
 }
 
 }  // namespace b200fft

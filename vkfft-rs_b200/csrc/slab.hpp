@@ -35,6 +35,10 @@ struct Slab {
     bool connected = false;
     unsigned epoch = 0;
     unsigned long long timeout_ns = 20ull * 1000000000ull;
+    // phase timing (b200fft_slab_set_phase_timing): events bracketing the local passes,
+    // the exchange pass, the barrier and the passes after it, recorded by every call
+    bool timing = false;
+    void *events[5] = {};  // cudaEvent_t, created on the attached context's device
 
     size_t buffer_bytes() const;
     ~Slab();
@@ -46,5 +50,9 @@ void slab_attach(Context *ctx, Slab *s, unsigned char *handle_out);
 void slab_connect(Context *ctx, Slab *s, const unsigned char *handles);
 void execute_slab(Context *ctx, Slab *s, const void *in, void *out, void *workspace, CUstream_st *stream);
 void release_slab_device(Slab *s);  // frees the exchange buffers and peer mappings (slab.cu)
+void slab_set_phase_timing(Slab *s, bool enabled);
+// Milliseconds of the last call's phases: [local passes, exchange pass, barrier, passes
+// after the exchange]; waits for that call to finish.
+void slab_phase_times(Slab *s, float ms[4]);
 
 }  // namespace b200fft

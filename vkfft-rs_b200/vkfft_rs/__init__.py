@@ -273,6 +273,8 @@ def library():
         "b200fft_slab_build": ([P(_Config), i32, u32, u32, P(_Device), P(vp)], i32),
         "b200fft_slab_destroy": ([vp], None),
         "b200fft_slab_get_info": ([vp, P(_SlabInfo)], i32),
+        "b200fft_slab_set_phase_timing": ([vp, i32], i32),
+        "b200fft_slab_phase_times": ([vp, P(ctypes.c_float)], i32),
         "b200fft_slab_set_timeout": ([vp, u64], i32),
         "b200fft_slab_attach": ([vp, vp, vp], i32),
         "b200fft_slab_connect": ([vp, vp, vp], i32),
@@ -883,6 +885,17 @@ class SlabTransform:
 
     def set_timeout(self, seconds):
         _check(library().b200fft_slab_set_timeout(self._h, int(seconds * 1e9)))
+
+    def set_phase_timing(self, enabled=True):
+        """Record CUDA events around the phases of every execution (after attach)."""
+        _check(library().b200fft_slab_set_phase_timing(self._h, int(bool(enabled))))
+
+    def phase_times(self):
+        """[local passes, exchange pass, barrier, passes after the exchange] of the last
+        execution, milliseconds (waits for it)."""
+        ms = (ctypes.c_float * 4)()
+        _check(library().b200fft_slab_phase_times(self._h, ms))
+        return [float(v) for v in ms]
 
     def attach(self, ctx):
         """Allocates the exchange buffers on ctx's device; returns this rank's handle."""
