@@ -475,6 +475,89 @@ def conv_section(args, ctx, dev, stream, ws, rank, dist):
             "parity": None if err is None else {"relL2_image0": err, "tol": 2e-6, "ok": err <= 2e-6}}
 
 
+# The reference's published pair-latency matrix (docs/PORTING_PLAN.md:281, RTX 4090, CUDA,
+# examples/native_benchmark.rs defaults: batch 64, 20 timed pairs after 3 warm-up pairs,
+# host-inclusive: each pair uploads the input, runs the forward and the normalised
+# inverse transform and downloads the result).  The N4089 rows plan with the portable
+# tuning on a device profile whose shared memory is cut to 32 / 16 KiB (the p29-FFT
+# witnesses, native_benchmark.rs:733-757).
+PUBLISHED_PAIRS = [
+    dict(n=4096, batch=64, ms=0.339), dict(n=103, batch=64, ms=0.657), dict(n=257, batch=64, ms=0.306),
+    dict(n=5760, batch=64, ms=0.507), dict(n=8192, batch=64, ms=0.572),
+    dict(n=4089, batch=64, ms=0.454, shared=32 * 1024), dict(n=4089, batch=64, ms=0.548, shared=16 * 1024),
+    dict(n=524288, batch=8, ms=99.107),
+]
+
+
+def run_published_pairs(args):
+    """bench.py --workload published-pairs: the reference's published cases, timed the way
+    its benchmark times them (host-inclusive forward + normalised inverse pairs through the
+    host API, wall clock) and device-resident (CUDA events), with the round-trip error."""
+    import torch
+    import vkfft_rs as V
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    ctx = V.CudaExecutionContext(local)
+    dev = ctx.device_profile()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = stream.cuda_stream
+    iters = args.steps
+    rows = []
+    for case in PUBLISHED_PAIRS:
+        n, batch = case["n"], case["batch"]
+        d = dev
+        cfg = V.FftConfig([n]).with_batch_count(batch)
+        if case.get("shared"):
+            d = dev.replace(shared_memory_bytes=case["shared"], shared_memory_pow2_bytes=case["shared"])
+            cfg = cfg.with_tuning(V.PlannerTuning.portable())
+        fwd = V.TransformIr.build(cfg, V.Direction.FORWARD, d)
+        inv = V.TransformIr.build(cfg.with_inverse_normalization(True), V.Direction.INVERSE, d)
+        idx = np.arange(n * batch, dtype=np.float32)
+        x = (np.sin(np.float32(0.0031) * idx) + idx * np.float32(1e-7)
+             + 1j * np.cos(np.float32(0.0023) * idx)).astype(np.complex64)
+        mid = np.empty_like(x)
+        back = np.empty_like(x)
+        for _ in range(max(args.warmup, 3)):
+            ctx.execute_transform(fwd, x, out=mid)
+            ctx.execute_transform(inv, mid, out=back)
+        t0 = time.perf_counter()
+        for _ in range(iters):
+            ctx.execute_transform(fwd, x, out=mid)
+            ctx.execute_transform(inv, mid, out=back)
+        host_ms = (time.perf_counter() - t0) / iters * 1e3
+        err = float(np.linalg.norm(back.astype(np.complex128) - x) / np.linalg.norm(x.astype(np.complex128)))
+        xd = torch.from_numpy(x.view(np.float32)).cuda()
+        yd = torch.empty_like(xd)
+        zd = torch.empty_like(xd)
+        wsb = torch.empty((max(fwd.workspace_bytes, inv.workspace_bytes, 1),), dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        res_ms = timed_steps(iters, args.warmup, stream,
+                             [lambda: ctx.execute_resident(fwd, xd.data_ptr(), yd.data_ptr(), wsb.data_ptr(), sp),
+                              lambda: ctx.execute_resident(inv, yd.data_ptr(), zd.data_ptr(), wsb.data_ptr(), sp)],
+                             None)
+        ctx.synchronize(sp)
+        kinds = [fwd.axis_child(0).kind.name]
+        rows.append({"n": n, "batch": batch, "shared_bytes": case.get("shared"), "algorithm": kinds[0],
+                     "host_pair_ms": host_ms, "resident_pair_ms": res_ms, "reference_rtx4090_host_pair_ms": case["ms"],
+                     "host_speedup_vs_published": case["ms"] / host_ms, "round_trip_rel_l2": err,
+                     "launches_per_pair": fwd.launch_count + inv.launch_count})
+    line = {"metric": "forward + normalised inverse pair latency, the reference's published matrix",
+            "value": statistics.mean(r["host_speedup_vs_published"] for r in rows), "unit": "x (geomean-free mean speed-up)",
+            "n_gpus": 1, "steps": iters, "warmup": args.warmup, "higher_is_better": True,
+            "vs_baseline": None, "dtype": "f32", "data": "the reference benchmark's deterministic input",
+            "config": {"workload": "published-pairs (docs/PORTING_PLAN.md:281; examples/native_benchmark.rs)",
+                       "timing": "host-inclusive: wall clock over the timed pairs through execute_transform "
+                                 "(pageable host arrays); resident: CUDA events",
+                       "reference_hardware": "RTX 4090 (CUDA), the reference's own figures"},
+            "cases": rows}
+    print(json.dumps(line))
+    ctx.close()
+    return 0
+
+
 def run_ours(args):
     import torch
     import vkfft_rs as V
@@ -897,12 +980,14 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true", help="profiling runs: no CPU baseline")
     ap.add_argument("--headline-only", action="store_true",
                     help="profiling runs: no config-3 slab / config-5 sharded sections")
-    ap.add_argument("--workload", default="c2c-4096", choices=["c2c-4096"] + sorted(WORKLOADS),
+    ap.add_argument("--workload", default="c2c-4096", choices=["c2c-4096", "published-pairs"] + sorted(WORKLOADS),
                     help="c2c-4096 is the headline (config 2); the others measure the remaining configs")
     args = ap.parse_args()
     BATCH = args.batch
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "published-pairs":
+        return run_published_pairs(args)
     if args.workload != "c2c-4096":
         return run_workload(args)
     return run_ours(args)

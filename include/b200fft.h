@@ -352,8 +352,14 @@ uint64_t b200fft_convolution_workspace_bytes(const b200fft_convolution *convolut
 int32_t b200fft_convolution_specialised_passes(const b200fft_convolution *convolution, int32_t *generic_passes);
 /* Element counts of the input / output arrays (real for the ND real convolution, complex
  * for ConvolutionIr / NdConvolutionIr). */
+/* Logical elements of the host API's arrays (input C * full real tensor, output K * C). */
 uint64_t b200fft_convolution_input_elements(const b200fft_convolution *convolution);
 uint64_t b200fft_convolution_output_elements(const b200fft_convolution *convolution);
+/* Elements of the device buffers b200fft_execute_convolution reads and writes: the
+ * formatted layouts when the config sets buffer strides (scalar K = 1 ND real
+ * convolution, convolution_ir.rs:3922-3928), else the logical counts. */
+uint64_t b200fft_convolution_input_buffer_elements(const b200fft_convolution *convolution);
+uint64_t b200fft_convolution_output_buffer_elements(const b200fft_convolution *convolution);
 int32_t b200fft_convolution_input_is_real(const b200fft_convolution *convolution);
 /* execute_nd_real_convolution_f32/f64 on device pointers (stream ordered). */
 b200fft_status b200fft_execute_convolution(b200fft_context *context, b200fft_convolution *convolution,

@@ -145,29 +145,54 @@ def next_smooth_at_least(target):
 
 
 def convolve_nd(x, kernel_spectrum, dims, coordinates=1, kernels=1, conjugate_sequence=False,
-                cross_power=False, threads=None):
-    """ND real FFT convolution (NdRealConvolutionIr, convolution_ir.rs:3867-4250): R2C of the
-    ``coordinates`` images, per output system (k, c) the product
-    policy(seq[c]) * kernel[k*C + c] (convolution_ir.rs:36-86; sequence conjugation and
-    cross-power normalisation p / |p| as vulkan.rs:17846-17873 emits it), then a normalised
-    C2R of the K*C systems.  ``kernel_spectrum`` holds K*C compact spectra or one that every
-    system shares."""
+                cross_power=False, matrix=0, symmetric=False, pads=None, threads=None):
+    """ND real FFT convolution (NdRealConvolutionIr, execute_nd_real_convolution_ir,
+    convolution_ir.rs:4192-4250): R2C of the ``coordinates`` images (each masked to zero on
+    the padding intervals ``pads`` {axis: (lo, hi)} first, the forward zero-pad pass), per
+    output system the product -- independent / scalar: policy(seq[c]) * kernel[k*C + c];
+    matrix (``matrix`` = 2 or 3 coordinates): sum over ic of prep(seq[ic]) *
+    kernel[k*planes + plane(oc, ic)] then the cross-power normalisation -- then a normalised
+    C2R of the K*C systems, masked on the padding intervals (the inverse zero-pad pass).
+    Sequence conjugation and cross-power normalisation p / |p| as vulkan.rs:17846-17873
+    emits them.  ``kernel_spectrum`` holds the reference layout (K*C, or K*planes for a
+    matrix, compact spectra) or, for independent coordinates, one spectrum every system
+    shares."""
     dims = tuple(dims)
     C, K = coordinates, kernels
-    seq = r2c_nd(np.asarray(x, dtype=np.float64).reshape((C,) + dims), len(dims), threads=threads)
+    mask = None
+    if pads:
+        mask = np.zeros(dims, dtype=bool)
+        for axis, (lo, hi) in pads.items():
+            idx = [slice(None)] * len(dims)
+            idx[int(axis)] = slice(lo, hi)
+            mask[tuple(idx)] = True
+    xr = np.asarray(x, dtype=np.float64).reshape((C,) + dims)
+    if mask is not None:
+        xr = np.where(mask, 0.0, xr)
+    seq = r2c_nd(xr, len(dims), threads=threads)
     seq = seq.reshape(C, -1)
     L = seq.shape[1]
     ker = np.asarray(kernel_spectrum, dtype=np.complex128).reshape(-1, L)
+    prep = (lambda v: np.conj(v)) if conjugate_sequence else (lambda v: v)
+    norm = (lambda p: p / np.sqrt(p.real * p.real + p.imag * p.imag)) if cross_power else (lambda p: p)
     out = np.empty((K * C, L), dtype=np.complex128)
-    for k in range(K):
-        for c in range(C):
-            s = np.conj(seq[c]) if conjugate_sequence else seq[c]
-            p = s * (ker[k * C + c] if ker.shape[0] > 1 else ker[0])
-            if cross_power:
-                p = p / np.sqrt(p.real * p.real + p.imag * p.imag)
-            out[k * C + c] = p
+    if matrix:
+        planes = matrix * (matrix + 1) // 2 if symmetric else matrix * matrix
+        for k in range(K):
+            for oc in range(matrix):
+                acc = np.zeros(L, dtype=np.complex128)
+                for ic in range(matrix):
+                    acc += prep(seq[ic]) * ker[k * planes + conv_plane(matrix, symmetric, oc, ic)]
+                out[k * matrix + oc] = norm(acc)
+    else:
+        for k in range(K):
+            for c in range(C):
+                out[k * C + c] = norm(prep(seq[c]) * (ker[k * C + c] if ker.shape[0] > 1 else ker[0]))
     half = dims[:-1] + (dims[-1] // 2 + 1,)
-    return c2r_nd(out.reshape((K * C,) + half), dims[-1], len(dims), normalize=True, threads=threads)
+    y = c2r_nd(out.reshape((K * C,) + half), dims[-1], len(dims), normalize=True, threads=threads)
+    if mask is not None:
+        y = np.where(mask, 0.0, y)
+    return y
 
 
 def conv_plane(m, symmetric, oc, ic):

@@ -39,7 +39,8 @@ B200FFT_HD void conv_multiply_one(const ConvMultiply &m, int64_t L) {
             r.y += p.y;
         }
     } else {
-        r = mul(prep(spec[in_s * m.T + i]), ker[kid * m.T + i]);
+        const int64_t kt = m.shared_kernel ? 0 : kid * m.C + oc;
+        r = mul(prep(spec[(in_s * m.C + oc) * m.T + i]), ker[kt * m.T + i]);
     }
     if (m.cross_power) {
         const T k = T(1) / sqrt(r.x * r.x + r.y * r.y);

@@ -371,6 +371,7 @@ b200fft_status b200fft_convolution_build(const b200fft_config *config, const b20
 void b200fft_convolution_destroy(b200fft_convolution *convolution) {
     if (!convolution) return;
     forget_program(convolution->c->id);
+    if (convolution->c->dense_twin) forget_program(convolution->c->dense_twin->id);
     delete convolution;
 }
 
@@ -404,8 +405,9 @@ b200fft_status b200fft_execute_convolution_host(b200fft_context *context, b200ff
         need(convolution, "convolution");
         need(input, "input");
         need(output, "output");
-        execute_program_host(context->ctx, convolution->c->id, convolution->c->prog, input, input_bytes, output,
-                             output_bytes);
+        // host arrays are logical tensors: a formatted convolution runs its dense twin
+        const Convolution &cv = convolution->c->dense_twin ? *convolution->c->dense_twin : *convolution->c;
+        execute_program_host(context->ctx, cv.id, cv.prog, input, input_bytes, output, output_bytes);
     });
 }
 
@@ -542,6 +544,10 @@ void b200fft_ticket_destroy(b200fft_ticket *ticket) {
     delete ticket;
 }
 
-uint64_t b200fft_convolution_input_elements(const b200fft_convolution *c) { return c ? c->c->prog.input_elems : 0; }
-uint64_t b200fft_convolution_output_elements(const b200fft_convolution *c) { return c ? c->c->prog.output_elems : 0; }
+uint64_t b200fft_convolution_input_elements(const b200fft_convolution *c) { return c ? c->c->logical_in_elems : 0; }
+uint64_t b200fft_convolution_output_elements(const b200fft_convolution *c) { return c ? c->c->logical_out_elems : 0; }
+uint64_t b200fft_convolution_input_buffer_elements(const b200fft_convolution *c) { return c ? c->c->prog.input_elems : 0; }
+uint64_t b200fft_convolution_output_buffer_elements(const b200fft_convolution *c) {
+    return c ? c->c->prog.output_elems : 0;
+}
 int32_t b200fft_convolution_input_is_real(const b200fft_convolution *c) { return c ? c->c->prog.input_real : 0; }

@@ -120,8 +120,8 @@ static std::unique_ptr<Convolution> build_c2c_convolution(const FftConfig &c, co
 
     Program &prog = conv->prog;
     prog.is_double = dbl;
-    prog.input_elems = B * C * T;
-    prog.output_elems = out_systems * C * T;
+    prog.input_elems = conv->logical_in_elems = B * C * T;
+    prog.output_elems = conv->logical_out_elems = out_systems * C * T;
     int same[2 + kScratchBuffers];
     for (int k = 0; k < 2 + kScratchBuffers; k++) same[k] = k;
     append_program(prog, conv->forward->prog, same);  // spectrum of the input systems -> out
@@ -155,6 +155,121 @@ static std::unique_ptr<Convolution> build_c2c_convolution(const FftConfig &c, co
     return conv;
 }
 
+// Checks a user kernel spectrum of `n_scalars` values for non-finite entries.
+static void check_spectrum_finite(const void *spectrum, size_t n_scalars, bool dbl) {
+    for (size_t k = 0; k < n_scalars; k++) {
+        const double v = dbl ? static_cast<const double *>(spectrum)[k] : (double)static_cast<const float *>(spectrum)[k];
+        if (!std::isfinite(v)) fail_invalid_ir("convolution kernel spectrum contains non-finite values");
+    }
+}
+
+// ND real convolution in its general ownerships (NdRealConvolutionIr::build_from_spectrum,
+// convolution_ir.rs:3884-4059): 2x2 / 3x3 matrix coordinates, zero padding (matrix,
+// independent or scalar ownership) and formatted buffer strides (scalar, K = 1).  As the
+// reference composes it: the forward R2C of the C coordinate systems (the config's zero
+// padding and input strides, output dense), the multiply of the compact spectra into the
+// K * C output systems (matrix, independent or scalar, with the conjugation / cross-power
+// policy), the normalised C2R of the output systems (zero padding, output strides).  The
+// three programs are concatenated into one launch list: forward output -> scratch 6,
+// multiply -> scratch 7, inverse input <- scratch 7.  The unpadded independent case keeps
+// the fused program of build_convolution below.
+static std::unique_ptr<Convolution> build_real_convolution_generic(const FftConfig &c, const DeviceProfile &device,
+                                                                   const void *spectrum, uint64_t copies) {
+    const size_t rank = c.dimensions.size();
+    const int M = c.matrix_convolution > 1 ? (int)c.matrix_convolution : 0;
+    const size_t C = c.coordinate_features, K = c.convolution_kernel_count;
+    const size_t W = c.dimensions[rank - 1];
+    std::vector<size_t> compact = c.dimensions;
+    compact[rank - 1] = W / 2 + 1;
+    const size_t L = prod(compact, 0, rank);
+    const size_t planes = M ? (c.symmetric_convolution_kernel ? (size_t)(M * (M + 1) / 2) : (size_t)(M * M)) : 1;
+    const size_t expect = M ? K * planes : K * C;
+    const bool shared = !M && copies == 1 && expect > 1;
+    if (copies != expect && !shared)
+        throw FftError(B200FFT_INPUT_LENGTH_MISMATCH, "input contains " + std::to_string(copies * L) +
+                                                          " complex elements but kernel expects " +
+                                                          std::to_string(expect * L));
+    const bool dbl = c.precision == Precision::F64;
+    const size_t esz = dbl ? 16 : 8;
+    check_spectrum_finite(spectrum, copies * L * 2, dbl);
+    auto conv = std::make_unique<Convolution>();
+    static std::atomic<uint64_t> next_id{1ull << 43};
+    conv->id = next_id++;
+    conv->config = c;
+    conv->device = device;
+    conv->spectrum_elems = L;
+    FftConfig fc = c;
+    fc.perform_convolution = false;
+    fc.convolution_conjugation = ConvolutionConjugation::None;
+    fc.cross_power_spectrum_normalization = false;
+    fc.coordinate_features = 1;
+    fc.matrix_convolution = 1;
+    fc.symmetric_convolution_kernel = false;
+    fc.convolution_kernel_count = 1;
+    fc.batch_count = C;
+    fc.normalize_inverse = false;
+    fc.output_buffer_axis_strides.assign(rank, std::nullopt);
+    fc.output_buffer_batch_stride.reset();
+    conv->forward = build_transform(fc, B200FFT_FORWARD, device);
+    FftConfig ic = fc;
+    ic.transform = TransformKind::C2R;
+    ic.batch_count = K * C;
+    ic.normalize_inverse = true;
+    ic.input_buffer_axis_strides.assign(rank, std::nullopt);
+    ic.input_buffer_batch_stride.reset();
+    ic.output_buffer_axis_strides = c.output_buffer_axis_strides;
+    ic.output_buffer_batch_stride = c.output_buffer_batch_stride;
+    conv->inverse = build_transform(ic, B200FFT_INVERSE, device);
+
+    Program &prog = conv->prog;
+    prog.is_double = dbl;
+    prog.input_real = prog.output_real = true;
+    prog.input_elems = conv->forward->prog.input_elems;
+    prog.output_elems = conv->inverse->prog.output_elems;
+    conv->logical_in_elems = conv->forward->logical_in_elems;
+    conv->logical_out_elems = conv->inverse->logical_out_elems;
+    int fwd_map[2 + kScratchBuffers], inv_map[2 + kScratchBuffers];
+    for (int k = 0; k < 2 + kScratchBuffers; k++) fwd_map[k] = inv_map[k] = k;
+    fwd_map[BUF_OUT] = BUF_SCRATCH6;
+    inv_map[BUF_IN] = BUF_SCRATCH7;
+    append_program(prog, conv->forward->prog, fwd_map);
+    HostTable st;
+    st.is_raw = true;
+    st.raw.assign(static_cast<const unsigned char *>(spectrum),
+                  static_cast<const unsigned char *>(spectrum) + copies * L * esz);
+    prog.tables.push_back(std::move(st));
+    PassPlan mp{};
+    mp.kernel = KERNEL_CMUL;
+    mp.reg_table = (int)prog.tables.size() - 1;
+    mp.cm.T = (int64_t)L;
+    mp.cm.total = (int64_t)(K * C * L);
+    mp.cm.C = (int32_t)C;
+    mp.cm.K = (int32_t)K;
+    mp.cm.matrix = M;
+    mp.cm.symmetric = c.symmetric_convolution_kernel ? 1 : 0;
+    mp.cm.planes = (int32_t)planes;
+    mp.cm.conj_seq = c.convolution_conjugation == ConvolutionConjugation::Sequence ? 1 : 0;
+    mp.cm.cross_power = c.cross_power_spectrum_normalization ? 1 : 0;
+    mp.cm.shared_kernel = shared ? 1 : 0;
+    mp.src_buf = BUF_SCRATCH6;
+    mp.dst_buf = BUF_SCRATCH7;
+    mp.label = "convolution multiply";
+    for (auto &row : mp.op_tables) row[0] = row[1] = row[2] = -1;
+    prog.passes.push_back(mp);
+    append_program(prog, conv->inverse->prog, inv_map);
+    prog.scratch_elems[6] = std::max(prog.scratch_elems[6], std::max(C * L, conv->forward->prog.output_elems));
+    prog.scratch_elems[7] = std::max(prog.scratch_elems[7], std::max(K * C * L, conv->inverse->prog.input_elems));
+    if (c.has_formatted_strides()) {
+        FftConfig dense = c;
+        dense.input_buffer_axis_strides.assign(rank, std::nullopt);
+        dense.output_buffer_axis_strides.assign(rank, std::nullopt);
+        dense.input_buffer_batch_stride.reset();
+        dense.output_buffer_batch_stride.reset();
+        conv->dense_twin = build_real_convolution_generic(dense, device, spectrum, copies);
+    }
+    return conv;
+}
+
 std::unique_ptr<Convolution> build_convolution(const FftConfig &config_in, const DeviceProfile &device,
                                                const void *spectrum, uint64_t copies) {
     config_in.validate();
@@ -167,13 +282,34 @@ std::unique_ptr<Convolution> build_convolution(const FftConfig &config_in, const
         config_in.dimensions.size() < 2 || config_in.batch_count != 1)
         fail_unsupported(
             "multidimensional real performConvolution IR requires batch1 ND R2C application ownership");
-    if (config_in.matrix_convolution > 1)
-        fail_unsupported("B200 engine: matrix convolution is not implemented yet");
+    // ownership rules of NdRealConvolutionIr::build_from_spectrum (convolution_ir.rs:3899-3937)
+    const int Mx = config_in.matrix_convolution > 1 ? (int)config_in.matrix_convolution : 0;
+    if (Mx && Mx != 2 && Mx != 3) fail_invalid_ir("matrix convolution IR requires a 2x2 or 3x3 matrix");
+    if (Mx == 3 && config_in.symmetric_convolution_kernel)
+        fail_unsupported(
+            "pinned VkFFT 1.3.4 3x3 symmetric-kernel code aliases yz and zz while the API guide documents six planes");
+    if (Mx && config_in.coordinate_features != (size_t)Mx)
+        fail_unsupported(
+            "multidimensional real performConvolution IR supports batch1 independent-coordinate or matrix K=1/K>1 "
+            "ownership");
+    for (size_t a = 0; a < config_in.omit_dimension.size(); a++)
+        if (config_in.omit_dimension[a])
+            fail_unsupported(
+                "multidimensional real performConvolution currently requires active dimensions without omitDimension");
+    if (config_in.has_formatted_strides() &&
+        (config_in.coordinate_features != 1 || config_in.convolution_kernel_count != 1 || Mx))
+        fail_unsupported("multidimensional real formatted performConvolution currently requires scalar batch1 K1");
+    bool padded = false;
+    for (auto &z : config_in.zero_padding) padded |= z.has_value();
+    if (padded && Mx && config_in.symmetric_convolution_kernel)
+        fail_unsupported(
+            "multidimensional real performConvolution zero padding requires batch1/K1 nonsymmetric matrix ownership");
+    if (config_in.convolution_conjugation == ConvolutionConjugation::Kernel)
+        fail_unsupported("kernel-conjugated convolution is not executable in the pinned VkFFT codegen");
     if (!(config_in.precision == Precision::F32 || config_in.precision == Precision::F64))
         fail_precision("B200 engine", precision_name(config_in.precision));
-    for (auto &z : config_in.zero_padding)
-        if (z) fail_unsupported("B200 engine: zero padding is not implemented yet");
-    if (config_in.has_formatted_strides()) fail_unsupported("B200 engine: formatted buffer strides are not implemented yet");
+    if (Mx || padded || config_in.has_formatted_strides())
+        return build_real_convolution_generic(config_in.resolve_tuning_for_device(device), device, spectrum, copies);
     const FftConfig c = config_in.resolve_tuning_for_device(device);
     auto conv = std::make_unique<Convolution>();
     static std::atomic<uint64_t> next_id{1ull << 40};
@@ -218,8 +354,8 @@ std::unique_ptr<Convolution> build_convolution(const FftConfig &config_in, const
     prog.is_double = dbl;
     prog.input_real = true;
     prog.output_real = true;
-    prog.input_elems = C * full;
-    prog.output_elems = K * C * full;
+    prog.input_elems = conv->logical_in_elems = C * full;
+    prog.output_elems = conv->logical_out_elems = K * C * full;
     HostTable st;
     st.is_raw = true;
     const size_t esz = dbl ? 16 : 8;

@@ -41,6 +41,7 @@ struct Entry {
     TransformKind kind;
     bool rec = false;   // recursive FFT-Rader tuning
     bool conv = false;  // ND real convolution, batch = coordinate features
+    size_t shared = 0;  // planner device with this much shared memory, portable tuning
 };
 
 PlannerTuning rec_tuning() {
@@ -73,6 +74,10 @@ std::vector<Entry> catalogue() {
         // the reference's published pair-timing lengths (docs/PORTING_PLAN.md:281)
         for (size_t n : {103, 257, 5760, 4089}) e.push_back({{n}, 64, p, C2C});
         e.push_back({{4089}, 64, p, C2C, true});
+        // its p29-FFT witnesses: portable tuning on 32 / 16 KiB of planner shared memory
+        // (examples/native_benchmark.rs:733-757)
+        e.push_back({{4089}, 64, p, C2C, false, false, 32 * 1024});
+        e.push_back({{4089}, 64, p, C2C, false, false, 16 * 1024});
         // family representatives: Rader direct / FFT, Bluestein fused / three-pass,
         // mixed radix, four-step, composite Rader
         for (size_t n : {17, 47, 89, 97, 360, 1000, 1536, 2187, 2401, 3125, 2288, 6000, 10000, 4106, 8191,
@@ -135,6 +140,11 @@ int main(int argc, char **argv) {
         cfg.precision = en.prec;
         cfg.transform = en.kind;
         if (en.rec) cfg.with_tuning(rec_tuning());
+        DeviceProfile d = dev;
+        if (en.shared) {
+            d.shared_memory_bytes = d.shared_memory_pow2_bytes = en.shared;
+            cfg.with_tuning(PlannerTuning::portable());
+        }
         try {
             if (en.conv) {
                 cfg.batch_count = 1;
@@ -153,7 +163,7 @@ int main(int argc, char **argv) {
                 FftConfig c = cfg;
                 c.normalize_inverse = norm;
                 if (dir == 1 && en.kind == TransformKind::R2C) c.transform = TransformKind::C2R;
-                auto t = build_transform(c, dir, dev);
+                auto t = build_transform(c, dir, d);
                 add_program(t->prog, by_nt, keep, passes);
             }
             if (en.dims.size() == 3 && en.kind == TransformKind::C2C && en.dims[0] % 8 == 0 && en.batch == 1) {

@@ -134,10 +134,12 @@ struct PassParams : PassShape {
 // Convolution multiply (convolution_ir.rs:36-151, :4252-4440): out system s, coordinate
 // oc, element i of a T-element tensor:
 //   matrix:   sum_ic prep(spec[(in_s C + ic) T + i]) ker[(kid planes + plane(oc, ic)) T + i]
-//   scalar:   prep(spec[in_s T + i]) ker[kid T + i]
+//   scalar:   prep(spec[(in_s C + oc) T + i]) ker[(kid C + oc) T + i]
 // with in_s = 0, kid = s for K > 1 (one input system fanned out to K kernels) and in_s = s,
-// kid = 0 otherwise; prep conjugates the sequence (Sequence policy) and the product is
-// divided by its modulus with cross-power normalisation.
+// kid = 0 otherwise (C = 1 for the C2C scalar case; C > 1 is the ND real path's
+// independent coordinates); a shared kernel is one tensor for every (kid, oc).  prep
+// conjugates the sequence (Sequence policy) and the product is divided by its modulus
+// with cross-power normalisation.
 struct ConvMultiply {
     const void *src;
     void *dst;
@@ -151,7 +153,7 @@ struct ConvMultiply {
     int32_t planes;       // kernel planes per kernel set
     int32_t conj_seq;
     int32_t cross_power;
-    int32_t _pad;
+    int32_t shared_kernel;  // scalar: one kernel tensor for every output system
 };
 
 // DCT / DST of one axis (r2r_ir.rs:621-1110) as pre pass -> complex FFT of length L ->

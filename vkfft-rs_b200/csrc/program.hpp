@@ -26,8 +26,10 @@ enum BufId : int {
     BUF_SCRATCH3 = 5,  // pass-level Rader lines
     BUF_SCRATCH4 = 6,  // dense input behind a boundary copy (zero padding / formatted strides)
     BUF_SCRATCH5 = 7,  // dense output in front of a boundary copy
+    BUF_SCRATCH6 = 8,  // convolution: spectrum of the input systems
+    BUF_SCRATCH7 = 9,  // convolution: product spectra of the output systems
 };
-constexpr int kScratchBuffers = 6;
+constexpr int kScratchBuffers = 8;
 
 struct HostTable {
     bool is_int = false;

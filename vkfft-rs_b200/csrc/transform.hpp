@@ -44,6 +44,10 @@ struct Convolution {
     std::unique_ptr<Transform> inverse;  // normalised C2R
     Program prog;                        // forward + multiply + inverse, one launch list
     size_t spectrum_elems = 0;           // complex elements of one spectrum copy
+    // logical (host-API) element counts; prog.input_elems / output_elems are the device
+    // buffers', which differ with formatted strides
+    size_t logical_in_elems = 0, logical_out_elems = 0;
+    std::unique_ptr<Convolution> dense_twin;  // same convolution on dense buffers (host API)
 };
 
 std::unique_ptr<Convolution> build_convolution(const FftConfig &config, const DeviceProfile &device,

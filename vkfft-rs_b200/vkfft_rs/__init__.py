@@ -268,6 +268,8 @@ def library():
         "b200fft_convolution_input_elements": ([vp], u64),
         "b200fft_convolution_output_elements": ([vp], u64),
         "b200fft_convolution_input_is_real": ([vp], i32),
+        "b200fft_convolution_input_buffer_elements": ([vp], u64),
+        "b200fft_convolution_output_buffer_elements": ([vp], u64),
         "b200fft_execute_convolution": ([vp, vp, vp, vp, vp, vp], i32),
         "b200fft_execute_convolution_host": ([vp, vp, vp, ctypes.c_size_t, vp, ctypes.c_size_t], i32),
         "b200fft_slab_build": ([P(_Config), i32, u32, u32, P(_Device), P(vp)], i32),
@@ -765,6 +767,8 @@ class _ConvolutionApplication:
         self.input_elements = int(lib.b200fft_convolution_input_elements(handle))
         self.output_elements = int(lib.b200fft_convolution_output_elements(handle))
         self.input_is_real = bool(lib.b200fft_convolution_input_is_real(handle))
+        self.input_buffer_elements = int(lib.b200fft_convolution_input_buffer_elements(handle))
+        self.output_buffer_elements = int(lib.b200fft_convolution_output_buffer_elements(handle))
 
     @classmethod
     def _build(cls, config, kernel_spectrum, device, plane_elems):
