@@ -162,6 +162,43 @@ int table_stage_twiddles(Program &prog, size_t R, size_t P) {
     return add_table(prog, key, std::move(t));
 }
 
+// Rader line kernel table (reg_kernels.cu reg_rader_kernel): FFT_{P-1} of the Rader
+// kernel b[q] = W_P^(g^-q mod P), divided by P - 1, with g the smallest primitive root of
+// P; evaluated in binary128 from exactly reduced ratios.
+int table_rader_line(Program &prog, size_t P) {
+    std::string key = "rline" + std::to_string(P);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
+    const size_t L = P - 1;
+    size_t g = 2;
+    for (;; g++) {
+        size_t v = 1, order = 0;
+        do {
+            v = v * g % P;
+            order++;
+        } while (v != 1);
+        if (order == L) break;
+    }
+    size_t ginv = 1;
+    for (size_t k = 0; k < P - 2; k++) ginv = ginv * g % P;
+    std::vector<size_t> r(L);  // g^-q mod P
+    size_t v = 1;
+    for (size_t q = 0; q < L; q++, v = v * ginv % P) r[q] = v;
+    HostTable t;
+    for (size_t k = 0; k < L; k++) {
+        QC acc{0, 0};
+        for (size_t q = 0; q < L; q++) {
+            const QC b = root_q(r[q], P), w = root_q((q * k) % L, L);
+            acc.re += b.re * w.re - b.im * w.im;
+            acc.im += b.re * w.im + b.im * w.re;
+        }
+        acc.re /= (q128)L;
+        acc.im /= (q128)L;
+        put_q(t, k, acc);
+    }
+    return add_table(prog, key, std::move(t));
+}
+
 // Four-step twiddles W_N^{c e} for line (column) c < ncols and element e < nrows, stored
 // element-major (entry e*ncols + c): lines-fastest passes read consecutive entries.
 int table_twiddle_transposed(Program &prog, size_t ncols, size_t nrows, size_t N) {
@@ -1060,6 +1097,34 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
                     pp.label = "register stockham (bulk prefetch)";
                 }
             }
+            for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
+            prog.passes.push_back(pp);
+            return;
+        }
+    }
+
+    // Strided prime lines whose Rader convolution is one codelet FFT: one thread per
+    // line, Rader's algorithm in registers (reg_rader_kernel)
+    if (alg->kind == AlgorithmKind::Rader && strided && reg_kernels_enabled() && !job.in_real && !job.in_herm &&
+        !job.out_real && out_count == N && alg->primes.size() == 1 && alg->primes[0].prime == N) {
+        const int rv = reg_variant(prog, N, REG_RADER_LINE, true);
+        if (rv >= 0) {
+            PassPlan pp{};
+            pp.kernel = KERNEL_REG;
+            pp.reg_variant = rv;
+            pp.reg_table = table_rader_line(prog, N);
+            pp.rp.nlines = no * S;
+            pp.rp.ni = S;
+            pp.rp.src = RegSide{job.in_os, 1, S};
+            pp.rp.dst = RegSide{job.out_os, 1, So};
+            pp.rp.scale = scale;
+            pp.rp.conj = inv ? 1 : 0;
+            pp.rp.n = (int32_t)N;
+            pp.src_buf = job.in_buf;
+            pp.src_off = job.in_off;
+            pp.dst_buf = job.out_buf;
+            pp.dst_off = job.out_off;
+            pp.label = "register rader line";
             for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
             prog.passes.push_back(pp);
             return;

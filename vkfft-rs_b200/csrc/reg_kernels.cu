@@ -665,6 +665,70 @@ __global__ void __launch_bounds__(G *(N / E), MINB) reg_fft_persistent(const __g
     if (threadIdx.x == 0 && in_flight && !bar_wait(bar, parity)) atomicOr(rp.err, 64);
 }
 
+// ---- Rader lines in registers ---------------------------------------------------------
+// One thread per line of prime length P (the strided higher axes of the ND configs, e.g.
+// the 17-point axis of [1024, 17, 65537]): the P points are loaded straight into
+// registers (a warp reads 32 neighbouring lines of the same position: coalesced), and
+// Rader's algorithm (rader_ir.rs: generator permutation, cyclic convolution of length
+// P - 1 through the codelet FFT, x0 added back) runs without shared memory:
+//   a[q] = x[g^q],  A = FFT(a),  X[0] = x[0] + A[0],
+//   c = IFFT(A * FFT(b)),  b[q] = W_P^(g^-q),  X[g^-m] = x[0] + c[m],
+// with the inverse FFT as conj(FFT(conj .)) and rp.tw = FFT(b) / (P - 1) (lower.cpp
+// table_rader_line).  g is the smallest primitive root of P; the permutations are
+// compile-time constants, so every register index folds.
+__host__ __device__ constexpr int pow_mod(int g, int e, int p) {
+    int r = 1;
+    for (int k = 0; k < e; k++) r = r * g % p;
+    return r;
+}
+__host__ __device__ constexpr int smallest_primitive_root(int p) {
+    for (int g = 2; g < p; g++) {
+        bool ok = true;
+        for (int e = 1; e < p - 1; e++)
+            if (pow_mod(g, e, p) == 1) ok = false;
+        if (ok) return g;
+    }
+    return 1;
+}
+
+template <typename T, int P, int G>
+__global__ void __launch_bounds__(G) reg_rader_kernel(const __grid_constant__ RegParams rp) {
+    constexpr int L = P - 1;
+    constexpr int g = smallest_primitive_root(P);
+    constexpr int ginv = pow_mod(g, P - 2, P);  // g^-1 mod P
+    const int64_t line = (int64_t)blockIdx.x * G + threadIdx.x;
+    if (line >= rp.nlines) return;
+    const int64_t o = rp.ni == 1 ? line : line / rp.ni;
+    const int64_t i = line - o * rp.ni;
+    const int64_t ib = o * rp.src.os + i * rp.src.is, ob = o * rp.dst.os + i * rp.dst.is;
+    cplx<T> x[P];
+#pragma unroll
+    for (int p = 0; p < P; p++) {
+        x[p] = ld_c<T>(rp.in, ib + (int64_t)p * rp.src.es);
+        if (rp.conj) x[p].y = -x[p].y;
+    }
+    cplx<T> a[L];
+#pragma unroll
+    for (int q = 0; q < L; q++) a[q] = x[pow_mod(g, q, P)];
+    dft<L, T>(a);
+    const cplx<T> x0 = x[0];
+    const cplx<T> X0 = {x0.x + a[0].x, x0.y + a[0].y};
+    const cplx<T> *B = reinterpret_cast<const cplx<T> *>(rp.tw);
+#pragma unroll
+    for (int k = 0; k < L; k++) {
+        const cplx<T> y = mul(a[k], tw_load(B, k));
+        a[k] = {y.x, -y.y};
+    }
+    dft<L, T>(a);  // conj(c[m]) in a[m]
+    const T s = T(rp.scale);
+    auto put = [&](int k, cplx<T> v) {
+        st_c<T>(rp.out, ob + (int64_t)k * rp.dst.es, cplx<T>{v.x * s, rp.conj ? -v.y * s : v.y * s});
+    };
+    put(0, X0);
+#pragma unroll
+    for (int m = 0; m < L; m++) put(pow_mod(ginv, m, P), cplx<T>{x0.x + a[m].x, x0.y - a[m].y});
+}
+
 }  // namespace regk
 
 // ---- variant table ----------------------------------------------------------------
@@ -732,6 +796,9 @@ static const RegVariant kRegVariants[] = {
     RV(double, REG_C2C, true, 256, 16, 16, 16, 16), RV(double, REG_C2C, true, 512, 16, 8, 16, 16, 2),
     RV(double, REG_C2C, true, 1024, 16, 4, 16, 16, 4), RV(double, REG_C2C, true, 2048, 16, 4, 16, 16, 8),
     RV(double, REG_C2C, true, 4096, 16, 2, 16, 16, 16),
+    // Rader lines in registers (one thread per line, strided higher axes)
+    {0, 17, REG_RADER_LINE, 1, 128, 128, 0, (const void *)regk::reg_rader_kernel<float, 17, 128>, {16}, 0},
+    {1, 17, REG_RADER_LINE, 1, 128, 128, 0, (const void *)regk::reg_rader_kernel<double, 17, 128>, {16}, 0},
     RV_STRIDED(float, REG_C2C_PEER),
     RV_STRIDED(double, REG_C2C_PEER),
     RV_STRIDED(float, REG_CONV),

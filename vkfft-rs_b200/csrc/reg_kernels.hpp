@@ -24,6 +24,8 @@ enum RegMode : int32_t {
     REG_R2R_HALF = 8, // DCT/DST-II/III of a contiguous line of n = 2N reals: the reduction's real
                       // length-n sequence through the even-half algebra, FFT of length N;
                       // tw2 = [W_n^k | W_4n^k], k = 0..N
+    REG_RADER_LINE = 9,  // prime-length lines, one thread per line: Rader's algorithm in registers
+                         // (N = P; tw = FFT_{P-1} of the Rader kernel / (P - 1))
 };
 
 // Line l = o * ni + i; element p of the line is at o*os + i*is + p*es (units of the
