@@ -48,7 +48,9 @@ def test_catalogue_covers_every_generic_pass(V, kind, dims, batch, prec, tuning)
             continue
         ir = V.TransformIr.build(cfg.with_inverse_normalization(norm), direction, profile(V))
         covered, total = ir.specialised_passes
-        assert total >= 1 and covered == total, (dims, direction, covered, total)
+        # every generic pass is specialised (the BASELINE 65537 / 17 axes have none left:
+        # they run the register kernels)
+        assert covered == total, (dims, direction, covered, total)
 
 
 def test_config5_convolution_is_covered(V):

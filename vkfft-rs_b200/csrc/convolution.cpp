@@ -44,6 +44,7 @@ static void append_program(Program &dst, const Program &src, const int (&remap)[
                 if (id >= 0) id += off;
         if (pp.reg_table >= 0) pp.reg_table += off;
         if (pp.reg_table2 >= 0) pp.reg_table2 += off;
+        if (pp.reg_table3 >= 0) pp.reg_table3 += off;
         pp.src_buf = remap[pp.src_buf];
         pp.dst_buf = remap[pp.dst_buf];
         dst.passes.push_back(pp);

@@ -1286,9 +1286,62 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
     size_t M1, M2;
     AxisAlgorithm smooth;
     if (!four_step_split(ce, M, smooth, M1, M2)) fail_unsupported("B200 engine: Bluestein length not decomposable");
-    const int spec = table_bluestein_spectrum(prog, N, M);
     const int64_t scr_os = (int64_t)M * S;
     prog.scratch_elems[0] = std::max(prog.scratch_elems[0], (size_t)(no * M * S));
+    // contiguous complex axis: the three passes in the register kernels (REG_BLU_A/B/C)
+    {
+        const int va = reg_variant(prog, M1, REG_BLU_A, true), vc = reg_variant(prog, M1, REG_BLU_C, true);
+        if (S == 1 && So == 1 && va >= 0 && vc >= 0 && reg_kernels_enabled() && !job.in_real && !herm &&
+            !job.out_real) {
+            const int ttw = table_twiddle_transposed(prog, M2, M1, M);  // W_M^(n2 k1) at k1 M2 + n2
+            auto reg_pass = [&](int rv, size_t len, int64_t nlines, int64_t ni, RegSide src, RegSide dst, int t2, int t3,
+                                int64_t n, int in_buf, int64_t in_off, int out_buf, int64_t out_off, double sc,
+                                const char *label) {
+                PassPlan pp{};
+                pp.kernel = KERNEL_REG;
+                pp.reg_variant = rv;
+                pp.reg_table = table_reg_twiddles(prog, len, rv);
+                pp.reg_table2 = t2;
+                pp.reg_table3 = t3;
+                pp.rp.nlines = nlines;
+                pp.rp.ni = ni;
+                pp.rp.src = src;
+                pp.rp.dst = dst;
+                pp.rp.scale = sc;
+                pp.rp.conj = inv ? 1 : 0;
+                pp.rp.n = (int32_t)n;
+                pp.src_buf = in_buf;
+                pp.src_off = in_off;
+                pp.dst_buf = out_buf;
+                pp.dst_off = out_off;
+                pp.label = label;
+                for (auto &row : pp.op_tables) row[0] = row[1] = row[2] = -1;
+                prog.passes.push_back(pp);
+            };
+            const int64_t m2 = (int64_t)M2;
+            reg_pass(va, M1, no * m2, m2, RegSide{job.in_os, 1, m2}, RegSide{scr_os, 1, m2}, chirp, ttw, (int64_t)N,
+                     job.in_buf, job.in_off, BUF_SCRATCH0, 0, 1.0, "bluestein columns (register)");
+            {
+                // the rows (FFT * spectrum * inverse FFT of length M2) stay on the generic
+                // pass: its host-modelled shared-memory layout avoids the bank conflicts the
+                // register kernel's power-of-two padding has on these odd-radix rows
+                PassBuilder b(prog, (int)M2, line_stages(M2, nullptr), true, no * (int64_t)M1, kMaxOps);
+                b.load((int)M2, 0);
+                b.fft();
+                b.mul_region(table_bluestein_spectrum_rows(prog, N, M, M1, M2), F_CONJ_OUT, (int)M2, 1);
+                b.fft();
+                b.store((int)M2, F_CONJ_IN | F_CONJ_LUT, MUL_TWIDDLE_CE, ttw, 1.0, 1, (int)M2);
+                prog.passes.push_back(b.finish(no, 1, (int64_t)M1, make_side(scr_os, 1, m2, 1, false, M, (int)M2, 1),
+                                               make_side(scr_os, 1, m2, 1, false, M, (int)M2, 1), BUF_SCRATCH0, 0,
+                                               BUF_SCRATCH0, 0, "bluestein rows"));
+            }
+            reg_pass(vc, M1, no * m2, m2, RegSide{scr_os, 1, m2}, RegSide{job.out_os, 1, m2}, chirp, -1,
+                     (int64_t)out_count, BUF_SCRATCH0, 0, job.out_buf, job.out_off, scale,
+                     "bluestein columns inverse (register)");
+            return;
+        }
+    }
+    const int spec = table_bluestein_spectrum(prog, N, M);
     // contiguous axis (S = 1): the rows of pass B are contiguous in scratch and its threads
     // walk elements, so its spectrum and twiddle tables are laid out row by row
     const bool rows_contig = S == 1;

@@ -53,6 +53,7 @@ struct PassPlan {
     int reg_variant = -1;
     int reg_table = -1;           // twiddle table id of a KERNEL_REG pass
     int reg_table2 = -1;          // KERNEL_REG HALF modes: the W_2h table
+    int reg_table3 = -1;          // KERNEL_REG Bluestein four-step modes: the W_M twiddles
     int reg_variant_plain = -1;   // persistent reg_variant: the ordinary variant, used when the
                                   // input is not 16-byte aligned for the bulk copies
     bool reg_in_real = false, reg_out_real = false;

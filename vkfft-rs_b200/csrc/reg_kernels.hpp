@@ -26,6 +26,13 @@ enum RegMode : int32_t {
                       // tw2 = [W_n^k | W_4n^k], k = 0..N
     REG_RADER_LINE = 9,  // prime-length lines, one thread per line: Rader's algorithm in registers
                          // (N = P; tw = FFT_{P-1} of the Rader kernel / (P - 1))
+    // The column passes of a four-step Bluestein convolution of a contiguous axis, M = M1 M2,
+    // block position pos = n2 + M2 k1 of a line's M-point scratch block (lower.cpp; the rows
+    // between them run the generic pass):
+    REG_BLU_A = 10,   // strided columns n2 (length M1): x[n] * chirp[n] for n = n2 + M2 n1 < rp.n
+                      // (else 0; conjugated first when inverse), FFT, * W_M^(n2 k1) = tw3[pos]
+    REG_BLU_C = 12,   // strided columns: inverse FFT (conjugation trick), * chirp[n], scale, stored
+                      // for n = n2 + M2 n1 < rp.n (conjugated last when inverse)
 };
 
 // Line l = o * ni + i; element p of the line is at o*os + i*is + p*es (units of the
@@ -38,7 +45,8 @@ struct RegParams {
     const void *in;
     void *out;
     const void *tw;      // per-stage transposed twiddle tables (reg_kernels.cu)
-    const void *tw2;     // HALF modes: W_{2h}^k, k = 0..h
+    const void *tw2;     // HALF modes: W_{2h}^k, k = 0..h; Bluestein modes: chirp / spectrum rows
+    const void *tw3;     // Bluestein four-step modes: W_M^(n2 k1) by block position
     int64_t nlines;      // transforms in this launch
     int64_t ni;          // inner line count (1 for contiguous lines)
     RegSide src, dst;

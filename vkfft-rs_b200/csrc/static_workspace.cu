@@ -129,6 +129,7 @@ void execute_program_static(Context *ctx, uint64_t /*id*/, const Program &prog, 
             rp.out = static_cast<unsigned char *>(bufs[pp.dst_buf]) + pp.dst_off * (pp.reg_out_real ? esz / 2 : esz);
             rp.tw = tables[pp.reg_table];
             rp.tw2 = pp.reg_table2 >= 0 ? tables[pp.reg_table2] : nullptr;
+            rp.tw3 = pp.reg_table3 >= 0 ? tables[pp.reg_table3] : nullptr;
             rp.err = ctx->d_err;
             int rv = pp.reg_variant;
             if (pp.reg_variant_plain >= 0 && (reinterpret_cast<uintptr_t>(rp.in) & 15)) rv = pp.reg_variant_plain;
