@@ -1323,8 +1323,9 @@ void lower_c2c_axis(Program &prog, const AxisJob &job) {
                      job.in_buf, job.in_off, BUF_SCRATCH0, 0, 1.0, "bluestein columns (register)");
             {
                 // the rows (FFT * spectrum * inverse FFT of length M2) stay on the generic
-                // pass: its host-modelled shared-memory layout avoids the bank conflicts the
-                // register kernel's power-of-two padding has on these odd-radix rows
+                // pass: the register version (radices 5 3 3 3 3, 15 points per thread)
+                // needs 174 registers, one 216-thread CTA per SM, and measured 4.3 ms per
+                // direction for 65537 x 2048 against the generic pass's 2.6 ms
                 PassBuilder b(prog, (int)M2, line_stages(M2, nullptr), true, no * (int64_t)M1, kMaxOps);
                 b.load((int)M2, 0);
                 b.fft();

@@ -32,7 +32,10 @@ template <typename T> struct vec2;
 template <> struct vec2<float> { using type = float2; };
 template <> struct vec2<double> { using type = double2; };
 
-__device__ __forceinline__ int pad(int e) { return e + (e >> 4); }
+// Shared-memory slot of line position e: one spare slot every 16 positions for
+// power-of-two lines (their radix-16 strides would otherwise collapse onto few banks);
+// odd-radix lines are unpadded (their stage strides are odd multiples already).
+template <int N> __device__ __forceinline__ int pad(int e) { return (N & (N - 1)) == 0 ? e + (e >> 4) : e; }
 
 // Shared-memory stride between the G lines of a CTA (complex elements, >= pad(N-1) + 1).
 // A 128-byte wavefront holds W complex values (16 for f32, 8 for f64).  Within one
@@ -287,7 +290,7 @@ __device__ __forceinline__ void r2r_half_epilogue(const RegParams &rp, cplx<T> (
     if ((rp.r2r_kind & 3) == 1) {
         __syncthreads();  // the last stage's shared-memory reads are done
 #pragma unroll
-        for (int m = 0; m < E; m++) sline[pad(t + m * TT)] = v[m];
+        for (int m = 0; m < E; m++) sline[pad<N>(t + m * TT)] = v[m];
         __syncthreads();
         if (!valid) return;
         auto put = [&](int k, T x) { __stcs(out + (dst ? n - 1 - k : k), x * s); };
@@ -299,7 +302,7 @@ __device__ __forceinline__ void r2r_half_epilogue(const RegParams &rp, cplx<T> (
 #pragma unroll
         for (int m = 0; m < E; m++) {
             const int p = t + m * TT;
-            const cplx<T> zq = sline[pad((N - p) & (N - 1))];
+            const cplx<T> zq = sline[pad<N>((N - p) & (N - 1))];
             const cplx<T> u = mul(tw_load(B, p), post(v[m], zq, p));
             put(p, T(2) * u.x);
             if (p != 0) put(n - p, T(-2) * u.y);
@@ -371,7 +374,7 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
 #pragma unroll
         for (int k = 0; k < NB; k++)
 #pragma unroll
-            for (int q = 0; q < R; q++) v[k + q * NB] = sline[pad(t + k * TT + q * (N / R))];
+            for (int q = 0; q < R; q++) v[k + q * NB] = sline[pad<N>(t + k * TT + q * (N / R))];
         if (!LAST) __syncthreads();  // every thread has read before anyone overwrites
     }
 #pragma unroll
@@ -409,7 +412,7 @@ __device__ __forceinline__ void stage(cplx<T> (&v)[E], int t, cplx<T> *sline, co
         } else {
             const int e0 = (b - j) * R + j;
 #pragma unroll
-            for (int q = 0; q < R; q++) sline[pad(e0 + q * P)] = x[q];
+            for (int q = 0; q < R; q++) sline[pad<N>(e0 + q * P)] = x[q];
         }
     }
 }
@@ -449,7 +452,7 @@ __device__ __forceinline__ void r2c_half_epilogue(const RegParams &rp, const cpl
     constexpr int TT = N / E;
     __syncthreads();  // the last stage's shared-memory reads are done
 #pragma unroll
-    for (int m = 0; m < E; m++) sline[pad(t + m * TT)] = v[m];
+    for (int m = 0; m < E; m++) sline[pad<N>(t + m * TT)] = v[m];
     __syncthreads();
     if (!valid) return;
     const cplx<T> *w2 = reinterpret_cast<const cplx<T> *>(rp.tw2);
@@ -461,7 +464,7 @@ __device__ __forceinline__ void r2c_half_epilogue(const RegParams &rp, const cpl
 #pragma unroll
     for (int m = 0; m < E; m++) {
         const int p = t + m * TT;
-        const cplx<T> zk2 = sline[pad((N - p) & (N - 1))];
+        const cplx<T> zk2 = sline[pad<N>((N - p) & (N - 1))];
         st_c<T>(rp.out, out_base + p, post(v[m], zk2, p));
         if (p == 0) st_c<T>(rp.out, out_base + N, post(v[m], v[m], N));
     }
