@@ -719,6 +719,9 @@ WORKLOADS = {
     "c2c-65537-f32": dict(kind="c2c", dims=[65537], batch=2048, prec="F32", config=4),
     "c2c-65537-f64": dict(kind="c2c", dims=[65537], batch=2048, prec="F64", config=4),
     "conv-2048": dict(kind="conv", dims=[2048, 2048], batch=64, prec="F32", config=5),
+    # config-4 shape family at 1/16 of the outer axis (570 MB, profiling the 17-point Rader
+    # line kernel and the Bluestein passes of 65537 on a small case)
+    "c2c-64x17x65537-f32": dict(kind="c2c", dims=[64, 17, 65537], batch=1, prec="F32", config=4),
     # small 2D case (512 MB): one contiguous and one strided 1024-point axis (profiling)
     "c2c-1024^2x64": dict(kind="c2c", dims=[1024, 1024], batch=64, prec="F32", config=3),
     # DCT / DST (not a headline config): forward DCT-II + normalised inverse (DCT-III)
