@@ -106,7 +106,7 @@ def test_mixed_direct_and_fft_rader_axis(V, ctx, prec):
 
 @pytest.mark.parametrize("prec", ["F32", "F64"])
 @pytest.mark.parametrize("dims,batch", [([8, 16], 3), ([64, 64, 64], 1), ([32, 17, 100], 2), ([5, 47, 12], 2),
-                                        ([2, 17, 4099], 1), ([16, 1, 64], 2)])
+                                        ([2, 17, 4099], 1), ([16, 1, 64], 2), ([512, 512], 3), ([3, 512, 512], 1)])
 def test_c2c_nd(V, ctx, dims, batch, prec):
     for direction, norm in ((V.Direction.FORWARD, False), (V.Direction.INVERSE, True)):
         ir, err = run_c2c(V, ctx, dims, batch, prec, direction, normalize=norm, seed=len(dims))
