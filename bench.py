@@ -76,7 +76,8 @@ class ClockSampler:
         self.bus_id = None
         try:
             import torch
-            self.bus_id = torch.cuda.get_device_properties(device_ordinal).pci_bus_id.upper()  # 0000:1B:00.0
+            pr = torch.cuda.get_device_properties(device_ordinal)  # domain / bus / device numbers
+            self.bus_id = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
         except Exception:
             pass
         self.rows = []  # nvidia-smi: (wall time, fields)
@@ -87,15 +88,27 @@ class ClockSampler:
         self.active = False
         self.stop = False
         self.handle = None
+        self.nvml_error = None
         try:
             import pynvml
             pynvml.nvmlInit()
-            dom, rest = self.bus_id.split(":", 1)
-            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(f"{int(dom, 16):08X}:{rest}")
             self.nvml = pynvml
+            # match this rank's GPU among NVML's devices by PCI bus id (domain width differs)
+            for k in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(k)
+                bid = pynvml.nvmlDeviceGetPciInfo(h).busId
+                bid = bid.decode() if isinstance(bid, bytes) else bid
+                if self.bus_id and self._same_bus(bid, self.bus_id):
+                    self.handle = h
+                    break
+            if self.handle is None:
+                raise RuntimeError(f"no NVML device with PCI bus id {self.bus_id}")
             self.nv_max = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
-        except Exception:
+            pynvml.nvmlDeviceGetClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        except Exception as e:  # the nvidia-smi rows remain
             self.handle = None
+            self.nvml_error = f"{type(e).__name__}: {e}"
 
     @staticmethod
     def _same_bus(a, b):
@@ -174,14 +187,16 @@ class ClockSampler:
             pad = 1.5 * self.PERIOD_MS * 1e-3
             rows = [r for t, r in self.rows if self.t_start - pad <= t <= self.t_end + pad]
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0,
+                    "nvml_error": self.nvml_error}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows),
-                "window": "nvidia-smi rows in the timed region +- one sampling period (50 ms)"}
+                "window": "nvidia-smi rows in the timed region +- one sampling period (50 ms)",
+                "nvml_error": self.nvml_error}
 
 
 def cpu_baseline(steps_hint=1, budget_s=12.0):
