@@ -130,11 +130,14 @@ static void put_root(HostTable &t, const Program &prog, size_t idx, size_t m, si
 // a transposed block tw[(q-1)*P + j] = W_{P R}^{j q}, q = 1..R-1, j = 0..P-1, blocks in
 // stage order (reg_kernels.cu reads them at compile-time offsets).
 int table_reg_twiddles(Program &prog, size_t n, int variant) {
-    std::string key = "regtw" + std::to_string(n);
-    auto it = prog.table_cache.find(key);
-    if (it != prog.table_cache.end()) return it->second;
     int rad[8];
     const int ns = reg_variant_radices(variant, rad);
+    // keyed by the radix sequence too: two variants of one length may order their stages
+    // differently (and so need different tables)
+    std::string key = "regtw" + std::to_string(n);
+    for (int s = 0; s < ns; s++) key += "_" + std::to_string(rad[s]);
+    auto it = prog.table_cache.find(key);
+    if (it != prog.table_cache.end()) return it->second;
     HostTable t;
     size_t P = 1;
     for (int s = 0; s < ns; s++) {

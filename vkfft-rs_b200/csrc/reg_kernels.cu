@@ -817,7 +817,7 @@ static const RegVariant kRegVariants[] = {
     RV(float, REG_C2C, true, 16, 16, 32, 16), RV(float, REG_C2C, true, 32, 16, 32, 16, 2),
     RV(float, REG_C2C, true, 64, 16, 32, 16, 4), RV(float, REG_C2C, true, 128, 16, 32, 16, 8),
     RV(float, REG_C2C, true, 256, 16, 16, 16, 16), RV(float, REG_C2C, true, 512, 16, 16, 16, 16, 2),
-    RV(float, REG_C2C, true, 1024, 16, 16, 16, 16, 4), RV(float, REG_C2C, true, 2048, 16, 8, 16, 16, 8),
+    RV(float, REG_C2C, true, 1024, 32, 16, 32, 32), RV(float, REG_C2C, true, 2048, 16, 8, 16, 16, 8),
     RV(float, REG_C2C, true, 4096, 16, 4, 16, 16, 16),
     RV(double, REG_C2C, true, 16, 16, 32, 16), RV(double, REG_C2C, true, 32, 16, 32, 16, 2),
     RV(double, REG_C2C, true, 64, 16, 16, 16, 4), RV(double, REG_C2C, true, 128, 16, 16, 16, 8),
