@@ -816,7 +816,7 @@ static const RegVariant kRegVariants[] = {
     // strided (higher-axis) C2C lines: G neighbouring lines per CTA
     RV(float, REG_C2C, true, 16, 16, 32, 16), RV(float, REG_C2C, true, 32, 16, 32, 16, 2),
     RV(float, REG_C2C, true, 64, 16, 32, 16, 4), RV(float, REG_C2C, true, 128, 16, 32, 16, 8),
-    RV(float, REG_C2C, true, 256, 16, 16, 16, 16), RV(float, REG_C2C, true, 512, 16, 16, 16, 16, 2),
+    RV(float, REG_C2C, true, 256, 16, 16, 16, 16), RV(float, REG_C2C, true, 512, 32, 16, 32, 16),
     RV(float, REG_C2C, true, 1024, 32, 16, 32, 32), RV(float, REG_C2C, true, 2048, 16, 8, 16, 16, 8),
     RV(float, REG_C2C, true, 4096, 16, 4, 16, 16, 16),
     RV(double, REG_C2C, true, 16, 16, 32, 16), RV(double, REG_C2C, true, 32, 16, 32, 16, 2),
