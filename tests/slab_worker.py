@@ -54,13 +54,13 @@ def run_case(ctx, rank, world, dims, prec, real):
     spec = torch.empty(fwd.output_elements * 2, dtype=xin.dtype, device="cuda")
     back = torch.empty_like(xin)
     s = torch.cuda.current_stream().cuda_stream
+    full = oracle.r2c_nd(x, len(dims)) if real else oracle.fft_nd(x, len(dims))
+    ref = full[:, rank * C1:(rank + 1) * C1]
     errs = []
     for _ in range(2):  # two calls: both exchange buffers (call parity) are used
         ctx.execute_slab(fwd, xin.data_ptr(), spec.data_ptr(), stream=s)
         ctx.execute_slab(inv, spec.data_ptr(), back.data_ptr(), stream=s)
         ctx.synchronize(s)
-        full = oracle.r2c_nd(x, len(dims)) if real else oracle.fft_nd(x, len(dims))
-        ref = full[:, rank * C1:(rank + 1) * C1]
         got = spec.cpu().numpy().view(cdt)
         errs.append(rel_l2(got, ref))
         got_back = back.cpu().numpy().view(rdt if real else cdt)
@@ -79,7 +79,10 @@ def main():
     ctx = V.CudaExecutionContext(local)
     failures = []
     cases = [([64, 32, 48], "F32", False), ([32, 64, 64], "F32", True), ([16, 24, 20], "F64", False),
-             ([34, 18, 17], "F64", False), ([8198, 4, 6], "F32", False), ([128, 256], "F32", False)]
+             ([34, 18, 17], "F64", False), ([8198, 4, 6], "F32", False), ([128, 256], "F32", False),
+             # the exchange passes of these run the strided 512- and 1024-point register
+             # kernels (axis 1 forward, axis 0 inverse)
+             ([512, 512, 8], "F32", False), ([1024, 1024, 2], "F32", False), ([512, 512, 4], "F64", False)]
     for dims, prec, real in cases:
         if dims[0] % world or dims[1] % world:
             continue

@@ -33,6 +33,9 @@ void mark_exchange_pass(Program &prog, size_t first, int out_buf) {
         if (twin < 0) fail_runtime("slab exchange pass has no peer-scatter register kernel");
         pp.reg_variant = twin;
         pp.reg_variant_plain = -1;
+        // the twin may split the line into other radices than the variant the lowering
+        // chose, and its stage twiddles follow its own radix sequence
+        pp.reg_table = table_reg_twiddles(prog, (size_t)pp.rp.n, twin);
         pp.peer_es = pp.rp.dst.es;
         return;
     }
