@@ -245,4 +245,5 @@ namespace b200fft {
 int reg_variant_radices(int, int *) { return 0; }
 int reg_variant_peer_twin(int) { return -1; }
 int reg_variant_persistent_twin(int) { return -1; }
+int reg_variant_length(int) { return 0; }
 }  // namespace b200fft

@@ -86,3 +86,19 @@ def test_slab_layout_contract_world2(dims, real):
     for rank, err, exc in results:
         assert exc is None, f"rank {rank}: {exc}"
         assert err < 1e-12, (rank, err)
+
+
+@pytest.mark.parametrize("dims,prec", [([512, 512, 8], "F32"), ([1024, 1024, 2], "F32"), ([512, 512, 4], "F64"),
+                                       ([512, 512, 512], "F32"), ([64, 1024, 16], "F32")])
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_slab_exchange_pass_tables_match_its_kernel(V, cuda_profile, dims, prec, world):
+    """The exchange pass runs the peer-scatter twin of the register kernel the lowering
+    picked, which may split the line into other radices (512 and 1024 f32 strided lines
+    do).  Building the plan fails unless every register pass reads the stage twiddles of
+    its own radix split; both directions, every rank."""
+    cfg = V.FftConfig(dims).with_precision(V.Precision[prec]).with_inverse_normalization(True)
+    for rank in range(world):
+        for direction in (V.Direction.FORWARD, V.Direction.INVERSE):
+            slab = V.SlabTransform.build(cfg, direction, world, rank, cuda_profile)
+            assert slab.planes_per_rank == dims[0] // world
+            slab.destroy()

@@ -277,7 +277,9 @@ std::unique_ptr<Convolution> build_convolution(const FftConfig &config_in, const
     if (config_in.perform_convolution && config_in.transform == TransformKind::C2C) {
         if (!(config_in.precision == Precision::F32 || config_in.precision == Precision::F64))
             fail_precision("B200 engine", precision_name(config_in.precision));
-        return build_c2c_convolution(config_in.resolve_tuning_for_device(device), device, spectrum, copies);
+        auto conv = build_c2c_convolution(config_in.resolve_tuning_for_device(device), device, spectrum, copies);
+        check_reg_twiddle_tables(conv->prog);
+        return conv;
     }
     if (!config_in.perform_convolution || config_in.transform != TransformKind::R2C ||
         config_in.dimensions.size() < 2 || config_in.batch_count != 1)
@@ -309,8 +311,11 @@ std::unique_ptr<Convolution> build_convolution(const FftConfig &config_in, const
         fail_unsupported("kernel-conjugated convolution is not executable in the pinned VkFFT codegen");
     if (!(config_in.precision == Precision::F32 || config_in.precision == Precision::F64))
         fail_precision("B200 engine", precision_name(config_in.precision));
-    if (Mx || padded || config_in.has_formatted_strides())
-        return build_real_convolution_generic(config_in.resolve_tuning_for_device(device), device, spectrum, copies);
+    if (Mx || padded || config_in.has_formatted_strides()) {
+        auto conv = build_real_convolution_generic(config_in.resolve_tuning_for_device(device), device, spectrum, copies);
+        check_reg_twiddle_tables(conv->prog);
+        return conv;
+    }
     const FftConfig c = config_in.resolve_tuning_for_device(device);
     auto conv = std::make_unique<Convolution>();
     static std::atomic<uint64_t> next_id{1ull << 40};
@@ -422,6 +427,7 @@ std::unique_ptr<Convolution> build_convolution(const FftConfig &config_in, const
     cj.in_buf = spec_buf;
     cj.out_buf = BUF_OUT;
     lower_c2r_axis(prog, cj);
+    check_reg_twiddle_tables(prog);
     return conv;
 }
 

@@ -98,6 +98,7 @@ static void host_fft_q(std::vector<QC> &x) {
 static int add_table(Program &prog, const std::string &key, HostTable t) {
     auto it = prog.table_cache.find(key);
     if (it != prog.table_cache.end()) return it->second;
+    t.key = key;
     prog.tables.push_back(std::move(t));
     int id = (int)prog.tables.size() - 1;
     prog.table_cache[key] = id;
@@ -126,16 +127,23 @@ static void put_root(HostTable &t, const Program &prog, size_t idx, size_t m, si
     t.c[idx] = conj ? std::conj(v) : v;
 }
 
-// Stage twiddles of a register-kernel variant: for every stage s > 0 (span P, radix R)
-// a transposed block tw[(q-1)*P + j] = W_{P R}^{j q}, q = 1..R-1, j = 0..P-1, blocks in
-// stage order (reg_kernels.cu reads them at compile-time offsets).
-int table_reg_twiddles(Program &prog, size_t n, int variant) {
+static std::string reg_twiddle_key(size_t n, int variant) {
     int rad[8];
     const int ns = reg_variant_radices(variant, rad);
     // keyed by the radix sequence too: two variants of one length may order their stages
     // differently (and so need different tables)
     std::string key = "regtw" + std::to_string(n);
     for (int s = 0; s < ns; s++) key += "_" + std::to_string(rad[s]);
+    return key;
+}
+
+// Stage twiddles of a register-kernel variant: for every stage s > 0 (span P, radix R)
+// a transposed block tw[(q-1)*P + j] = W_{P R}^{j q}, q = 1..R-1, j = 0..P-1, blocks in
+// stage order (reg_kernels.cu reads them at compile-time offsets).
+int table_reg_twiddles(Program &prog, size_t n, int variant) {
+    int rad[8];
+    const int ns = reg_variant_radices(variant, rad);
+    const std::string key = reg_twiddle_key(n, variant);
     auto it = prog.table_cache.find(key);
     if (it != prog.table_cache.end()) return it->second;
     HostTable t;
@@ -149,6 +157,18 @@ int table_reg_twiddles(Program &prog, size_t n, int variant) {
     }
     if (t.c.empty()) t.c.push_back({1.0, 0.0});
     return add_table(prog, key, std::move(t));
+}
+
+void check_reg_twiddle_tables(const Program &prog) {
+    for (const PassPlan &pp : prog.passes) {
+        if (pp.kernel != KERNEL_REG || pp.reg_table < 0 || pp.reg_variant < 0) continue;
+        if ((size_t)pp.reg_table >= prog.tables.size()) fail_runtime("register pass names a missing table");
+        const std::string &key = prog.tables[(size_t)pp.reg_table].key;
+        if (key.compare(0, 5, "regtw") != 0) continue;  // not a stage-twiddle table
+        for (int v : {pp.reg_variant, pp.reg_variant_plain})
+            if (v >= 0 && key != reg_twiddle_key((size_t)reg_variant_length(v), v))
+                fail_runtime("register pass reads the stage twiddles of another length or radix split");
+    }
 }
 
 // Twiddles of one radix-R Stockham stage of span P, transposed: entry (q-1)*P + j holds

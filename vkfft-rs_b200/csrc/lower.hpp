@@ -58,6 +58,7 @@ int reg_variant_radices(int v, int *out);
 int reg_variant_peer_twin(int v);  // REG_C2C -> REG_C2C_PEER variant (-1: none)
 int reg_variant_persistent_twin(int v);  // contiguous C2C / R2R / even-half -> bulk-prefetch variant (-1: none)
 int reg_variant_lines_per_cta(int v);
+int reg_variant_length(int v);
 bool line_fits_on_chip(int complex_bytes, size_t L, const AxisAlgorithm *alg, bool strided);
 void lower_c2c_axis(Program &prog, const AxisJob &job);
 void lower_r2c_axis(Program &prog, const RealAxisJob &job);

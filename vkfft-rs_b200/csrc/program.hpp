@@ -32,6 +32,7 @@ enum BufId : int {
 constexpr int kScratchBuffers = 8;
 
 struct HostTable {
+    std::string key;      // cache key: the table's kind and parameters (empty: uncached)
     bool is_int = false;
     bool is_raw = false;  // already in the pass precision (user-supplied convolution spectra)
     std::vector<std::complex<double>> c;   // values (double-double programs: the high words)
@@ -137,6 +138,9 @@ FastDiv make_fastdiv(uint32_t d);
 // Tables (host f64).  All roots are forward: W_N^m = exp(-2 pi i m / N).
 int table_twiddle(Program &prog, size_t n);
 int table_reg_twiddles(Program &prog, size_t n, int variant);
+// Fails unless every register pass (and its misaligned-input fallback variant) that reads
+// stage twiddles reads the table of its own variant's length and radix split.
+void check_reg_twiddle_tables(const Program &prog);
 int table_bluestein_chirp(Program &prog, size_t n);
 int table_bluestein_spectrum(Program &prog, size_t n, size_t m);
 int table_bluestein_spectrum_rows(Program &prog, size_t n, size_t m, size_t m1, size_t m2);

@@ -894,6 +894,8 @@ int reg_variant_radices(int v, int *out) {
 
 int reg_variant_lines_per_cta(int v) { return kRegVariants[v].g; }
 
+int reg_variant_length(int v) { return kRegVariants[v].n; }
+
 // The REG_C2C_PEER twin of a REG_C2C variant (same precision, length and layout), or -1.
 int reg_variant_peer_twin(int v) {
     const RegVariant &a = kRegVariants[v];

@@ -211,6 +211,8 @@ std::unique_ptr<Slab> build_slab(const FftConfig &config_in, int direction, int 
     s->output_elems = post.output_elems;
     s->input_real = pre.input_real;
     s->output_real = post.output_real;
+    check_reg_twiddle_tables(pre);
+    check_reg_twiddle_tables(post);
     return s;
 }
 

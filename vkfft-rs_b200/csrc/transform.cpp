@@ -219,6 +219,7 @@ std::unique_ptr<Transform> build_transform(const FftConfig &config_in, int direc
     auto t = build_transform_core(config_in, direction, device);
     add_boundaries(*t);
     finalize_dd_scales(t->prog);
+    check_reg_twiddle_tables(t->prog);
     return t;
 }
 
