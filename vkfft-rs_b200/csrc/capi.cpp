@@ -407,6 +407,7 @@ b200fft_status b200fft_execute_convolution_host(b200fft_context *context, b200ff
         need(output, "output");
         // host arrays are logical tensors: a formatted convolution runs its dense twin
         const Convolution &cv = convolution->c->dense_twin ? *convolution->c->dense_twin : *convolution->c;
+        std::lock_guard<std::mutex> host_lock(context->ctx->host_mu);  // staging buffers: one host call at a time
         execute_program_host(context->ctx, cv.id, cv.prog, input, input_bytes, output, output_bytes);
     });
 }

@@ -108,6 +108,7 @@ void context_destroy(Context *ctx) {
         ctx->job_cv.notify_all();
         ctx->worker.join();
     }
+    ctx->staging.reset();  // joins its copy threads, frees the pinned rings
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     for (auto &kv : ctx->tables) cudaFree(kv.second.base);
@@ -270,6 +271,30 @@ void execute_program(Context *ctx, uint64_t id, const Program &prog, const void 
     }
 }
 
+static HostStaging &staging_of(Context *ctx) {  // the caller holds ctx->host_mu
+    if (!ctx->staging) ctx->staging = std::make_unique<HostStaging>(ctx->device);
+    return *ctx->staging;
+}
+
+// Host -> device copy of one host call's input: pinned arrays go straight to the copy
+// engine, large pageable ones through the context's pinned staging, small pageable ones
+// through the driver's own pageable path.
+static void host_upload(Context *ctx, void *dst, const void *src, size_t bytes, bool pageable, cudaStream_t s) {
+    if (pageable && bytes >= StagingTuning().min_staged_upload)
+        staging_of(ctx).upload(dst, src, bytes, s);
+    else
+        check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s), "input upload");
+}
+
+// Device -> host copy of a host call's output; a staged copy returns when the bytes are
+// in `dst`, a direct one is queued on `s`.
+static void host_download(Context *ctx, void *dst, const void *src, size_t bytes, bool pageable, cudaStream_t s) {
+    if (pageable && bytes >= StagingTuning().min_staged_download)
+        staging_of(ctx).download(dst, src, bytes, s);
+    else
+        check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s), "output download");
+}
+
 void execute_program_host(Context *ctx, uint64_t id, const Program &prog, const void *in, size_t in_bytes, void *out,
                           size_t out_bytes) {
     const size_t in_need = prog.input_bytes(), out_need = prog.output_bytes();
@@ -282,17 +307,20 @@ void execute_program_host(Context *ctx, uint64_t id, const Program &prog, const 
         std::lock_guard<std::mutex> l(ctx->mu);
         din = ensure_buffer(ctx->stage_in, ctx->stage_in_bytes, in_need, "input staging allocation");
         dout = ensure_buffer(ctx->stage_out, ctx->stage_out_bytes, out_need, "output staging allocation");
-        check(cudaMemcpyAsync(din, in, in_need, cudaMemcpyHostToDevice, ctx->stream), "input upload");
     }
+    host_upload(ctx, din, in, in_need, host_is_pageable(in), ctx->stream);
     execute_program(ctx, id, prog, din, dout, nullptr, ctx->stream);
-    check(cudaMemcpyAsync(out, dout, out_need, cudaMemcpyDeviceToHost, ctx->stream), "output download");
-    int err = 0;
-    check(cudaMemcpyAsync(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream), "error word read");
+    int local_err = 0;
+    int *err = ctx->staging ? ctx->staging->pinned_word() : &local_err;
+    *err = 0;
+    check(cudaMemcpyAsync(err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream), "error word read");
+    host_download(ctx, out, dout, out_need, host_is_pageable(out), ctx->stream);
     check(cudaStreamSynchronize(ctx->stream), "stream synchronize");
-    if (err) {
+    if (*err) {
+        const int e = *err;
         cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream);
         cudaStreamSynchronize(ctx->stream);
-        fail_runtime("B200 FFT kernel reported error word " + std::to_string(err));
+        fail_runtime("B200 FFT kernel reported error word " + std::to_string(e));
     }
 }
 
@@ -447,19 +475,18 @@ void execute_transform_host(Context *ctx, Transform &t_in, const void *in, size_
             ensure_buffer(ctx->pipe_buf, ctx->pipe_bytes, Context::kPipeSlots * slot_bytes, "pipeline staging allocation"));
     }
     const size_t nchunks = nfull + (rem ? 1 : 0);
+    // large pageable arrays go through the pinned staging sub-batch by sub-batch (a staged
+    // download returns once its bytes are on the host); pinned ones overlap on the streams
+    const bool page_in = host_is_pageable(in), page_out = host_is_pageable(out);
     for (size_t i = 0; i < nchunks; i++) {
         const int slot = (int)(i % Context::kPipeSlots);
         cudaStream_t s = ctx->pipe[slot];
         Transform *tt = i < nfull ? ct : rt;
         const size_t nb = i < nfull ? chunk : rem;
         unsigned char *din = base + slot * slot_bytes, *dout = din + cin, *dscr = dout + cout;
-        check(cudaMemcpyAsync(din, static_cast<const unsigned char *>(in) + i * chunk * in_per, nb * in_per,
-                              cudaMemcpyHostToDevice, s),
-              "input upload");
+        host_upload(ctx, din, static_cast<const unsigned char *>(in) + i * chunk * in_per, nb * in_per, page_in, s);
         execute_program(ctx, tt->id, tt->prog, din, dout, scr ? dscr : nullptr, s);
-        check(cudaMemcpyAsync(static_cast<unsigned char *>(out) + i * chunk * out_per, dout, nb * out_per,
-                              cudaMemcpyDeviceToHost, s),
-              "output download");
+        host_download(ctx, static_cast<unsigned char *>(out) + i * chunk * out_per, dout, nb * out_per, page_out, s);
     }
     for (cudaStream_t s : ctx->pipe) check(cudaStreamSynchronize(s), "stream synchronize");
     int err = 0;

@@ -15,6 +15,7 @@
 #include <unordered_map>
 
 #include "aot.hpp"
+#include "host_staging.hpp"
 #include "transform.hpp"
 
 namespace b200fft {
@@ -39,6 +40,8 @@ struct Context {
     void *stage_in = nullptr, *stage_out = nullptr;
     size_t stage_in_bytes = 0, stage_out_bytes = 0;
     std::mutex host_mu;  // host executions (staging buffers, pipeline streams) one at a time
+    // pinned staging of large pageable host arrays (created by the first host call needing it)
+    std::unique_ptr<HostStaging> staging;
     // asynchronous submissions: one worker thread runs them in submission order
     std::mutex job_mu;
     std::condition_variable job_cv;
