@@ -276,6 +276,12 @@ uint64_t b200fft_transform_workspace_bytes(const b200fft_transform *transform);
 int32_t b200fft_transform_specialised_passes(const b200fft_transform *transform, int32_t *generic_passes);
 /* Number of kernel launches one execution issues. */
 uint32_t b200fft_transform_launch_count(const b200fft_transform *transform);
+/* The kernel kind of each launch of one execution, in order, one label per line (e.g.
+ * "register stockham (tensor-map tiles)"), written NUL-terminated into buffer (at most
+ * capacity bytes, truncated); returns the length the whole text needs, without the NUL.
+ * No counterpart in the reference (introspection of this engine's launch list); needs no
+ * GPU. */
+uint64_t b200fft_transform_describe_passes(const b200fft_transform *transform, char *buffer, uint64_t capacity);
 
 /* ---- execution runtime (backend/cuda/runtime.rs) ------------------------- */
 /* CudaExecutionContext::probe (cuda/runtime.rs:979): number of CUDA devices, or

@@ -74,3 +74,19 @@ def test_library_links_no_runtime_compiler(V):
     lib = os.path.join(os.path.dirname(V.__file__), os.pardir, "libb200fft.so")
     out = subprocess.run(["ldd", os.path.abspath(lib)], capture_output=True, text=True).stdout
     assert "nvrtc" not in out and "libnvJitLink" not in out, out
+
+
+
+@pytest.mark.parametrize("dims,prec,labels", [
+    ([4096], "F32", ["register stockham (bulk prefetch)"]),
+    ([4096], "F64", ["register stockham"]),
+    ([512, 512, 512], "F32", ["register stockham (bulk prefetch)", "register stockham", "register stockham"]),
+])
+def test_pass_labels_name_each_launch(V, cuda_profile, dims, prec, labels):
+    """b200fft_transform_describe_passes lists the kernel kind of every launch: dense
+    contiguous f32 lines take the bulk-copy prefetch kernel, strided and f64 lines the
+    ordinary register kernel."""
+    ir = V.TransformIr.build(V.FftConfig(dims).with_batch_count(64 if len(dims) == 1 else 1)
+                             .with_precision(V.Precision[prec]), V.Direction.FORWARD, cuda_profile)
+    assert ir.pass_labels == labels
+    assert len(ir.pass_labels) == ir.launch_count

@@ -506,6 +506,21 @@ b200fft_status b200fft_context_synchronize(b200fft_context *context, void *strea
     });
 }
 
+uint64_t b200fft_transform_describe_passes(const b200fft_transform *transform, char *buffer, uint64_t capacity) {
+    if (!transform) return 0;
+    std::string text;
+    for (const PassPlan &pp : transform->t->prog.passes) {
+        if (!text.empty()) text += '\n';
+        text += pp.label;
+    }
+    if (buffer && capacity) {
+        const size_t n = std::min<size_t>(text.size(), (size_t)capacity - 1);
+        std::memcpy(buffer, text.data(), n);
+        buffer[n] = '\0';
+    }
+    return text.size();
+}
+
 int32_t b200fft_transform_specialised_passes(const b200fft_transform *transform, int32_t *generic_passes) {
     if (!transform) return -1;
     int total = 0;

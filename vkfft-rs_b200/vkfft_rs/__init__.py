@@ -253,6 +253,7 @@ def library():
         "b200fft_transform_workspace_bytes": ([vp], u64),
         "b200fft_transform_launch_count": ([vp], u32),
         "b200fft_transform_specialised_passes": ([vp, P(i32)], i32),
+        "b200fft_transform_describe_passes": ([vp, ctypes.c_char_p, ctypes.c_uint64], ctypes.c_uint64),
         "b200fft_probe": ([P(i32)], i32),
         "b200fft_context_create": ([i32, P(vp)], i32),
         "b200fft_context_destroy": ([vp], None),
@@ -666,6 +667,14 @@ class TransformIr:
         if h and _lib is not None:
             _lib.b200fft_transform_destroy(h)
             self._h = None
+
+    @property
+    def pass_labels(self):
+        """The kernel kind of each launch of one execution, in order."""
+        n = library().b200fft_transform_describe_passes(self._h, None, 0)
+        buf = ctypes.create_string_buffer(n + 1)
+        library().b200fft_transform_describe_passes(self._h, buf, n + 1)
+        return buf.value.decode().split("\n") if n else []
 
     @property
     def specialised_passes(self):
