@@ -154,6 +154,29 @@ def emit_split(r):
     return lines
 
 
+# f32 radix-2 butterfly on sm_100+: both complex sums in one packed add and one packed
+# subtract (add / sub .rn.f32x2 round each lane exactly as the scalar adds do, so results
+# are bit-identical; every larger power-of-two codelet is built from this butterfly).
+F32X2_DFT2 = [
+    "",
+    "template <> B200FFT_HD void dft2<float>(cplx<float>* v) {",
+    "#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000",
+    "    unsigned long long a, b, s, d;",
+    "    asm(\"mov.b64 %0, {%1, %2};\" : \"=l\"(a) : \"f\"(v[0].x), \"f\"(v[0].y));",
+    "    asm(\"mov.b64 %0, {%1, %2};\" : \"=l\"(b) : \"f\"(v[1].x), \"f\"(v[1].y));",
+    "    asm(\"add.rn.f32x2 %0, %1, %2;\" : \"=l\"(s) : \"l\"(a), \"l\"(b));",
+    "    asm(\"sub.rn.f32x2 %0, %1, %2;\" : \"=l\"(d) : \"l\"(a), \"l\"(b));",
+    "    asm(\"mov.b64 {%0, %1}, %2;\" : \"=f\"(v[0].x), \"=f\"(v[0].y) : \"l\"(s));",
+    "    asm(\"mov.b64 {%0, %1}, %2;\" : \"=f\"(v[1].x), \"=f\"(v[1].y) : \"l\"(d));",
+    "#else",
+    "    const cplx<float> a = v[0], b = v[1];",
+    "    v[0].x = a.x + b.x; v[0].y = a.y + b.y;",
+    "    v[1].x = a.x - b.x; v[1].y = a.y - b.y;",
+    "#endif",
+    "}",
+]
+
+
 def main():
     out = [
         "// Generated by gen_codelets.py -- do not edit by hand.",
@@ -185,6 +208,8 @@ def main():
             return
         if r in PRIMES:
             out.extend(emit_prime(r))
+            if r == 2:
+                out.extend(F32X2_DFT2)
         else:
             r1, r2 = SPLITS[r]
             gen(r1)
