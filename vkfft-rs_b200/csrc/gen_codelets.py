@@ -154,20 +154,34 @@ def emit_split(r):
     return lines
 
 
-# f32 radix-2 butterfly on sm_100+: both complex sums in one packed add and one packed
-# subtract (add / sub .rn.f32x2 round each lane exactly as the scalar adds do, so results
-# are bit-identical; every larger power-of-two codelet is built from this butterfly).
+# Packed f32 arithmetic on sm_100+ (PTX add / sub / mul / fma .rn.f32x2): each lane rounds
+# exactly as the scalar operation does.  A complex point is one register pair (x, y).
+F32X2_HELPERS = [
+    "#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000",
+    "#define B200FFT_F32X2 1",
+    "namespace f32x2 {",
+    "using u64 = unsigned long long;",
+    "__device__ __forceinline__ u64 pk(float x, float y) { u64 r; asm(\"mov.b64 %0, {%1, %2};\" : \"=l\"(r) : \"f\"(x), \"f\"(y)); return r; }",
+    "__device__ __forceinline__ void up(u64 r, float &x, float &y) { asm(\"mov.b64 {%0, %1}, %2;\" : \"=f\"(x), \"=f\"(y) : \"l\"(r)); }",
+    "__device__ __forceinline__ u64 add(u64 a, u64 b) { u64 r; asm(\"add.rn.f32x2 %0, %1, %2;\" : \"=l\"(r) : \"l\"(a), \"l\"(b)); return r; }",
+    "__device__ __forceinline__ u64 sub(u64 a, u64 b) { u64 r; asm(\"sub.rn.f32x2 %0, %1, %2;\" : \"=l\"(r) : \"l\"(a), \"l\"(b)); return r; }",
+    "__device__ __forceinline__ u64 mul(u64 a, u64 b) { u64 r; asm(\"mul.rn.f32x2 %0, %1, %2;\" : \"=l\"(r) : \"l\"(a), \"l\"(b)); return r; }",
+    "// a * b + c",
+    "__device__ __forceinline__ u64 fma(u64 a, u64 b, u64 c) { u64 r; asm(\"fma.rn.f32x2 %0, %1, %2, %3;\" : \"=l\"(r) : \"l\"(a), \"l\"(b), \"l\"(c)); return r; }",
+    "}  // namespace f32x2",
+    "#endif",
+    "",
+]
+
+# f32 radix-2 butterfly: both complex sums in one packed add and one packed subtract (every
+# larger power-of-two codelet is built from this butterfly).
 F32X2_DFT2 = [
     "",
     "template <> B200FFT_HD void dft2<float>(cplx<float>* v) {",
-    "#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000",
-    "    unsigned long long a, b, s, d;",
-    "    asm(\"mov.b64 %0, {%1, %2};\" : \"=l\"(a) : \"f\"(v[0].x), \"f\"(v[0].y));",
-    "    asm(\"mov.b64 %0, {%1, %2};\" : \"=l\"(b) : \"f\"(v[1].x), \"f\"(v[1].y));",
-    "    asm(\"add.rn.f32x2 %0, %1, %2;\" : \"=l\"(s) : \"l\"(a), \"l\"(b));",
-    "    asm(\"sub.rn.f32x2 %0, %1, %2;\" : \"=l\"(d) : \"l\"(a), \"l\"(b));",
-    "    asm(\"mov.b64 {%0, %1}, %2;\" : \"=f\"(v[0].x), \"=f\"(v[0].y) : \"l\"(s));",
-    "    asm(\"mov.b64 {%0, %1}, %2;\" : \"=f\"(v[1].x), \"=f\"(v[1].y) : \"l\"(d));",
+    "#ifdef B200FFT_F32X2",
+    "    const f32x2::u64 a = f32x2::pk(v[0].x, v[0].y), b = f32x2::pk(v[1].x, v[1].y);",
+    "    f32x2::up(f32x2::add(a, b), v[0].x, v[0].y);",
+    "    f32x2::up(f32x2::sub(a, b), v[1].x, v[1].y);",
     "#else",
     "    const cplx<float> a = v[0], b = v[1];",
     "    v[0].x = a.x + b.x; v[0].y = a.y + b.y;",
@@ -175,6 +189,49 @@ F32X2_DFT2 = [
     "#endif",
     "}",
 ]
+
+
+# Primes whose f32 butterfly is packed.  Radix 7 measured slower packed (the fused 4099
+# Bluestein line, M = 8 * 3 * 7^3: 4.30 -> 4.39 ms; its nine constant pairs per kind cost
+# registers), so 7, 11 and 13 stay scalar.
+F32X2_PRIMES = (2, 3, 5)
+
+
+def emit_prime_f32x2(r):
+    """f32 prime-radix butterfly on packed pairs: s_n = v_n + v_(r-n) packed; the
+    differences are formed swapped, e_n = (dy, dx), so that b' = sum (s_nk, -s_nk) * e_n
+    is (by, -bx) and the outputs v_k = a + b', v_(r-k) = a - b' are packed too, with
+    a = x0 + sum c_nk s_n.  Lane by lane the operations of the scalar codelet."""
+    h = (r - 1) // 2
+    L = ["", f"template <> B200FFT_HD void dft{r}<float>(cplx<float>* v) {{", "#ifdef B200FFT_F32X2",
+         "    using namespace f32x2;", "    const u64 x0 = pk(v[0].x, v[0].y);"]
+    for n in range(1, h + 1):
+        L.append(f"    const u64 s{n} = add(pk(v[{n}].x, v[{n}].y), pk(v[{r - n}].x, v[{r - n}].y));")
+        L.append(f"    const u64 e{n} = pk(v[{n}].y - v[{r - n}].y, v[{n}].x - v[{r - n}].x);")
+    acc = "x0"
+    for n in range(1, h + 1):
+        acc = f"add({acc}, s{n})"
+    L.append(f"    up({acc}, v[0].x, v[0].y);")
+    for k in range(1, h + 1):
+        a = "x0"
+        b = None
+        for n in range(1, h + 1):
+            c, sn = cs(n * k, r)
+            cf, sf = lit(c).replace("kc<T>", "kc<float>"), lit(sn).replace("kc<T>", "kc<float>")
+            a = f"fma(pk({cf}, {cf}), s{n}, {a})"
+            term = f"pk({sf}, -{sf})"
+            b = f"mul({term}, e{n})" if b is None else f"fma({term}, e{n}, {b})"
+        L.append(f"    {{ const u64 a = {a};")
+        L.append(f"      const u64 b = {b};")
+        L.append(f"      up(add(a, b), v[{k}].x, v[{k}].y);")
+        L.append(f"      up(sub(a, b), v[{r - k}].x, v[{r - k}].y); }}")
+    L.append("#else")
+    body = emit_prime(r)[1:-1]  # the generic body, specialised to float
+    L.extend(line.replace("const T ", "const float ").replace("cplx<T>", "cplx<float>").replace("kc<T>", "kc<float>")
+             for line in body)
+    L.append("#endif")
+    L.append("}")
+    return L
 
 
 def main():
@@ -200,7 +257,7 @@ def main():
         "};",
         "template <typename T> B200FFT_HD T kc(double hi, double lo) { return KConst<T>::make(hi, lo); }",
         "",
-    ]
+    ] + F32X2_HELPERS
     done = set()
 
     def gen(r):
@@ -208,8 +265,8 @@ def main():
             return
         if r in PRIMES:
             out.extend(emit_prime(r))
-            if r == 2:
-                out.extend(F32X2_DFT2)
+            if r in F32X2_PRIMES:
+                out.extend(F32X2_DFT2 if r == 2 else emit_prime_f32x2(r))
         else:
             r1, r2 = SPLITS[r]
             gen(r1)
