@@ -48,8 +48,8 @@ void CopyPool::claim_items(uint64_t gen) {
     for (;;) {
         uint64_t v = next_.load(std::memory_order_acquire);
         if ((v >> kGenShift) != gen) return;
-        const size_t k = (size_t)(v & ((1ull << kGenShift) - 1));
-        if (k >= n_.load(std::memory_order_acquire)) return;
+        const size_t k = (size_t)(v & kField);
+        if (k >= (size_t)((v >> kCountShift) & kField)) return;  // the job's own count
         if (!next_.compare_exchange_weak(v, v + 1, std::memory_order_acq_rel)) continue;
         // item k of job `gen` is ours: the job (and fn_) stays in place until it is done
         try {
@@ -90,13 +90,13 @@ void CopyPool::worker_main() {
 }
 
 void CopyPool::start(size_t n, const std::function<void(size_t)> &fn) {
+    if (n > kField) fail_runtime("host copy pool: a job of more than 2^20 - 1 items");
     fn_ = &fn;
     err_ = nullptr;
     job_n_ = n;
     done_.store(0, std::memory_order_relaxed);
-    n_.store(n, std::memory_order_release);
-    const uint64_t gen = ++gen_;
-    next_.store(gen << kGenShift, std::memory_order_release);
+    const uint64_t gen = ++gen_ & ((1ull << (64 - kGenShift)) - 1);
+    next_.store((gen << kGenShift) | ((uint64_t)n << kCountShift), std::memory_order_release);
     if (!workers_.empty()) {
         { std::lock_guard<std::mutex> l(mu_); }  // a worker between its check and its wait sees the job
         cv_.notify_all();
@@ -111,7 +111,7 @@ void CopyPool::finish() {
 void CopyPool::run(size_t n, const std::function<void(size_t)> &fn) {
     if (n == 0) return;
     start(n, fn);
-    claim_items(gen_);
+    claim_items(gen_ & ((1ull << (64 - kGenShift)) - 1));
     finish();
 }
 

@@ -37,8 +37,8 @@ public:
     CopyPool(const CopyPool &) = delete;
     CopyPool &operator=(const CopyPool &) = delete;
     int threads() const { return (int)workers_.size() + 1; }
-    // Runs fn(k) for every k in [0, n) on the workers and the calling thread; returns when
-    // all items have finished and rethrows the first exception an item raised.
+    // Runs fn(k) for every k in [0, n) (n < 2^20) on the workers and the calling thread;
+    // returns when all items have finished and rethrows the first exception an item raised.
     void run(size_t n, const std::function<void(size_t)> &fn);
     // The same on the workers alone (there must be some): start() returns at once, so the
     // caller can act on items as they finish; finish() waits for the job and rethrows.
@@ -46,7 +46,10 @@ public:
     void finish();
 
 private:
-    static constexpr int kGenShift = 40;
+    // the claim word: job generation (high 24 bits) | item count (20 bits) | next item
+    // (low 20 bits), so a claim is checked against the count of its own job
+    static constexpr int kGenShift = 40, kCountShift = 20;
+    static constexpr uint64_t kField = (1ull << 20) - 1;
     void worker_main();
     void claim_items(uint64_t gen);
 
@@ -56,10 +59,9 @@ private:
     std::mutex mu_;
     std::condition_variable cv_;
     bool stop_ = false;
-    // next item of the current job, tagged with the job's generation in the high bits:
-    // a worker that wakes late cannot claim an item of a later job by mistake
+    // next item of the current job with its count and generation: a worker that wakes
+    // late cannot claim an item of a later job by mistake
     std::atomic<uint64_t> next_{0};
-    std::atomic<size_t> n_{0};
     std::atomic<size_t> done_{0};
     uint64_t gen_ = 0;
     size_t job_n_ = 0;
